@@ -1,0 +1,428 @@
+#!/usr/bin/env python3
+"""RVQ decode benchmark (B200, sm_100a).
+
+Workload (one GPU): the ping-pong slot fill of a Qwen-style decoder block --
+hidden 2560, intermediate 9728, 32 query / 8 KV heads of 128 -- whose 7
+projections are RVQ-compressed (K=4 stages, 256 codes, d=8, per-row fp16
+scales) and whose 4 norm weights are bf16 copies.  One step decodes one
+layer into a bf16 slot: 100,925,440 weights, 252,375,040 algorithmic bytes
+(slot writes + index reads + scale reads).  Steps cycle through 8 distinct
+layers and 2 slots, so consecutive steps never find their inputs in L2
+(every step touches > 250 MB against a 126 MB L2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one process per GPU): every rank decodes its own layers
+(weak scaling, no collective on the data path); the timed region is
+bracketed by barriers and the slowest rank's time is reported.
+
+Rank 0 prints one JSON line.  ``value`` is whole-job GB/s with inputs
+resident in HBM; ``e2e`` is the same metric through the reference-facing
+``decode_into`` API with the layer's compressed tensors copied from pinned
+host memory and the decoded slot copied back every step; ``cpu_baseline``
+times the CPU port of the reference's reconstruction on this host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "RVQ decode GB/s (% HBM peak); batch-1 ms/token at 1/2/4/8 B200"
+WORKLOAD = ("config1 ping-pong slot fill: Qwen-style block hidden 2560 / intermediate 9728 / "
+            "32q 8kv head 128, 7 RVQ projections (K=4, 256 codes, d=8, per-row fp16 scales) "
+            "+ 4 bf16 norms -> bf16 slot")
+N_LAYERS_ROTATED = 8
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU-baseline sample budget (rank 0, N=1)")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        data = json.load(f)
+    rec = data.get(kernel)
+    return None if rec is None else rec.get("bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.path = None
+        try:
+            self.uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.uuid = None
+
+    def start(self):
+        if self.uuid is None:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", self.uuid, "-lms", "100", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    try:
+                        sm.append(float(parts[1]))
+                        smax = float(parts[2])
+                    except ValueError:
+                        continue
+                    for name, val in zip(names, parts[5:9]):
+                        if val.lower().startswith("active"):
+                            reasons.add(name)
+            os.unlink(self.path)
+        except OSError:
+            return None
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# CPU reference arm / baseline (the oracle's C port of the reference path)
+# ---------------------------------------------------------------------------
+
+def cpu_block_sample(frac_rows: float, seed: int = 0):
+    """Entries of one config-1 block, each cut to its first `frac_rows` of
+    output rows (a contiguous vector range of every index plane)."""
+    from oracle.rvq_oracle import RVQEntryNP
+    from rvq_b200 import synthetic
+    art = synthetic.make_block_artifact(seed=seed)
+    out = []
+    for key, e in art["entries"].items():
+        if e["method"] != "rvq_groupwise":
+            continue
+        rows, cols = e["shape"]
+        keep_rows = max(1, int(rows * frac_rows))
+        nvec = keep_rows * cols // 8
+        cb = art["shared_codebooks"][e["codebook_id"]].float().numpy()
+        idx = e["indices"][:, :nvec].contiguous().numpy()
+        gv = int(e["group_size"]) // 8
+        sc = e["scales"][: (nvec + gv - 1) // gv].float().numpy()
+        ent = RVQEntryNP(indices=idx, codebook=cb, scales=sc, tail=sc[:0], d=8,
+                         group_size=int(e["group_size"]), trimmed_numel=nvec * 8,
+                         numel=nvec * 8)
+        algo = nvec * 8 * 2 + idx.size + sc.size * 2
+        out.append((ent, algo))
+    return out
+
+
+def time_cpu_port(sample, seconds: float, min_reps: int = 1):
+    import numpy as np
+
+    from oracle.c_oracle import decode_rvq_bits_c, max_threads
+    from oracle.rvq_oracle import OUT_BF16
+    threads = max_threads()
+    bufs = [np.empty(e.numel, np.uint16) for e, _ in sample]
+    algo = sum(a for _, a in sample)
+    for (e, _), b in zip(sample, bufs):        # warm-up (page-in)
+        decode_rvq_bits_c(e, OUT_BF16, nthreads=threads, out=b)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for (e, _), b in zip(sample, bufs):
+            decode_rvq_bits_c(e, OUT_BF16, nthreads=threads, out=b)
+        reps += 1
+        el = time.perf_counter() - t0
+        if reps >= min_reps and el >= seconds:
+            break
+    return algo * reps / el / 1e9, threads, reps, el, algo
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    # per step: 1/16 of every projection's rows of one block (contiguous)
+    frac = 1.0 / 16.0
+    sample = cpu_block_sample(frac)
+    import numpy as np
+
+    from oracle.c_oracle import decode_rvq_bits_c, max_threads
+    from oracle.rvq_oracle import OUT_BF16
+    threads = max_threads()
+    bufs = [np.empty(e.numel, np.uint16) for e, _ in sample]
+    algo = sum(a for _, a in sample)
+
+    def step():
+        for (e, _), b in zip(sample, bufs):
+            decode_rvq_bits_c(e, OUT_BF16, nthreads=threads, out=b)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    gbs = algo * args.steps / el / 1e9
+    desc = (f"1/16 of the rows of each of the 7 projections of one config-1 block per step "
+            f"({algo} algorithmic bytes), C/OpenMP port of the reference reconstruction, bf16 out")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": desc},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def build_layers(device, n_layers):
+    """n_layers distinct copies of one seeded block resident on the device,
+    2 bf16 slots, and one LayerDecodePlan per layer (layer l -> slot l % 2)."""
+    from rvq_b200 import synthetic
+    from rvq_b200.engine import LayerDecodePlan
+    art = synthetic.make_block_artifact(seed=0)
+    cbs = {k: v.to(device, torch.float32) for k, v in art["shared_codebooks"].items()}
+    rel = {}
+    for key, e in art["entries"].items():
+        rel[key.split("layers.0.")[-1]] = e
+    slots = [{k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16, device=device)
+              for k, e in rel.items()} for _ in range(2)]
+    layers, plans = [], []
+    for l in range(n_layers):
+        dev_entries = {k: {ek: (ev.to(device) if torch.is_tensor(ev) else ev) for ek, ev in e.items()}
+                       for k, e in rel.items()}
+        layers.append(dev_entries)
+        plans.append(LayerDecodePlan(list(dev_entries.items()), cbs, slots[l % 2]))
+    return art, rel, cbs, slots, layers, plans
+
+
+def time_device(plans, steps, warmup, stream, world):
+    for s in range(warmup):
+        plans[s % len(plans)].launch(stream.cuda_stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(steps):
+        plans[s % len(plans)].launch(stream.cuda_stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        torch.distributed.barrier()
+    return ms
+
+
+def time_e2e(rel, cbs_host, device, steps, warmup, stream):
+    """Reference-facing API end to end: pinned host -> device upload of the
+    layer's compressed tensors (infer_compressed_layerwise_triton.py:424-432),
+    decode_into per key (lines 161-176), decoded slot -> pinned host."""
+    from rvq_b200.engine import decode_into
+    host = {k: {ek: (ev.pin_memory() if torch.is_tensor(ev) else ev) for ek, ev in e.items()}
+            for k, e in rel.items()}
+    host_cbs = {k: v.float().pin_memory() for k, v in cbs_host.items()}
+    dev = {k: {ek: (torch.empty_like(ev, device=device) if torch.is_tensor(ev) else ev)
+               for ek, ev in e.items()} for k, e in rel.items()}
+    dev_cbs = {k: torch.empty_like(v, device=device) for k, v in host_cbs.items()}
+    slot = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16, device=device) for k, e in rel.items()}
+    back = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16).pin_memory() for k in rel}
+    h2d = sum(v.numel() * v.element_size() for e in host.values() for v in e.values() if torch.is_tensor(v))
+    h2d += sum(v.numel() * v.element_size() for v in host_cbs.values())
+    d2h = sum(v.numel() * v.element_size() for v in back.values())
+    launches = sum(1 for e in rel.values() if e["method"] != "bf16_raw")
+
+    def step():
+        for k, v in host_cbs.items():
+            dev_cbs[k].copy_(v, non_blocking=True)
+        for k, e in host.items():
+            for ek, ev in e.items():
+                if torch.is_tensor(ev):
+                    dev[k][ek].copy_(ev, non_blocking=True)
+        for k, e in dev.items():
+            decode_into(e, dev_cbs, slot[k])
+        for k in slot:
+            back[k].copy_(slot[k], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            step()
+        end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end), h2d, d2h, launches * steps
+
+
+def run_ours(args, world, rank, local):
+    from rvq_b200 import _native
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=device)
+    _native.load()
+    if not _native.available():
+        raise RuntimeError("rvq_b200 CUDA library has no usable sm_100 device")
+    art, rel, cbs, slots, layers, plans = build_layers(device, N_LAYERS_ROTATED)
+    bytes_per_step = plans[0].algorithmic_bytes
+    launches_per_step = plans[0].launches
+    stream = torch.cuda.Stream(device)
+
+    sampler = ClockSampler(device) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ms = time_device(plans, args.steps, max(args.warmup, 3), stream, world)
+    clocks = sampler.stop() if sampler else None
+
+    ms_t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    total_bytes = bytes_per_step * args.steps * world
+    gbs = total_bytes / (ms_max / 1e3) / 1e9
+    per_launch_s = (ms / 1e3) / (args.steps * launches_per_step)
+    achieved = bytes_per_step / launches_per_step / per_launch_s / 1e9
+    peak, peak_kind = measured_peaks()
+
+    e2e = None
+    if rank == 0 or world > 1:
+        e2e_ms, h2d, d2h, e2e_launches = time_e2e(rel, art["shared_codebooks"], device,
+                                                  args.e2e_steps, 2, stream)
+        e2e_t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        if world > 1:
+            torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
+        e2e_gbs = bytes_per_step * args.e2e_steps * world / (float(e2e_t.item()) / 1e3) / 1e9
+        e2e = {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
+               "api": "rvq_b200.engine.decode_into per entry (reference-facing)",
+               "gpu_launches": e2e_launches}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = cpu_block_sample(1.0)
+        v, threads, reps, el, algo = time_cpu_port(sample, args.cpu_seconds)
+        cpu = {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{reps} full config-1 block decode(s) ({algo} algorithmic bytes each), "
+                         f"C/OpenMP port of the reference reconstruction, bf16 out, {el:.1f} s"}
+
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "bytes_per_step_per_gpu": bytes_per_step,
+                   "weights_per_step_per_gpu": 100925440, "layers_rotated": N_LAYERS_ROTATED,
+                   "slots": 2, "l2": "inputs larger than L2: >250 MB touched per step, "
+                                     "8 distinct layers rotated",
+                   "parallelism": f"independent per-GPU decode x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": profile_traffic("rvq_layer_kernel"),
+                     "kernel": "rvq_layer_kernel",
+                     "algorithmic_bytes_per_launch": bytes_per_step // launches_per_step},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_init(args)
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+    run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

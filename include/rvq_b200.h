@@ -1,0 +1,131 @@
+/*
+ * rvq_b200 -- C ABI of the B200 (sm_100a) RVQ weight-reconstruction kernels.
+ *
+ * Plain pointers and sizes only: no torch or CUDA types in the signatures.
+ * Every pointer named "device" below is CUDA device memory on the device that
+ * is current for the calling thread; `stream` is a cudaStream_t of that
+ * device (NULL = legacy default stream).  Calls are asynchronous on `stream`:
+ * nothing here synchronises the device.
+ *
+ * Entry format: one "entry" is one RVQ-compressed tensor as written by the
+ * reference compressor (compress_full_model.py:375-388): `indices` [K, nvec]
+ * (uint8 when the codebook has <= 256 codes, else int16), a codebook
+ * [K, ncodes, d] (fp16 in the artifact, fp32 after the engine's upload,
+ * infer_compressed_layerwise_triton.py:424-427), one scale per `group_size`
+ * flattened elements (fp16) and a bf16 `tail`.  Only d == 8 is supported, as
+ * in the reference kernel (triton_decode_kernels.py:126-127).
+ *
+ * Results are bit-identical to the reference's reconstruction:
+ *   out[8n+t] = cast( float(scale[n / group_vecs]) * (((0 + cb0) + cb1) + ...) )
+ * with fp32 accumulation in stage order and round-to-nearest-even casts.
+ */
+#ifndef RVQ_B200_H
+#define RVQ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The Python layer maps them onto the reference's exceptions
+ * (triton_decode_kernels.py:119-165): RVQ_ERR_UNAVAILABLE -> RuntimeError,
+ * RVQ_ERR_UNSUPPORTED -> NotImplementedError, RVQ_ERR_INVALID -> ValueError. */
+enum rvq_status {
+    RVQ_OK = 0,
+    RVQ_ERR_INVALID = 1,      /* bad argument (null pointer, bad size, misuse) */
+    RVQ_ERR_UNSUPPORTED = 2,  /* valid input this build does not handle (d != 8, dtype) */
+    RVQ_ERR_UNAVAILABLE = 3,  /* no usable CUDA device / not an sm_100 device */
+    RVQ_ERR_CUDA = 4,         /* a CUDA runtime call failed; see rvq_last_cuda_error() */
+    RVQ_ERR_TOO_LARGE = 5     /* a size exceeds a documented limit */
+};
+
+/* Element kinds.  The output kinds keep the reference's OUT_KIND numbering
+ * (triton_decode_kernels.py:158-165). */
+enum rvq_kind {
+    RVQ_F16 = 0,
+    RVQ_BF16 = 1,
+    RVQ_F32 = 2,
+    RVQ_U8 = 3,
+    RVQ_I16 = 4
+};
+
+/* One RVQ entry to decode.  Replaces the arguments that
+ * decode_rvq_triton_into (triton_decode_kernels.py:114-185) passes to
+ * _rvq_decode_into_kernel plus the tail copy of lines 187-188. */
+typedef struct rvq_entry {
+    const void* indices;      /* device, [stages][stage_stride], index_kind elements */
+    const void* codebook;     /* device, [stages][ncodes][8] contiguous, codebook_kind */
+    const void* scales;       /* device, ceil(nvec / group_vecs) values, scale_kind */
+    const void* tail;         /* device, tail_numel values of tail_kind (may be NULL if 0) */
+    void* out;                /* device, >= trimmed + tail_numel elements of out_kind */
+    int64_t nvec;             /* vectors of d = 8 elements (indices.shape[1]) */
+    int64_t stage_stride;     /* elements between index planes (indices.stride(0)) */
+    int64_t group_vecs;       /* group_size / d: vectors sharing one scale */
+    int64_t trimmed;          /* trimmed_numel: core elements written (masked) */
+    int64_t tail_numel;       /* tail elements copied to out[trimmed ...] */
+    int32_t stages;           /* K >= 1 */
+    int32_t ncodes;           /* codebook entries per stage */
+    int32_t d;                /* must be 8 */
+    int32_t index_kind;       /* RVQ_U8 or RVQ_I16 */
+    int32_t codebook_kind;    /* RVQ_F16 or RVQ_F32 */
+    int32_t scale_kind;       /* RVQ_F16, RVQ_BF16 or RVQ_F32 */
+    int32_t tail_kind;        /* RVQ_F16, RVQ_BF16 or RVQ_F32 */
+    int32_t out_kind;         /* RVQ_F16, RVQ_BF16 or RVQ_F32 */
+} rvq_entry;
+
+/* A raw device-to-device copy of a `bf16_raw` entry (a 1-D norm weight),
+ * the int16 view copy of infer_compressed_layerwise_triton.py:165-167. */
+typedef struct rvq_copy {
+    const void* src;          /* device */
+    void* dst;                /* device */
+    int64_t nbytes;
+} rvq_copy;
+
+/* Maximum entries + copies one rvq_decode_layer call takes. */
+#define RVQ_MAX_LAYER_JOBS 32
+
+/* 1 when a device with compute capability 10.x is current and the kernels
+ * of this library load on it, else 0.  Replaces triton_available()
+ * (triton_decode_kernels.py:31-32). */
+int rvq_available(void);
+
+/* RVQ_OK when rvq_decode would accept `e`, else the status it would return.
+ * Host-only check: reads no device memory.  Replaces rvq_triton_supported
+ * (triton_decode_kernels.py:35-44) plus the argument checks of
+ * decode_rvq_triton_into (lines 122-165). */
+int rvq_check_entry(const rvq_entry* e);
+
+/* Decode one entry into e->out, then copy its tail.  Replaces
+ * decode_rvq_triton_into (triton_decode_kernels.py:114-190): one kernel
+ * launch on `stream`, no allocation, no synchronisation. */
+int rvq_decode(const rvq_entry* e, void* stream);
+
+/* Decode a whole layer slot in ONE launch: `n_entries` RVQ entries and
+ * `n_copies` raw copies (n_entries + n_copies <= RVQ_MAX_LAYER_JOBS).
+ * Replaces the per-key decode_into loop of prefetch_layer
+ * (infer_compressed_layerwise_triton.py:246-266) and the per-key
+ * _decode_entry_into calls of SlotResidency._decode_layer_async
+ * (infer_compressed_layerwise_single_slot.py:652-668). */
+int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* copies,
+                     int n_copies, void* stream);
+
+/* Reads and clears the sticky device flag that kernels set when an index is
+ * outside [0, ncodes) (the decoded element then uses code 0).  Synchronises
+ * the current device.  Returns 1 if the flag was set, 0 if not, or -RVQ_ERR_CUDA. */
+int rvq_take_index_error(void);
+
+/* Last CUDA error code seen by this library on the calling thread (0 = none). */
+int rvq_last_cuda_error(void);
+
+/* Static description of a status code. */
+const char* rvq_status_string(int status);
+
+/* Library version as 10000*major + 100*minor + patch. */
+int rvq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RVQ_B200_H */

@@ -1,0 +1,86 @@
+// Shared device/host helpers of the rvq_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "rvq_b200.h"
+
+namespace rvq {
+
+// ---------------------------------------------------------------------------
+// Division by a run-time invariant divisor (Granlund & Montgomery, "Division
+// by invariant integers using multiplication", PLDI 1994, round-up variant):
+// with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+//   n / d == (umulhi(n, m) + n) >> l   for every 32-bit n.
+// The sum is formed in 64 bits so n may use all 32 bits.
+// ---------------------------------------------------------------------------
+struct FastDiv {
+    uint32_t d;
+    uint32_t m;
+    uint32_t l;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f;
+    f.d = d;
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    f.l = l;
+    f.m = (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1ull);
+    return f;
+}
+
+__host__ __device__ __forceinline__ uint32_t fastdiv(uint32_t n, const FastDiv& f) {
+#ifdef __CUDA_ARCH__
+    uint32_t hi = __umulhi(n, f.m);
+#else
+    uint32_t hi = (uint32_t)(((uint64_t)n * f.m) >> 32);
+#endif
+    return (uint32_t)(((uint64_t)hi + n) >> f.l);
+}
+
+// ---------------------------------------------------------------------------
+// Element conversions.  All casts to 16-bit types round to nearest even and
+// keep subnormals (no -ftz in this build).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float load_as_f32(const void* p, int64_t i, int kind) {
+    if (kind == RVQ_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    if (kind == RVQ_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_from_f32(void* p, int64_t i, int kind, float v) {
+    if (kind == RVQ_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+    else if (kind == RVQ_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// fp32 <- fp16 (exact) + fp32, one rounding: the sm_100 mixed-precision add.
+__device__ __forceinline__ float add_f16_f32(uint16_t h, float c) {
+    float d;
+    asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(h), "f"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, int out_kind) {
+    if (out_kind == RVQ_BF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+inline int elem_bytes(int kind) {
+    switch (kind) {
+        case RVQ_F16: case RVQ_BF16: case RVQ_I16: return 2;
+        case RVQ_F32: return 4;
+        case RVQ_U8: return 1;
+        default: return 0;
+    }
+}
+
+}  // namespace rvq

@@ -1,0 +1,551 @@
+// RVQ decode kernels for B200 (sm_100a) and their C ABI.
+//
+// Computes, for every vector n of every job (reference semantics:
+// _rvq_decode_into_kernel, triton_decode_kernels.py:74-111, and
+// _decode_rvq_into, infer_compressed_layerwise_single_slot.py:123-149):
+//
+//   acc[t] = ((0 + cb[0][i0][t]) + cb[1][i1][t]) + ... + cb[K-1][iK-1][t]   (fp32)
+//   out[8n+t] = cast(acc[t] * float(scale[n / group_vecs]))  for 8n+t < trimmed
+//   out[trimmed + i] = cast(tail[i])
+//
+// Design (HBM-write bound; 20 bytes of traffic per 8 bf16 weights at K=4):
+// * One persistent launch decodes a list of jobs (all RVQ entries and raw
+//   norm copies of a layer slot).  The work is cut into tiles of 128
+//   vectors; CTA b owns the contiguous tile range [T*b/G, T*(b+1)/G), so every
+//   CTA streams one or two contiguous regions and loads at most a couple of
+//   codebooks.
+// * 1 CTA of 1024 threads per SM.  The CTA stages the job's codebook in
+//   shared memory as fp16 with 8 copies interleaved per entry: lane L reads
+//   copy (L & 7), so the 8 lanes of each quarter-warp phase of a 16-byte
+//   shared load always hit 8 different bank quads -- random codes never
+//   conflict.  K=4 x 256 codes x 16 B x 8 copies = 128 KB.
+// * A codebook handed over as fp32 (what the engine uploads) is converted to
+//   fp16 while it is staged; the CTA checks that every value survives the
+//   round trip exactly and otherwise keeps fp32 entries instead, so the
+//   result never depends on that choice.
+// * Lane L of a warp owns vectors v0 + 32j + L (j = 0..3) of its tile: index
+//   loads are 32 consecutive bytes per plane, and each 128-bit store of the
+//   warp covers 512 contiguous output bytes.
+// * fp32 accumulation uses add.rn.f32.f16 (fp16 -> fp32 conversion fused into
+//   the add; exact conversion, one rounding, same result as cvt + add.rn).
+
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "rvq_common.cuh"
+
+namespace rvq {
+
+constexpr int kThreads = 1024;
+constexpr int kWarps = kThreads / 32;
+constexpr int kTileVecs = 128;                 // vectors per warp tile
+constexpr int kJ = kTileVecs / 32;             // vectors per lane per tile
+constexpr int kCopyTileBytes = 2048;           // bytes per warp tile of a raw copy
+constexpr int kSmemBudget = 200 * 1024;        // codebook staging limit per CTA
+constexpr int kMaxDevices = 64;
+
+enum JobKind : uint8_t { JOB_RVQ = 0, JOB_COPY = 1 };
+enum GatherMode : uint8_t { GATHER_SMEM_F16 = 0, GATHER_SMEM_F32 = 1, GATHER_GLOBAL = 2 };
+
+struct Job {
+    const void* idx;
+    const void* cb;
+    const void* scales;
+    const void* tail;
+    void* out;
+    uint32_t nvec;          // RVQ: vectors; COPY: bytes
+    uint32_t stage_stride;  // elements
+    FastDiv gv;
+    uint32_t full_vecs;     // vectors with all 8 elements < trimmed
+    uint32_t tail_numel;
+    uint64_t trimmed;
+    uint32_t tile_begin;
+    uint32_t tile_count;
+    uint16_t stages;
+    uint16_t ncodes;        // 0 encodes 65536 (never produced by int16 indices)
+    uint8_t kind;
+    uint8_t index_bytes;
+    uint8_t cb_kind;
+    uint8_t scale_kind;
+    uint8_t tail_kind;
+    uint8_t out_kind;
+    uint8_t copies_log2;    // fp16 staging copies = 1 << copies_log2
+    uint8_t f16_fits;       // fp16 staging fits in shared memory
+    uint8_t f32_fits;       // fp32 staging fits in shared memory
+    uint8_t out_aligned;    // out is 16-byte aligned
+    uint8_t pad[2];
+};
+
+struct LayerParams {
+    Job jobs[RVQ_MAX_LAYER_JOBS];
+    int njobs;
+    uint32_t total_tiles;
+};
+
+__device__ unsigned int g_index_error;
+
+// ---------------------------------------------------------------------------
+// Device pieces
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t load_code(const Job& job, int k, uint32_t n, bool& bad) {
+    uint32_t c;
+    size_t off = (size_t)k * job.stage_stride + n;
+    if (job.index_bytes == 1) c = __ldg(reinterpret_cast<const uint8_t*>(job.idx) + off);
+    else c = (uint16_t)__ldg(reinterpret_cast<const short*>(job.idx) + off);
+    uint32_t nc = job.ncodes ? job.ncodes : 65536u;
+    if (c >= nc) { bad = true; c = 0; }
+    return c;
+}
+
+__device__ __forceinline__ float load_scale(const Job& job, uint32_t n) {
+    uint32_t g = fastdiv(n, job.gv);
+    return load_as_f32(job.scales, g, job.scale_kind);
+}
+
+// Store the 8 fp32 values of vector n (scale already applied).
+__device__ __forceinline__ void store_vec(const Job& job, uint32_t n, const float (&v)[8]) {
+    if (n < job.full_vecs && job.out_aligned) {
+        if (job.out_kind == RVQ_F32) {
+            float4* o = reinterpret_cast<float4*>(job.out) + (size_t)n * 2;
+            o[0] = make_float4(v[0], v[1], v[2], v[3]);
+            o[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+            uint4 q;
+            q.x = pack2(v[0], v[1], job.out_kind);
+            q.y = pack2(v[2], v[3], job.out_kind);
+            q.z = pack2(v[4], v[5], job.out_kind);
+            q.w = pack2(v[6], v[7], job.out_kind);
+            reinterpret_cast<uint4*>(job.out)[n] = q;
+        }
+        return;
+    }
+    uint64_t base = (uint64_t)n * 8;
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+        if (base + t < job.trimmed) store_from_f32(job.out, (int64_t)(base + t), job.out_kind, v[t]);
+}
+
+// Stage job.cb into shared memory.  Returns the gather mode every thread of
+// the CTA agrees on.  Must be called by all threads of the CTA.
+__device__ int stage_codebook(const Job& job, uint4* smem) {
+    const int n_entries = (int)job.stages * (job.ncodes ? (int)job.ncodes : 65536);
+    const int copies = 1 << job.copies_log2;
+    const int lane = threadIdx.x & 31;
+    int inexact = 0;
+    if (job.f16_fits) {
+        for (int e = threadIdx.x; e < n_entries; e += blockDim.x) {
+            uint4 q;
+            if (job.cb_kind == RVQ_F16) {
+                q = __ldg(reinterpret_cast<const uint4*>(job.cb) + e);
+            } else {
+                const float4* src = reinterpret_cast<const float4*>(job.cb) + (size_t)e * 2;
+                float4 a = __ldg(src), b = __ldg(src + 1);
+                float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    __half h0 = __float2half_rn(f[2 * i]), h1 = __float2half_rn(f[2 * i + 1]);
+                    inexact |= (__float_as_uint(__half2float(h0)) != __float_as_uint(f[2 * i])) |
+                               (__float_as_uint(__half2float(h1)) != __float_as_uint(f[2 * i + 1])) |
+                               isnan(f[2 * i]) | isnan(f[2 * i + 1]);
+                    w[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+                }
+                q = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            // rotate the copy index with the lane so the 8 lanes of a phase
+            // write 8 different bank quads
+            for (int i = 0; i < copies; ++i) {
+                int cp = (i + lane) & (copies - 1);
+                smem[(size_t)e * copies + cp] = q;
+            }
+        }
+        inexact = __syncthreads_or(inexact);
+        if (!inexact) return GATHER_SMEM_F16;
+    }
+    if (job.f32_fits && job.cb_kind == RVQ_F32) {
+        if (job.f16_fits) __syncthreads();  // fp16 staging of this CTA is being replaced
+        const uint4* src = reinterpret_cast<const uint4*>(job.cb);
+        for (int e = threadIdx.x; e < n_entries * 2; e += blockDim.x) smem[e] = __ldg(src + e);
+        __syncthreads();
+        return GATHER_SMEM_F32;
+    }
+    __syncthreads();
+    return GATHER_GLOBAL;
+}
+
+// Fast tile: fp16 codebook staged with 1 << copies_log2 copies, KT stages
+// known at compile time (1..4).
+template <int KT>
+__device__ __forceinline__ void tile_fast(const Job& job, uint32_t tile, int lane, const uint4* smem) {
+    const uint32_t v0 = tile * kTileVecs;
+    const uint32_t cpy = lane & ((1u << job.copies_log2) - 1u);
+    const uint32_t ncodes = job.ncodes ? job.ncodes : 65536u;
+    bool bad = false;
+    uint32_t code[kJ][KT];
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) {
+        uint32_t n = v0 + 32 * j + lane;
+#pragma unroll
+        for (int k = 0; k < KT; ++k) code[j][k] = (n < job.nvec) ? load_code(job, k, n, bad) : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) {
+        uint32_t n = v0 + 32 * j + lane;
+        if (n >= job.nvec) break;
+        float acc[8];
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+            uint4 q = smem[((k * ncodes + code[j][k]) << job.copies_log2) + cpy];
+            uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint16_t lo = (uint16_t)(w[i] & 0xFFFFu), hi = (uint16_t)(w[i] >> 16);
+                if (k == 0) {
+                    acc[2 * i] = add_f16_f32(lo, 0.0f);
+                    acc[2 * i + 1] = add_f16_f32(hi, 0.0f);
+                } else {
+                    acc[2 * i] = add_f16_f32(lo, acc[2 * i]);
+                    acc[2 * i + 1] = add_f16_f32(hi, acc[2 * i + 1]);
+                }
+            }
+        }
+        float s = load_scale(job, n);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc[t] = __fmul_rn(acc[t], s);
+        store_vec(job, n, acc);
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(&g_index_error, 1u);
+}
+
+// Generic tile: any stage count and gather mode.
+__device__ void tile_generic(const Job& job, uint32_t tile, int lane, const uint4* smem, int mode) {
+    const uint32_t v0 = tile * kTileVecs;
+    const uint32_t cpy = lane & ((1u << job.copies_log2) - 1u);
+    const uint32_t ncodes = job.ncodes ? job.ncodes : 65536u;
+    bool bad = false;
+    for (int j = 0; j < kJ; ++j) {
+        uint32_t n = v0 + 32 * j + lane;
+        if (n >= job.nvec) break;
+        float acc[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc[t] = 0.0f;
+        for (int k = 0; k < (int)job.stages; ++k) {
+            uint32_t c = load_code(job, k, n, bad);
+            uint32_t e = k * ncodes + c;
+            float v[8];
+            if (mode == GATHER_SMEM_F16) {
+                uint4 q = smem[(e << job.copies_log2) + cpy];
+                uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    v[2 * i] = __half2float(__ushort_as_half((uint16_t)(w[i] & 0xFFFFu)));
+                    v[2 * i + 1] = __half2float(__ushort_as_half((uint16_t)(w[i] >> 16)));
+                }
+            } else if (mode == GATHER_SMEM_F32) {
+                const float4* p = reinterpret_cast<const float4*>(smem) + (size_t)e * 2;
+                float4 a = p[0], b = p[1];
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            } else if (job.cb_kind == RVQ_F32) {
+                const float4* p = reinterpret_cast<const float4*>(job.cb) + (size_t)e * 2;
+                float4 a = __ldg(p), b = __ldg(p + 1);
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            } else {
+                uint4 q = __ldg(reinterpret_cast<const uint4*>(job.cb) + e);
+                uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    v[2 * i] = __half2float(__ushort_as_half((uint16_t)(w[i] & 0xFFFFu)));
+                    v[2 * i + 1] = __half2float(__ushort_as_half((uint16_t)(w[i] >> 16)));
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) acc[t] = __fadd_rn(acc[t], v[t]);
+        }
+        float s = load_scale(job, n);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc[t] = __fmul_rn(acc[t], s);
+        store_vec(job, n, acc);
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(&g_index_error, 1u);
+}
+
+__device__ void copy_tile(const Job& job, uint32_t tile, int lane) {
+    const uint64_t begin = (uint64_t)tile * kCopyTileBytes;
+    const uint64_t end = min((uint64_t)job.nvec, begin + kCopyTileBytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(job.idx);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(job.out);
+    bool aligned = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
+    if (aligned) {
+        uint64_t vec_end = begin + ((end - begin) & ~15ull);
+        for (uint64_t o = begin + 16ull * lane; o < vec_end; o += 16 * 32)
+            *reinterpret_cast<uint4*>(dst + o) = __ldg(reinterpret_cast<const uint4*>(src + o));
+        for (uint64_t o = vec_end + lane; o < end; o += 32) dst[o] = src[o];
+    } else {
+        for (uint64_t o = begin + lane; o < end; o += 32) dst[o] = src[o];
+    }
+}
+
+__device__ void copy_tail(const Job& job) {
+    for (uint32_t i = threadIdx.x; i < job.tail_numel; i += blockDim.x) {
+        float v = load_as_f32(job.tail, i, job.tail_kind);
+        store_from_f32(job.out, (int64_t)(job.trimmed + i), job.out_kind, v);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_constant__ LayerParams p) {
+    extern __shared__ uint4 smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t T = p.total_tiles, G = gridDim.x, b = blockIdx.x;
+    const uint32_t t0 = (uint32_t)(((uint64_t)T * b) / G);
+    const uint32_t t1 = (uint32_t)(((uint64_t)T * (b + 1)) / G);
+    bool staged_once = false;
+    for (int j = 0; j < p.njobs; ++j) {
+        const Job& job = p.jobs[j];
+        const uint32_t jb = job.tile_begin, je = jb + job.tile_count;
+        const uint32_t a = max(t0, jb), e = min(t1, je);
+        if (a >= e) continue;
+        if (job.kind == JOB_COPY) {
+            for (uint32_t t = a + warp; t < e; t += kWarps) copy_tile(job, t - jb, lane);
+            continue;
+        }
+        if (job.nvec == 0) {                // tail-only entry: nothing to stage
+            if (a == jb) copy_tail(job);
+            continue;
+        }
+        if (staged_once) __syncthreads();   // readers of the previous codebook are done
+        staged_once = true;
+        const int mode = stage_codebook(job, smem);
+        if (a == jb) copy_tail(job);
+        if (mode == GATHER_SMEM_F16) {
+            switch (job.stages) {
+                case 1: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<1>(job, t - jb, lane, smem); break;
+                case 2: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<2>(job, t - jb, lane, smem); break;
+                case 3: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<3>(job, t - jb, lane, smem); break;
+                case 4: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<4>(job, t - jb, lane, smem); break;
+                default: for (uint32_t t = a + warp; t < e; t += kWarps) tile_generic(job, t - jb, lane, smem, mode); break;
+            }
+        } else {
+            for (uint32_t t = a + warp; t < e; t += kWarps) tile_generic(job, t - jb, lane, smem, mode);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+struct DeviceInfo {
+    bool ready = false;
+    bool ok = false;
+    int sm_count = 0;
+    int max_smem = 0;
+};
+
+static DeviceInfo g_devices[kMaxDevices];
+static std::mutex g_dev_mutex;
+static thread_local int t_last_cuda_error = 0;
+
+static int cuda_fail(cudaError_t e) {
+    t_last_cuda_error = (int)e;
+    return RVQ_ERR_CUDA;
+}
+
+// Per-device set-up: SM count, opt-in shared memory, kernel attribute.
+static int device_info(DeviceInfo** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return RVQ_ERR_UNAVAILABLE; }
+    if (dev < 0 || dev >= kMaxDevices) return RVQ_ERR_UNAVAILABLE;
+    DeviceInfo& di = g_devices[dev];
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (!di.ready) {
+        di.ready = true;
+        cudaDeviceProp prop;
+        e = cudaGetDeviceProperties(&prop, dev);
+        if (e != cudaSuccess || prop.major != 10) {
+            if (e != cudaSuccess) t_last_cuda_error = (int)e;
+            di.ok = false;
+        } else {
+            di.sm_count = prop.multiProcessorCount;
+            di.max_smem = (int)prop.sharedMemPerBlockOptin;
+            e = cudaFuncSetAttribute(rvq_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     di.max_smem);
+            di.ok = (e == cudaSuccess);
+            if (e != cudaSuccess) t_last_cuda_error = (int)e;
+        }
+    }
+    if (!di.ok) return RVQ_ERR_UNAVAILABLE;
+    *out = &di;
+    return RVQ_OK;
+}
+
+static bool is_float_kind(int k) { return k == RVQ_F16 || k == RVQ_BF16 || k == RVQ_F32; }
+
+static int check_entry(const rvq_entry* e) {
+    if (!e) return RVQ_ERR_INVALID;
+    if (e->d != 8) return RVQ_ERR_UNSUPPORTED;
+    if (!is_float_kind(e->out_kind)) return RVQ_ERR_UNSUPPORTED;
+    if (e->index_kind != RVQ_U8 && e->index_kind != RVQ_I16) return RVQ_ERR_UNSUPPORTED;
+    if (e->codebook_kind != RVQ_F16 && e->codebook_kind != RVQ_F32) return RVQ_ERR_UNSUPPORTED;
+    if (!is_float_kind(e->scale_kind) || !is_float_kind(e->tail_kind)) return RVQ_ERR_UNSUPPORTED;
+    if (e->stages < 1 || e->stages > 65535 || e->ncodes < 1 || e->ncodes > 65536) return RVQ_ERR_INVALID;
+    if (e->index_kind == RVQ_U8 && e->ncodes > 256) return RVQ_ERR_INVALID;
+    if (e->nvec < 0 || e->tail_numel < 0 || e->trimmed < 0 || e->group_vecs < 1) return RVQ_ERR_INVALID;
+    if (e->nvec >= (1ll << 31) || e->group_vecs >= (1ll << 31) || e->tail_numel >= (1ll << 31))
+        return RVQ_ERR_TOO_LARGE;
+    if (e->stage_stride < e->nvec || (int64_t)e->stages * e->stage_stride >= (1ll << 40)) return RVQ_ERR_INVALID;
+    if (e->trimmed > e->nvec * 8) return RVQ_ERR_INVALID;
+    if (!e->out) return RVQ_ERR_INVALID;
+    if (e->nvec > 0 && (!e->indices || !e->codebook || !e->scales)) return RVQ_ERR_INVALID;
+    if (e->tail_numel > 0 && !e->tail) return RVQ_ERR_INVALID;
+    if (e->codebook && ((uintptr_t)e->codebook & 15)) return RVQ_ERR_INVALID;
+    return RVQ_OK;
+}
+
+static size_t stage_bytes_f16(int copies_log2, int64_t entries) { return (size_t)entries * 16u << copies_log2; }
+
+static int fill_rvq_job(const rvq_entry* e, Job& j, size_t& smem_need) {
+    memset(&j, 0, sizeof(j));
+    j.kind = JOB_RVQ;
+    j.idx = e->indices;
+    j.cb = e->codebook;
+    j.scales = e->scales;
+    j.tail = e->tail;
+    j.out = e->out;
+    j.nvec = (uint32_t)e->nvec;
+    j.stage_stride = (uint32_t)e->stage_stride;
+    if (e->stage_stride >= (1ll << 32)) return RVQ_ERR_TOO_LARGE;
+    j.gv = make_fastdiv((uint32_t)e->group_vecs);
+    j.trimmed = (uint64_t)e->trimmed;
+    j.full_vecs = (uint32_t)(e->trimmed / 8);
+    j.tail_numel = (uint32_t)e->tail_numel;
+    j.stages = (uint16_t)e->stages;
+    j.ncodes = (uint16_t)(e->ncodes == 65536 ? 0 : e->ncodes);
+    j.index_bytes = (uint8_t)(e->index_kind == RVQ_U8 ? 1 : 2);
+    j.cb_kind = (uint8_t)e->codebook_kind;
+    j.scale_kind = (uint8_t)e->scale_kind;
+    j.tail_kind = (uint8_t)e->tail_kind;
+    j.out_kind = (uint8_t)e->out_kind;
+    j.out_aligned = ((uintptr_t)e->out & 15) == 0;
+    const int64_t entries = (int64_t)e->stages * e->ncodes;
+    int cl = 3;
+    while (cl > 0 && stage_bytes_f16(cl, entries) > (size_t)kSmemBudget) --cl;
+    j.copies_log2 = (uint8_t)cl;
+    j.f16_fits = stage_bytes_f16(cl, entries) <= (size_t)kSmemBudget;
+    j.f32_fits = (size_t)entries * 32u <= (size_t)kSmemBudget;
+    size_t need = 0;
+    if (j.f16_fits) need = stage_bytes_f16(cl, entries);
+    if (j.cb_kind == RVQ_F32 && j.f32_fits) need = need > (size_t)entries * 32u ? need : (size_t)entries * 32u;
+    if (need > smem_need) smem_need = need;
+    uint32_t tiles = (uint32_t)((e->nvec + kTileVecs - 1) / kTileVecs);
+    if (tiles == 0 && e->tail_numel > 0) tiles = 1;
+    j.tile_count = tiles;
+    return RVQ_OK;
+}
+
+static int launch_jobs(LayerParams& p, size_t smem_need, void* stream) {
+    DeviceInfo* di = nullptr;
+    int rc = device_info(&di);
+    if (rc != RVQ_OK) return rc;
+    uint32_t total = 0;
+    for (int i = 0; i < p.njobs; ++i) {
+        p.jobs[i].tile_begin = total;
+        total += p.jobs[i].tile_count;
+    }
+    p.total_tiles = total;
+    if (total == 0) return RVQ_OK;
+    if (smem_need > (size_t)di->max_smem) return RVQ_ERR_TOO_LARGE;
+    uint32_t grid = (uint32_t)di->sm_count;
+    if (grid > total) grid = total;
+    rvq_layer_kernel<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return RVQ_OK;
+}
+
+}  // namespace rvq
+
+using namespace rvq;
+
+extern "C" {
+
+int rvq_available(void) {
+    DeviceInfo* di = nullptr;
+    return device_info(&di) == RVQ_OK ? 1 : 0;
+}
+
+int rvq_check_entry(const rvq_entry* e) { return check_entry(e); }
+
+int rvq_decode(const rvq_entry* e, void* stream) {
+    return rvq_decode_layer(e, 1, nullptr, 0, stream);
+}
+
+int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* copies, int n_copies,
+                     void* stream) {
+    if (n_entries < 0 || n_copies < 0 || n_entries + n_copies > RVQ_MAX_LAYER_JOBS) return RVQ_ERR_INVALID;
+    if ((n_entries && !entries) || (n_copies && !copies)) return RVQ_ERR_INVALID;
+    LayerParams p;
+    memset(&p, 0, sizeof(p));
+    size_t smem = 0;
+    for (int i = 0; i < n_entries; ++i) {
+        int rc = check_entry(&entries[i]);
+        if (rc != RVQ_OK) return rc;
+        rc = fill_rvq_job(&entries[i], p.jobs[p.njobs], smem);
+        if (rc != RVQ_OK) return rc;
+        p.njobs++;
+    }
+    for (int i = 0; i < n_copies; ++i) {
+        const rvq_copy& c = copies[i];
+        if (c.nbytes < 0 || c.nbytes >= (1ll << 31)) return RVQ_ERR_INVALID;
+        if (c.nbytes == 0) continue;
+        if (!c.src || !c.dst) return RVQ_ERR_INVALID;
+        Job& j = p.jobs[p.njobs++];
+        memset(&j, 0, sizeof(j));
+        j.kind = JOB_COPY;
+        j.idx = c.src;
+        j.out = c.dst;
+        j.nvec = (uint32_t)c.nbytes;
+        j.tile_count = (uint32_t)((c.nbytes + kCopyTileBytes - 1) / kCopyTileBytes);
+    }
+    return launch_jobs(p, smem, stream);
+}
+
+int rvq_take_index_error(void) {
+    unsigned int v = 0, zero = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return -RVQ_ERR_CUDA; }
+    e = cudaMemcpyFromSymbol(&v, g_index_error, sizeof(v));
+    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return -RVQ_ERR_CUDA; }
+    e = cudaMemcpyToSymbol(g_index_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return -RVQ_ERR_CUDA; }
+    return v ? 1 : 0;
+}
+
+int rvq_last_cuda_error(void) { return t_last_cuda_error; }
+
+const char* rvq_status_string(int status) {
+    switch (status) {
+        case RVQ_OK: return "ok";
+        case RVQ_ERR_INVALID: return "invalid argument";
+        case RVQ_ERR_UNSUPPORTED: return "unsupported entry";
+        case RVQ_ERR_UNAVAILABLE: return "no usable sm_100 CUDA device";
+        case RVQ_ERR_CUDA: return "CUDA runtime error";
+        case RVQ_ERR_TOO_LARGE: return "size exceeds a limit";
+        default: return "unknown status";
+    }
+}
+
+int rvq_version(void) { return 100; }
+
+// Host-side mirror of the device division, exported for CPU tests.
+uint32_t rvq_test_fastdiv(uint32_t d, uint32_t n) {
+    FastDiv f = make_fastdiv(d);
+    return fastdiv(n, f);
+}
+
+}  // extern "C"

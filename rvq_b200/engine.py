@@ -1,0 +1,121 @@
+"""Decode dispatch of the layerwise engine, B200 edition.
+
+Mirrors the reference's engine-level entry points so they stay drop-ins:
+
+* ``decode_into(entry, codebooks, out)``  -- infer_compressed_layerwise_triton.py:161-176
+* ``decode_to_tensor(entry, codebooks, device, runtime_dtype)`` -- same file, 179-188
+
+and adds ``LayerDecodePlan``: all entries of one decoder layer (7 RVQ
+projections + 4 bf16 norm copies for Qwen3) decoded by ONE kernel launch,
+with the C descriptors built once and reused every time the layer is
+decoded.  It replaces the per-key loop of ``prefetch_layer``
+(infer_compressed_layerwise_triton.py:246-266).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _native
+from .triton_decode_kernels import decode_rvq_triton_into, prepare_entry, rvq_triton_supported
+
+RVQ_METHODS = ("rvq_groupwise", "rvq_mlp")
+
+
+def decode_into(entry: Dict[str, object], codebooks: Dict[str, torch.Tensor], out: torch.Tensor):
+    """Reference: infer_compressed_layerwise_triton.py:161-176."""
+    method = entry["method"]
+    if method == "bf16_raw":
+        flat_data = entry["data"].view(torch.int16)
+        out.view(torch.int16).copy_(flat_data, non_blocking=True)
+    elif method in RVQ_METHODS:
+        codebook = codebooks[entry["codebook_id"]]
+        if not rvq_triton_supported(entry, out):
+            raise ValueError(f"Triton kernel does not support entry shape {entry['shape']}")
+        decode_rvq_triton_into(entry, codebook, out)
+    else:
+        raise ValueError(f"Unsupported decode method: {method}")
+
+
+def decode_to_tensor(entry: Dict[str, object], codebooks: Dict[str, torch.Tensor],
+                     device: torch.device, runtime_dtype: torch.dtype) -> torch.Tensor:
+    """Reference: infer_compressed_layerwise_triton.py:179-188."""
+    shape = tuple(entry["shape"])
+    out = torch.empty(shape, dtype=runtime_dtype, device=device)
+    decode_into(entry, codebooks, out)
+    return out
+
+
+class LayerDecodePlan:
+    """Everything one layer-slot fill needs, resolved once.
+
+    ``items``: ``(key, entry)`` pairs of one layer; ``outs[key]``: the slot
+    tensor each entry decodes into.  ``launch(stream)`` queues the whole
+    layer as ceil(jobs / 32) launches (one for a Qwen3 layer: 11 jobs).
+    The tensors referenced by the plan must outlive it.
+    """
+
+    def __init__(self, items: Sequence[Tuple[str, Dict[str, object]]],
+                 codebooks: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor]):
+        self.keys: List[str] = []
+        entries: List[_native.RvqEntry] = []
+        copies: List[Tuple[int, int, int]] = []
+        self._keep: list = []
+        self.algorithmic_bytes = 0
+        for key, entry in items:
+            out = outs[key]
+            method = entry["method"]
+            if method == "bf16_raw":
+                data = entry["data"]
+                if not data.is_cuda or not out.is_cuda:
+                    raise ValueError("bf16_raw copy needs CUDA source and slot tensors")
+                if data.element_size() != 2 or out.element_size() != 2:
+                    raise ValueError("bf16_raw copy is a 16-bit view copy")
+                if data.numel() != out.numel() or not out.is_contiguous():
+                    raise ValueError(f"slot for {key} does not match its bf16_raw entry")
+                data = data.contiguous()
+                self._keep.append(data)
+                nbytes = data.numel() * 2
+                copies.append((data.data_ptr(), out.data_ptr(), nbytes))
+                self.algorithmic_bytes += 2 * nbytes
+            elif method in RVQ_METHODS:
+                cb = codebooks[entry["codebook_id"]]
+                if not rvq_triton_supported(entry, out):
+                    raise ValueError(f"Triton kernel does not support entry shape {entry['shape']}")
+                st, keep = prepare_entry(entry, cb, out)
+                self._keep.append(keep)
+                entries.append(st)
+                idx = entry["indices"]
+                self.algorithmic_bytes += (out.numel() * out.element_size()
+                                           + idx.numel() * idx.element_size()
+                                           + entry["scales"].numel() * entry["scales"].element_size()
+                                           + entry["tail"].numel() * entry["tail"].element_size())
+            else:
+                raise ValueError(f"Unsupported decode method: {method}")
+            self.keys.append(key)
+        self.batches = []
+        jobs = [("e", e) for e in entries] + [("c", c) for c in copies]
+        for i in range(0, len(jobs), _native.RVQ_MAX_LAYER_JOBS):
+            chunk = jobs[i:i + _native.RVQ_MAX_LAYER_JOBS]
+            es = [j for t, j in chunk if t == "e"]
+            cs = [j for t, j in chunk if t == "c"]
+            earr = (_native.RvqEntry * max(len(es), 1))(*es)
+            carr = (_native.RvqCopy * max(len(cs), 1))(*[_native.RvqCopy(*c) for c in cs])
+            self.batches.append((earr, len(es), carr, len(cs)))
+        self._lib = _native.load()
+
+    @property
+    def launches(self) -> int:
+        return len(self.batches)
+
+    def launch(self, stream: Optional[int] = None) -> None:
+        if stream is None:
+            stream = torch.cuda.current_stream().cuda_stream
+        s = ctypes.c_void_p(stream)
+        for earr, ne, carr, nc in self.batches:
+            rc = self._lib.rvq_decode_layer(earr, ne, carr, nc, s)
+            if rc:
+                _native.check(rc, "rvq_decode_layer")

@@ -1,0 +1,125 @@
+"""C-ABI library: loads, exports what include/rvq_b200.h declares, and its
+host-side logic behaves (no GPU needed, no kernel launched)."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from rvq_b200 import _native
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER_DIR = os.path.join(REPO, "include")
+
+
+def declared_functions():
+    names = set()
+    for fn in os.listdir(HEADER_DIR):
+        if not fn.endswith(".h"):
+            continue
+        text = open(os.path.join(HEADER_DIR, fn)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^\s*[A-Za-z_][\w\s\*]*?\b(rvq_\w+)\s*\(", text, flags=re.M):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _native.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for required in ("rvq_decode", "rvq_decode_layer", "rvq_available", "rvq_check_entry"):
+        assert required in names, names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_struct_layout_matches_header(lib):
+    # 5 pointers + 5 int64 + 8 int32
+    assert ctypes.sizeof(_native.RvqEntry) == 5 * 8 + 5 * 8 + 8 * 4
+    assert ctypes.sizeof(_native.RvqCopy) == 24
+
+
+def test_status_strings(lib):
+    assert _native.status_string(0) == "ok"
+    for s in range(1, 6):
+        assert _native.status_string(s) != "unknown status"
+
+
+def test_fastdiv_host_mirror(lib):
+    rng = np.random.default_rng(0)
+    divisors = [1, 2, 3, 5, 7, 16, 20, 40, 320, 512, 640, 1216, 3200, 65535, 65536, 1 << 20,
+                (1 << 31) - 1, (1 << 31) + 12345, (1 << 32) - 1]
+    divisors += list(rng.integers(1, 1 << 32, size=40, dtype=np.uint64))
+    for d in divisors:
+        d = int(d)
+        ns = [0, 1, d - 1, d, d + 1, 2 * d - 1, (1 << 32) - 1, (1 << 31), (1 << 31) - 1]
+        ns += list(rng.integers(0, 1 << 32, size=200, dtype=np.uint64))
+        for n in ns:
+            n = int(n) & 0xFFFFFFFF
+            assert lib.rvq_test_fastdiv(d, n) == n // d, (d, n)
+
+
+def _fake_entry(**kw):
+    e = _native.RvqEntry()
+    e.indices, e.codebook, e.scales, e.tail, e.out = 0x1000, 0x2000, 0x3000, 0, 0x4000
+    e.nvec, e.stage_stride, e.group_vecs, e.trimmed, e.tail_numel = 1024, 1024, 16, 8192, 0
+    e.stages, e.ncodes, e.d = 4, 256, 8
+    e.index_kind, e.codebook_kind, e.scale_kind = _native.RVQ_U8, _native.RVQ_F32, _native.RVQ_F16
+    e.tail_kind, e.out_kind = _native.RVQ_BF16, _native.RVQ_BF16
+    for k, v in kw.items():
+        setattr(e, k, v)
+    return e
+
+
+@pytest.mark.parametrize("field,value,status", [
+    ("d", 4, _native.RVQ_ERR_UNSUPPORTED),
+    ("out_kind", _native.RVQ_U8, _native.RVQ_ERR_UNSUPPORTED),
+    ("index_kind", _native.RVQ_F16, _native.RVQ_ERR_UNSUPPORTED),
+    ("stages", 0, _native.RVQ_ERR_INVALID),
+    ("ncodes", 300, _native.RVQ_ERR_INVALID),          # > 256 with uint8 indices
+    ("group_vecs", 0, _native.RVQ_ERR_INVALID),
+    ("trimmed", 1024 * 8 + 1, _native.RVQ_ERR_INVALID),
+    ("stage_stride", 1000, _native.RVQ_ERR_INVALID),
+    ("out", 0, _native.RVQ_ERR_INVALID),
+    ("tail_numel", 5, _native.RVQ_ERR_INVALID),          # tail pointer is NULL
+    ("codebook", 0x2004, _native.RVQ_ERR_INVALID),       # not 16-byte aligned
+    ("nvec", 1 << 31, _native.RVQ_ERR_TOO_LARGE),
+])
+def test_check_entry_rejects(lib, field, value, status):
+    e = _fake_entry(**{field: value})
+    if field == "nvec":
+        e.stage_stride = value
+    assert lib.rvq_check_entry(ctypes.byref(e)) == status
+
+
+def test_check_entry_accepts_valid(lib):
+    assert lib.rvq_check_entry(ctypes.byref(_fake_entry())) == 0
+    e = _fake_entry(index_kind=_native.RVQ_I16, ncodes=512)
+    assert lib.rvq_check_entry(ctypes.byref(e)) == 0
+
+
+def test_layer_call_rejects_too_many_jobs(lib):
+    arr = (_native.RvqEntry * 40)(*[_fake_entry() for _ in range(40)])
+    assert lib.rvq_decode_layer(arr, 40, None, 0, None) == _native.RVQ_ERR_INVALID
+
+
+def test_no_device_means_unavailable():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    from rvq_b200 import triton_decode_kernels as tdk
+    assert tdk.triton_available() is False
+    assert _native.load().rvq_available() == 0
+    with pytest.raises(RuntimeError):
+        import torch as _t
+        entry = {"d": 8, "group_size": 8, "trimmed_numel": 8, "method": "rvq_groupwise"}
+        tdk.decode_rvq_triton_into(entry, _t.zeros(1, 256, 8), _t.zeros(8))
