@@ -302,7 +302,8 @@ def time_e2e(rel, cbs_host, device, steps, warmup, stream):
                for ek, ev in e.items()} for k, e in rel.items()}
     dev_cbs = {k: torch.empty_like(v, device=device) for k, v in host_cbs.items()}
     slot = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16, device=device) for k, e in rel.items()}
-    back = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16).pin_memory() for k in rel}
+    back = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16).pin_memory()
+            for k, e in rel.items()}
     h2d = sum(v.numel() * v.element_size() for e in host.values() for v in e.values() if torch.is_tensor(v))
     h2d += sum(v.numel() * v.element_size() for v in host_cbs.values())
     d2h = sum(v.numel() * v.element_size() for v in back.values())

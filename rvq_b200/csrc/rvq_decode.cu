@@ -75,7 +75,9 @@ struct Job {
     uint8_t f16_fits;       // fp16 staging fits in shared memory
     uint8_t f32_fits;       // fp32 staging fits in shared memory
     uint8_t out_aligned;    // out is 16-byte aligned
-    uint8_t pad[2];
+    uint8_t fast_ok;        // eligible for the streaming fast path (see fill_rvq_job)
+    uint8_t pad;
+    uint32_t full_tiles;    // tiles whose 128 vectors are all complete (< full_vecs, < nvec)
 };
 
 struct LayerParams {
@@ -176,48 +178,66 @@ __device__ int stage_codebook(const Job& job, uint4* smem) {
     return GATHER_GLOBAL;
 }
 
-// Fast tile: fp16 codebook staged with 1 << copies_log2 copies, KT stages
-// known at compile time (1..4).
+// Fast path: u8 indices over 256 codes, fp16 staging with 8 copies, KT = 4
+// stages (the compressor's default), 16-bit output, every vector of every tile complete.  Each warp
+// walks tiles ta+warp, ta+warp+32, ... and prefetches the next tile's index
+// words and scales while it decodes the current one.  Codes travel by
+// shuffle: lane L loads index word L of a plane (codes of vectors 4L..4L+3)
+// and lane l takes byte (l & 3) of lane 8j + l/4's word for vector 32j + l.
 template <int KT>
-__device__ __forceinline__ void tile_fast(const Job& job, uint32_t tile, int lane, const uint4* smem) {
-    const uint32_t v0 = tile * kTileVecs;
-    const uint32_t cpy = lane & ((1u << job.copies_log2) - 1u);
-    const uint32_t ncodes = job.ncodes ? job.ncodes : 65536u;
-    bool bad = false;
-    uint32_t code[kJ][KT];
+__device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane,
+                                         const uint4* smem) {
+    const int out_kind = job.out_kind;
+    // the few job fields the loop needs, read once from parameter space
+    const uint32_t* idx32 = reinterpret_cast<const uint32_t*>(job.idx);
+    const uint32_t plane32 = job.stage_stride >> 2;
+    uint4* out = reinterpret_cast<uint4*>(job.out);
+    const unsigned short* scales = reinterpret_cast<const unsigned short*>(job.scales);
+    const FastDiv gv = job.gv;
+    const uint32_t cpy = lane & 7;
+    const uint32_t bsel = 0x4440u | (lane & 3);
+    uint32_t t = ta + warp;
+    uint32_t w[KT];
+    if (t < tb) {
 #pragma unroll
-    for (int j = 0; j < kJ; ++j) {
-        uint32_t n = v0 + 32 * j + lane;
-#pragma unroll
-        for (int k = 0; k < KT; ++k) code[j][k] = (n < job.nvec) ? load_code(job, k, n, bad) : 0u;
+        for (int k = 0; k < KT; ++k) w[k] = __ldg(idx32 + (size_t)k * plane32 + ((t * kTileVecs) >> 2) + lane);
     }
+    for (; t < tb; t += kWarps) {
+        // next tile's index words are requested before this tile is decoded;
+        // scales are a few hundred bytes per CTA and stay in L1
+        uint32_t wn[KT];
+        if (t + kWarps < tb) {
 #pragma unroll
-    for (int j = 0; j < kJ; ++j) {
-        uint32_t n = v0 + 32 * j + lane;
-        if (n >= job.nvec) break;
-        float acc[8];
+            for (int k = 0; k < KT; ++k)
+                wn[k] = __ldg(idx32 + (size_t)k * plane32 + (((t + kWarps) * kTileVecs) >> 2) + lane);
+        }
+        const uint32_t v0 = t * kTileVecs;
 #pragma unroll
-        for (int k = 0; k < KT; ++k) {
-            uint4 q = smem[((k * ncodes + code[j][k]) << job.copies_log2) + cpy];
-            uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        for (int j = 0; j < kJ; ++j) {
+            const uint32_t n = v0 + 32 * j + lane;
+            const float s = __half2float(__ushort_as_half(__ldg(scales + fastdiv(n, gv))));
+            float acc[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                uint16_t lo = (uint16_t)(w[i] & 0xFFFFu), hi = (uint16_t)(w[i] >> 16);
-                if (k == 0) {
-                    acc[2 * i] = add_f16_f32(lo, 0.0f);
-                    acc[2 * i + 1] = add_f16_f32(hi, 0.0f);
-                } else {
-                    acc[2 * i] = add_f16_f32(lo, acc[2 * i]);
-                    acc[2 * i + 1] = add_f16_f32(hi, acc[2 * i + 1]);
+            for (int k = 0; k < KT; ++k) {
+                const uint32_t c = __byte_perm(__shfl_sync(0xffffffffu, w[k], 8 * j + (lane >> 2)), 0, bsel);
+                const uint4 q = smem[((k * 256u + c) << 3) + cpy];
+                const uint32_t ws[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[2 * i] = add_f16_f32((uint16_t)(ws[i] & 0xFFFFu), k == 0 ? 0.0f : acc[2 * i]);
+                    acc[2 * i + 1] = add_f16_f32((uint16_t)(ws[i] >> 16), k == 0 ? 0.0f : acc[2 * i + 1]);
                 }
             }
+            uint4 q;
+            q.x = pack2(__fmul_rn(acc[0], s), __fmul_rn(acc[1], s), out_kind);
+            q.y = pack2(__fmul_rn(acc[2], s), __fmul_rn(acc[3], s), out_kind);
+            q.z = pack2(__fmul_rn(acc[4], s), __fmul_rn(acc[5], s), out_kind);
+            q.w = pack2(__fmul_rn(acc[6], s), __fmul_rn(acc[7], s), out_kind);
+            out[n] = q;
         }
-        float s = load_scale(job, n);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) acc[t] = __fmul_rn(acc[t], s);
-        store_vec(job, n, acc);
+        for (int k = 0; k < KT; ++k) w[k] = wn[k];
     }
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(&g_index_error, 1u);
 }
 
 // Generic tile: any stage count and gather mode.
@@ -305,10 +325,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
     const uint32_t t1 = (uint32_t)(((uint64_t)T * (b + 1)) / G);
     bool staged_once = false;
     for (int j = 0; j < p.njobs; ++j) {
-        const Job& job = p.jobs[j];
-        const uint32_t jb = job.tile_begin, je = jb + job.tile_count;
+        const uint32_t jb = p.jobs[j].tile_begin, je = jb + p.jobs[j].tile_count;
         const uint32_t a = max(t0, jb), e = min(t1, je);
         if (a >= e) continue;
+        const Job& job = p.jobs[j];
         if (job.kind == JOB_COPY) {
             for (uint32_t t = a + warp; t < e; t += kWarps) copy_tile(job, t - jb, lane);
             continue;
@@ -321,17 +341,15 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
         staged_once = true;
         const int mode = stage_codebook(job, smem);
         if (a == jb) copy_tail(job);
-        if (mode == GATHER_SMEM_F16) {
-            switch (job.stages) {
-                case 1: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<1>(job, t - jb, lane, smem); break;
-                case 2: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<2>(job, t - jb, lane, smem); break;
-                case 3: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<3>(job, t - jb, lane, smem); break;
-                case 4: for (uint32_t t = a + warp; t < e; t += kWarps) tile_fast<4>(job, t - jb, lane, smem); break;
-                default: for (uint32_t t = a + warp; t < e; t += kWarps) tile_generic(job, t - jb, lane, smem, mode); break;
+        uint32_t g = a;                     // first tile left for the generic path
+        if (mode == GATHER_SMEM_F16 && job.fast_ok) {
+            const uint32_t fe = min(e, jb + job.full_tiles);
+            if (a < fe) {
+                run_fast<4>(job, a - jb, fe - jb, warp, lane, smem);
+                g = fe;
             }
-        } else {
-            for (uint32_t t = a + warp; t < e; t += kWarps) tile_generic(job, t - jb, lane, smem, mode);
         }
+        for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t - jb, lane, smem, mode);
     }
 }
 
@@ -445,6 +463,12 @@ static int fill_rvq_job(const rvq_entry* e, Job& j, size_t& smem_need) {
     uint32_t tiles = (uint32_t)((e->nvec + kTileVecs - 1) / kTileVecs);
     if (tiles == 0 && e->tail_numel > 0) tiles = 1;
     j.tile_count = tiles;
+    const uint64_t complete = (uint64_t)(e->nvec < (int64_t)j.full_vecs ? e->nvec : j.full_vecs);
+    j.full_tiles = (uint32_t)(complete / kTileVecs);
+    j.fast_ok = e->index_kind == RVQ_U8 && e->ncodes == 256 && e->stages == 4 && cl == 3 &&
+                (e->out_kind == RVQ_BF16 || e->out_kind == RVQ_F16) && j.out_aligned &&
+                e->scale_kind == RVQ_F16 &&
+                ((uintptr_t)e->indices & 3) == 0 && (e->stage_stride & 3) == 0;
     return RVQ_OK;
 }
 
