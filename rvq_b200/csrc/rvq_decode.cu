@@ -78,12 +78,15 @@ struct Job {
     uint8_t fast_ok;        // eligible for the streaming fast path (see fill_rvq_job)
     uint8_t pad;
     uint32_t full_tiles;    // tiles whose 128 vectors are all complete (< full_vecs, < nvec)
+    uint32_t cta_begin;     // job-per-CTA schedule: first CTA of this job
+    uint32_t cta_count;     // job-per-CTA schedule: CTAs of this job (copies: owning CTA in cta_begin)
 };
 
 struct LayerParams {
     Job jobs[RVQ_MAX_LAYER_JOBS];
     int njobs;
     uint32_t total_tiles;
+    uint32_t per_cta_jobs;  // 1: every CTA works on one RVQ job; 0: contiguous tile ranges
 };
 
 __device__ unsigned int g_index_error;
@@ -317,13 +320,53 @@ __device__ void copy_tail(const Job& job) {
     }
 }
 
+// Decode tiles [a, e) (job-local) of one RVQ job; `owner` copies the tail.
+// All threads of the CTA call it.
+__device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t e, bool owner, int warp,
+                                            int lane, uint4* smem, bool& staged_once) {
+    if (job.nvec == 0) {                    // tail-only entry: nothing to stage
+        if (owner) copy_tail(job);
+        return;
+    }
+    if (staged_once) __syncthreads();       // readers of the previous codebook are done
+    staged_once = true;
+    const int mode = stage_codebook(job, smem);
+    if (owner) copy_tail(job);
+    uint32_t g = a;                         // first tile left for the generic path
+    if (mode == GATHER_SMEM_F16 && job.fast_ok) {
+        const uint32_t fe = min(e, job.full_tiles);
+        if (a < fe) {
+            run_fast<4>(job, a, fe, warp, lane, smem);
+            g = fe;
+        }
+    }
+    for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t, lane, smem, mode);
+}
+
 __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_constant__ LayerParams p) {
     extern __shared__ uint4 smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t T = p.total_tiles, G = gridDim.x, b = blockIdx.x;
+    const uint32_t G = gridDim.x, b = blockIdx.x;
+    bool staged_once = false;
+    if (p.per_cta_jobs) {
+        // raw copies first (each owned by one CTA), then this CTA's share of its RVQ job
+        for (int j = 0; j < p.njobs; ++j) {
+            const Job& job = p.jobs[j];
+            if (job.kind == JOB_COPY && job.cta_begin == b)
+                for (uint32_t t = warp; t < job.tile_count; t += kWarps) copy_tile(job, t, lane);
+        }
+        for (int j = 0; j < p.njobs; ++j) {
+            const Job& job = p.jobs[j];
+            if (job.kind != JOB_RVQ || b < job.cta_begin || b >= job.cta_begin + job.cta_count) continue;
+            const uint32_t r = b - job.cta_begin, cc = job.cta_count, tc = job.tile_count;
+            const uint32_t a = (uint32_t)(((uint64_t)tc * r) / cc), e = (uint32_t)(((uint64_t)tc * (r + 1)) / cc);
+            process_rvq(job, a, e, r == 0, warp, lane, smem, staged_once);
+        }
+        return;
+    }
+    const uint32_t T = p.total_tiles;
     const uint32_t t0 = (uint32_t)(((uint64_t)T * b) / G);
     const uint32_t t1 = (uint32_t)(((uint64_t)T * (b + 1)) / G);
-    bool staged_once = false;
     for (int j = 0; j < p.njobs; ++j) {
         const uint32_t jb = p.jobs[j].tile_begin, je = jb + p.jobs[j].tile_count;
         const uint32_t a = max(t0, jb), e = min(t1, je);
@@ -333,23 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
             for (uint32_t t = a + warp; t < e; t += kWarps) copy_tile(job, t - jb, lane);
             continue;
         }
-        if (job.nvec == 0) {                // tail-only entry: nothing to stage
-            if (a == jb) copy_tail(job);
-            continue;
-        }
-        if (staged_once) __syncthreads();   // readers of the previous codebook are done
-        staged_once = true;
-        const int mode = stage_codebook(job, smem);
-        if (a == jb) copy_tail(job);
-        uint32_t g = a;                     // first tile left for the generic path
-        if (mode == GATHER_SMEM_F16 && job.fast_ok) {
-            const uint32_t fe = min(e, jb + job.full_tiles);
-            if (a < fe) {
-                run_fast<4>(job, a - jb, fe - jb, warp, lane, smem);
-                g = fe;
-            }
-        }
-        for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t - jb, lane, smem, mode);
+        process_rvq(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
     }
 }
 
@@ -472,6 +499,64 @@ static int fill_rvq_job(const rvq_entry* e, Job& j, size_t& smem_need) {
     return RVQ_OK;
 }
 
+// Job-per-CTA schedule: every RVQ job gets a number of CTAs proportional
+// to its tiles (largest remainder, at least one), so no CTA restages a
+// codebook or waits at a job boundary.  Returns the grid size, or 0 when
+// the jobs do not fit that scheme (more RVQ jobs than half the SMs).
+static uint32_t plan_per_cta(LayerParams& p, uint32_t sms) {
+    uint32_t n_rvq = 0;
+    uint64_t total = 0;
+    for (int i = 0; i < p.njobs; ++i)
+        if (p.jobs[i].kind == JOB_RVQ && p.jobs[i].tile_count) { ++n_rvq; total += p.jobs[i].tile_count; }
+    if (n_rvq == 0 || 2 * n_rvq > sms) return 0;
+    double ideal[RVQ_MAX_LAYER_JOBS] = {0};
+    uint32_t cnt[RVQ_MAX_LAYER_JOBS] = {0};
+    uint32_t sum = 0;
+    for (int i = 0; i < p.njobs; ++i) {
+        const Job& j = p.jobs[i];
+        if (j.kind != JOB_RVQ || !j.tile_count) continue;
+        ideal[i] = (double)sms * j.tile_count / (double)total;
+        uint32_t c = (uint32_t)ideal[i];
+        if (c < 1) c = 1;
+        if (c > j.tile_count) c = j.tile_count;
+        cnt[i] = c;
+        sum += c;
+    }
+    while (sum > sms) {                     // at-least-one rounding overshot: take from the richest
+        int best = -1;
+        double bd = -1e30;
+        for (int i = 0; i < p.njobs; ++i)
+            if (cnt[i] > 1 && cnt[i] - ideal[i] > bd) { bd = cnt[i] - ideal[i]; best = i; }
+        if (best < 0) return 0;
+        --cnt[best];
+        --sum;
+    }
+    while (sum < sms) {                     // hand out the rest by largest remainder
+        int best = -1;
+        double bd = -1e30;
+        for (int i = 0; i < p.njobs; ++i)
+            if (p.jobs[i].kind == JOB_RVQ && cnt[i] && cnt[i] < p.jobs[i].tile_count && ideal[i] - cnt[i] > bd) {
+                bd = ideal[i] - cnt[i];
+                best = i;
+            }
+        if (best < 0) break;
+        ++cnt[best];
+        ++sum;
+    }
+    uint32_t begin = 0, copy_owner = 0;
+    for (int i = 0; i < p.njobs; ++i) {
+        Job& j = p.jobs[i];
+        if (j.kind == JOB_RVQ) {
+            j.cta_begin = begin;
+            j.cta_count = cnt[i];
+            begin += cnt[i];
+        }
+    }
+    for (int i = 0; i < p.njobs; ++i)
+        if (p.jobs[i].kind == JOB_COPY) p.jobs[i].cta_begin = (copy_owner++) % (begin ? begin : 1);
+    return begin;
+}
+
 static int launch_jobs(LayerParams& p, size_t smem_need, void* stream) {
     DeviceInfo* di = nullptr;
     int rc = device_info(&di);
@@ -484,8 +569,12 @@ static int launch_jobs(LayerParams& p, size_t smem_need, void* stream) {
     p.total_tiles = total;
     if (total == 0) return RVQ_OK;
     if (smem_need > (size_t)di->max_smem) return RVQ_ERR_TOO_LARGE;
-    uint32_t grid = (uint32_t)di->sm_count;
-    if (grid > total) grid = total;
+    uint32_t grid = plan_per_cta(p, (uint32_t)di->sm_count);
+    p.per_cta_jobs = grid ? 1u : 0u;
+    if (!grid) {
+        grid = (uint32_t)di->sm_count;
+        if (grid > total) grid = total;
+    }
     rvq_layer_kernel<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);

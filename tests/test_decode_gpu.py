@@ -194,3 +194,39 @@ def test_reference_exceptions(cuda_device):
         decode_rvq_triton_into(dict(entry, indices=entry["indices"].cpu()), cb, out)
     with pytest.raises(NotImplementedError):
         decode_rvq_triton_into(entry, cb, out.to(torch.int32))
+
+
+def test_layer_launch_many_mixed_entries(cuda_device):
+    """One launch, 25 RVQ entries of very different sizes (1 tile .. ~100 tiles,
+    K = 1..4, int16 codes, tails) plus raw copies: the per-CTA job schedule
+    must give every entry exactly the reference's result."""
+    from rvq_b200.engine import LayerDecodePlan
+    g = torch.Generator().manual_seed(77)
+    items, cbs, outs, wants = [], {}, {}, {}
+    shapes = [(8, 8), (64, 64), (3, 40), (500, 256), (1000, 96), (17, 8), (256, 512), (2, 1024)]
+    for i in range(25):
+        o, inn = shapes[i % len(shapes)]
+        stages = [4, 4, 3, 2, 1, 4][i % 6]
+        ncodes = 512 if i % 7 == 3 else 256
+        group = [inn, 8, 64, inn][i % 4] if inn % 64 == 0 else inn
+        if (o * inn) % 8:
+            continue
+        cb = synthetic.make_codebook(stages, ncodes, 8, g)
+        e = synthetic.make_rvq_entry(o, inn, g, stages=stages, ncodes=ncodes, group_size=group,
+                                     codebook_id=f"cb{i}")
+        wants[f"e{i}"] = decode_rvq_bits_c(entry_np_from_torch(e, cb), OUT_BF16)
+        cbs[f"cb{i}"] = cb.to(cuda_device, torch.float32 if i % 2 else torch.float16)
+        items.append((f"e{i}", {k: (v.to(cuda_device) if torch.is_tensor(v) else v) for k, v in e.items()}))
+        outs[f"e{i}"] = torch.empty((o, inn), dtype=torch.bfloat16, device=cuda_device)
+    for i in range(4):
+        data = torch.randn(300 + 7 * i, generator=g).to(torch.bfloat16)
+        key = f"norm{i}"
+        items.append((key, synthetic.make_raw_entry(data) | {"data": data.to(cuda_device)}))
+        outs[key] = torch.empty(data.shape, dtype=torch.bfloat16, device=cuda_device)
+        wants[key] = data.view(torch.int16).numpy().view(np.uint16)
+    plan = LayerDecodePlan(items, cbs, outs)
+    assert plan.launches == 1
+    plan.launch()
+    torch.cuda.synchronize()
+    for key, want in wants.items():
+        assert bits_equal(out_bits(outs[key]), want, OUT_BF16), key
