@@ -417,9 +417,13 @@ static int device_info(DeviceInfo** out) {
             di.ok = false;
         } else {
             di.sm_count = prop.multiProcessorCount;
-            di.max_smem = (int)prop.sharedMemPerBlockOptin;
-            e = cudaFuncSetAttribute(rvq_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     di.max_smem);
+            cudaFuncAttributes fa;
+            e = cudaFuncGetAttributes(&fa, rvq_layer_kernel);
+            // dynamic shared memory may use what the kernel's static shared memory leaves
+            di.max_smem = (int)prop.sharedMemPerBlockOptin - (e == cudaSuccess ? (int)fa.sharedSizeBytes : 0);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(rvq_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         di.max_smem);
             di.ok = (e == cudaSuccess);
             if (e != cudaSuccess) t_last_cuda_error = (int)e;
         }
