@@ -179,3 +179,41 @@ def algorithmic_decode_bytes(entry: Dict[str, object], out_elem_bytes: int = 2,
     return (numel * out_elem_bytes + idx.numel() * idx.element_size()
             + entry["scales"].numel() * entry["scales"].element_size()
             + entry["tail"].numel() * entry["tail"].element_size() + codebook_bytes)
+
+
+def qwen3_config(shape: BlockShape, n_layers: int, vocab: int, *, rope_theta: float = 1e6,
+                 max_positions: int = 4096, rms_eps: float = 1e-6):
+    """A Qwen3 config of the given block shape with tied embeddings."""
+    from transformers import Qwen3Config
+    cfg = Qwen3Config(
+        vocab_size=vocab, hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+        num_hidden_layers=n_layers, num_attention_heads=shape.n_heads,
+        num_key_value_heads=shape.n_kv_heads, head_dim=shape.head_dim,
+        max_position_embeddings=max_positions, rms_norm_eps=rms_eps,
+        tie_word_embeddings=True, torch_dtype="bfloat16")
+    try:
+        cfg.rope_theta = rope_theta
+        if getattr(cfg, "rope_parameters", None) is not None:
+            cfg.rope_parameters["rope_theta"] = rope_theta
+    except Exception:
+        pass
+    cfg._attn_implementation = "eager"
+    return cfg
+
+
+def make_model_artifact(shape: BlockShape, n_layers: int, vocab: int, seed: int = 0, *,
+                        stages: int = 4, ncodes: int = 256, group_size: Optional[int] = None,
+                        embed_std: float = 0.02) -> Dict[str, object]:
+    """A whole random-init model in artifact form: bf16_raw tied embeddings,
+    per-layer RVQ projections and bf16 norms, final norm; one codebook per
+    projection family (the compressor's default "family" share mode)."""
+    gen = torch.Generator().manual_seed(seed)
+    cbs = make_family_codebooks(gen, stages=stages, ncodes=ncodes)
+    entries: Dict[str, Dict[str, object]] = {}
+    embed = torch.randn(vocab, shape.hidden, generator=gen) * embed_std
+    entries["model.embed_tokens.weight"] = make_raw_entry(embed)
+    for l in range(n_layers):
+        entries.update(make_block_entries(shape, l, gen, stages=stages, ncodes=ncodes,
+                                          group_size=group_size))
+    entries["model.norm.weight"] = make_raw_entry(1.0 + 0.02 * torch.randn(shape.hidden, generator=gen))
+    return {"format_version": 1, "model_type": "qwen3", "shared_codebooks": cbs, "entries": entries}

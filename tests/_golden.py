@@ -67,8 +67,10 @@ class GoldenCase:
 
 
 def case_names() -> List[str]:
+    """Decode fixtures (engine fixtures are named engine_*)."""
     return sorted(os.path.splitext(os.path.basename(p))[0]
-                  for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+                  for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
+                  if not os.path.basename(p).startswith("engine_"))
 
 
 def load_case(name: str) -> GoldenCase:
