@@ -22,6 +22,7 @@
 #ifndef RVQ_B200_H
 #define RVQ_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -109,6 +110,36 @@ int rvq_decode(const rvq_entry* e, void* stream);
  * (infer_compressed_layerwise_single_slot.py:652-668). */
 int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* copies,
                      int n_copies, void* stream);
+
+/* One fused dequant-GEMV y = W x for a batch of one (no counterpart in the
+ * reference, which reconstructs W into the slot and then calls F.linear:
+ * infer_compressed_layerwise_triton.py:290-292 / lines 296-297).  W is an
+ * RVQ entry with K=4 stages, 256 codes, uint8 codes, no tail; `rows` x `cols`
+ * is its shape (cols a multiple of 32, code planes 4-byte aligned).  The product is computed through
+ * per-stage lookup tables of codeword . x dot products, i.e. W is never
+ * materialised and never rounded to bf16: results match "reconstruct, round
+ * to bf16, matmul" to within the bf16 rounding of W (about 1e-3 relative). */
+typedef struct rvq_gemv_job {
+    rvq_entry weight;         /* the weight entry; weight.out is ignored */
+    const void* x;            /* device, [cols] activations of x_kind */
+    void* y;                  /* device, [rows] output of y_kind */
+    int64_t rows;
+    int64_t cols;
+    int32_t x_kind;           /* RVQ_BF16, RVQ_F16 or RVQ_F32 */
+    int32_t y_kind;           /* RVQ_BF16, RVQ_F16 or RVQ_F32 */
+} rvq_gemv_job;
+
+/* Bytes of device workspace rvq_gemv needs for these jobs (per-tile row
+ * partials and row-range tickets).  The workspace must be zero-filled once
+ * when it is allocated; every launch leaves its tickets at zero again.
+ * Launches that share a workspace must not overlap on the GPU. */
+size_t rvq_gemv_workspace_size(const rvq_gemv_job* jobs, int n_jobs);
+
+/* Up to 16 GEMVs (e.g. q, k and v of one layer, sharing x) in one launch.
+ * Deterministic: partial sums over 256-column tiles are added in tile order.
+ * `workspace` is 256-byte aligned device memory of at least
+ * rvq_gemv_workspace_size() bytes. */
+int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Reads and clears the sticky device flag that kernels set when an index is
  * outside [0, ncodes) (the decoded element then uses code 0).  Synchronises

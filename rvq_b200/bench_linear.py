@@ -1,0 +1,104 @@
+"""Linear-layer microbenchmark on the [9728 x 2560] gate projection.
+
+    python -m rvq_b200.bench_linear [--reps 200]
+
+Times, with CUDA events on one stream and weights rotated over 16 resident
+copies (so no copy's codes stay in L2 between uses):
+
+* ``fused``:  rvq_gemv (batch 1), W never materialised;
+* ``decode+gemm``: rvq_decode_layer into a bf16 slot, then torch.matmul
+  (cuBLAS) -- the reference's dataflow (infer_compressed_layerwise_triton.py:
+  263, 290-292);
+* ``dense``: torch.matmul on a resident bf16 weight (the uncompressed model);
+
+at batch 1, 8, 64 and a 2048-token prefill.  Prints one JSON object.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import synthetic
+from .engine import LayerDecodePlan
+from .gemv import GemvPlan
+
+ROWS, COLS = 9728, 2560
+COPIES = 16
+
+
+def _time(fn, reps, stream):
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(reps):
+        fn(i)
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps * 1e3      # us
+
+
+def run(reps: int = 200, device="cuda:0"):
+    device = torch.device(device)
+    torch.cuda.set_device(device)
+    g = torch.Generator().manual_seed(0)
+    cb = synthetic.make_codebook(4, 256, 8, g)
+    entry = synthetic.make_rvq_entry(ROWS, COLS, g, codebook_id="mlp_gate_proj")
+    cbd = cb.to(device, torch.float32)
+    copies = [{k: (v.to(device) if torch.is_tensor(v) else v) for k, v in entry.items()} for _ in range(COPIES)]
+    stream = torch.cuda.current_stream(device)
+    out = {"workload": "gate projection [9728 x 2560], K=4, 256 codes, d=8, per-row fp16 scales, bf16 activations",
+           "weights_rotated": COPIES, "results": {}}
+    code_bytes = copies[0]["indices"].numel() + copies[0]["scales"].numel() * 2
+
+    # fused GEMV, batch 1
+    x1 = torch.randn(COLS, generator=g).to(device, torch.bfloat16)
+    ys = [torch.empty(ROWS, dtype=torch.bfloat16, device=device) for _ in range(COPIES)]
+    plans = [GemvPlan([(c, cbd, x1, y)]) for c, y in zip(copies, ys)]
+    t = _time(lambda i: plans[i % COPIES].launch(stream.cuda_stream), reps, stream)
+    algo = code_bytes + COLS * 2 + ROWS * 2
+    out["results"]["fused_b1"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
+                                  "algorithmic_bytes": algo}
+
+    # decode + GEMM (slot then cuBLAS), and dense
+    slot = torch.empty(ROWS, COLS, dtype=torch.bfloat16, device=device)
+    dplans = [LayerDecodePlan([("w", c)], {"mlp_gate_proj": cbd}, {"w": slot}) for c in copies]
+    dense = []
+    for i in range(COPIES):
+        dplans[i].launch(stream.cuda_stream)
+        dense.append(slot.clone())
+    t_dec = _time(lambda i: dplans[i % COPIES].launch(stream.cuda_stream), reps, stream)
+    out["results"]["decode_only"] = {"us": round(t_dec, 2)}
+    for b in (1, 8, 64, 2048):
+        x = torch.randn(b, COLS, generator=g).to(device, torch.bfloat16)
+
+        def dec_gemm(i, x=x):
+            dplans[i % COPIES].launch(stream.cuda_stream)
+            torch.matmul(x, slot.t())
+
+        def dense_mm(i, x=x):
+            torch.matmul(x, dense[i % COPIES].t())
+
+        r = reps if b < 2048 else max(20, reps // 10)
+        t_dg = _time(dec_gemm, r, stream)
+        t_dn = _time(dense_mm, r, stream)
+        flops = 2.0 * b * ROWS * COLS
+        out["results"][f"decode+gemm_b{b}"] = {"us": round(t_dg, 2), "TFLOP/s": round(flops / t_dg / 1e6, 2)}
+        out["results"][f"dense_b{b}"] = {"us": round(t_dn, 2), "TFLOP/s": round(flops / t_dn / 1e6, 2),
+                                         "GB/s": round((ROWS * COLS * 2 + b * (COLS + ROWS) * 2) / t_dn / 1e3, 1)}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reps", type=int, default=200)
+    a = ap.parse_args()
+    print(json.dumps(run(a.reps)))
+
+
+if __name__ == "__main__":
+    main()

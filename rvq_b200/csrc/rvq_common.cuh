@@ -74,6 +74,13 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int out_kind) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Last CUDA error seen by the library on the calling thread (shared by all
+// translation units through this inline function's static).
+inline int& last_cuda_error_slot() {
+    static thread_local int v = 0;
+    return v;
+}
+
 inline int elem_bytes(int kind) {
     switch (kind) {
         case RVQ_F16: case RVQ_BF16: case RVQ_I16: return 2;

@@ -393,10 +393,9 @@ struct DeviceInfo {
 
 static DeviceInfo g_devices[kMaxDevices];
 static std::mutex g_dev_mutex;
-static thread_local int t_last_cuda_error = 0;
 
 static int cuda_fail(cudaError_t e) {
-    t_last_cuda_error = (int)e;
+    last_cuda_error_slot() = (int)e;
     return RVQ_ERR_CUDA;
 }
 
@@ -404,7 +403,7 @@ static int cuda_fail(cudaError_t e) {
 static int device_info(DeviceInfo** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return RVQ_ERR_UNAVAILABLE; }
+    if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return RVQ_ERR_UNAVAILABLE; }
     if (dev < 0 || dev >= kMaxDevices) return RVQ_ERR_UNAVAILABLE;
     DeviceInfo& di = g_devices[dev];
     std::lock_guard<std::mutex> lock(g_dev_mutex);
@@ -413,7 +412,7 @@ static int device_info(DeviceInfo** out) {
         cudaDeviceProp prop;
         e = cudaGetDeviceProperties(&prop, dev);
         if (e != cudaSuccess || prop.major != 10) {
-            if (e != cudaSuccess) t_last_cuda_error = (int)e;
+            if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
             di.ok = false;
         } else {
             di.sm_count = prop.multiProcessorCount;
@@ -425,7 +424,7 @@ static int device_info(DeviceInfo** out) {
                 e = cudaFuncSetAttribute(rvq_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          di.max_smem);
             di.ok = (e == cudaSuccess);
-            if (e != cudaSuccess) t_last_cuda_error = (int)e;
+            if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
         }
     }
     if (!di.ok) return RVQ_ERR_UNAVAILABLE;
@@ -635,15 +634,15 @@ int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* co
 int rvq_take_index_error(void) {
     unsigned int v = 0, zero = 0;
     cudaError_t e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return -RVQ_ERR_CUDA; }
+    if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return -RVQ_ERR_CUDA; }
     e = cudaMemcpyFromSymbol(&v, g_index_error, sizeof(v));
-    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return -RVQ_ERR_CUDA; }
+    if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return -RVQ_ERR_CUDA; }
     e = cudaMemcpyToSymbol(g_index_error, &zero, sizeof(zero));
-    if (e != cudaSuccess) { t_last_cuda_error = (int)e; return -RVQ_ERR_CUDA; }
+    if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return -RVQ_ERR_CUDA; }
     return v ? 1 : 0;
 }
 
-int rvq_last_cuda_error(void) { return t_last_cuda_error; }
+int rvq_last_cuda_error(void) { return last_cuda_error_slot(); }
 
 const char* rvq_status_string(int status) {
     switch (status) {

@@ -1,0 +1,116 @@
+"""Fused RVQ dequant-GEMV (batch 1) from Python.
+
+``GemvPlan`` binds up to 16 (entry, codebook, x, y) products -- e.g. the q, k
+and v projections of a layer that share x -- to one ``rvq_gemv`` launch
+(include/rvq_b200.h), with the C descriptors and the zero-filled workspace
+built once and reused.  ``rvq_linear`` is the one-shot form.
+
+The reference has no fused path: it reconstructs each weight into a slot and
+calls ``F.linear`` (infer_compressed_layerwise_triton.py:290-292, 296-297).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _native
+
+
+class RvqGemvJob(ctypes.Structure):
+    _fields_ = [
+        ("weight", _native.RvqEntry),
+        ("x", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("x_kind", ctypes.c_int32),
+        ("y_kind", ctypes.c_int32),
+    ]
+
+
+_bound = False
+
+
+def _lib():
+    global _bound
+    lib = _native.load()
+    if not _bound:
+        lib.rvq_gemv_workspace_size.restype = ctypes.c_size_t
+        lib.rvq_gemv_workspace_size.argtypes = [ctypes.POINTER(RvqGemvJob), ctypes.c_int]
+        lib.rvq_gemv.restype = ctypes.c_int
+        lib.rvq_gemv.argtypes = [ctypes.POINTER(RvqGemvJob), ctypes.c_int, ctypes.c_void_p,
+                                 ctypes.c_size_t, ctypes.c_void_p]
+        _bound = True
+    return lib
+
+
+def gemv_supported(entry: Dict[str, object]) -> bool:
+    """Whether ``rvq_gemv`` takes this entry (K=4, 256 codes, uint8 codes,
+    no tail, d=8, columns a multiple of 32 -- code words are read 4 groups at
+    a time)."""
+    idx = entry["indices"]
+    shape = entry["shape"]
+    return (entry["method"] in ("rvq_groupwise", "rvq_mlp") and int(entry["d"]) == 8
+            and len(shape) == 2 and int(shape[1]) % 32 == 0 and idx.dtype == torch.uint8
+            and int(idx.shape[0]) == 4 and entry["tail"].numel() == 0
+            and int(entry["trimmed_numel"]) == int(shape[0]) * int(shape[1]))
+
+
+class GemvPlan:
+    """One launch computing ``y_i = W_i x_i`` for every bound product."""
+
+    def __init__(self, products: Sequence[Tuple[Dict[str, object], torch.Tensor, torch.Tensor, torch.Tensor]]):
+        if not 1 <= len(products) <= 16:
+            raise ValueError("a GEMV launch takes 1 to 16 products")
+        self._keep: list = []
+        jobs: List[RvqGemvJob] = []
+        device = None
+        for entry, codebook, x, y in products:
+            if not gemv_supported(entry):
+                raise NotImplementedError(f"rvq_gemv does not take entry of shape {entry['shape']}")
+            rows, cols = int(entry["shape"][0]), int(entry["shape"][1])
+            if x.numel() != cols or y.numel() != rows or not x.is_contiguous() or not y.is_contiguous():
+                raise ValueError("x must have cols elements and y rows elements, both contiguous")
+            if codebook.dtype not in (torch.float16, torch.float32):
+                codebook = codebook.to(torch.float32)
+            if not codebook.is_contiguous() or codebook.data_ptr() % 16:
+                codebook = codebook.contiguous().clone()
+            scales = entry["scales"] if entry["scales"].is_contiguous() else entry["scales"].contiguous()
+            indices = entry["indices"] if entry["indices"].is_contiguous() else entry["indices"].contiguous()
+            self._keep.append((codebook, scales, indices, x, y))
+            w = _native.make_entry(indices, codebook, scales, None, y.view(-1), d=8,
+                                   group_size=int(entry["group_size"]),
+                                   trimmed=int(entry["trimmed_numel"]))
+            jobs.append(RvqGemvJob(w, x.data_ptr(), y.data_ptr(), rows, cols,
+                                   _native.kind_of(x), _native.kind_of(y)))
+            device = y.device
+        self.device = device
+        self.jobs = (RvqGemvJob * len(jobs))(*jobs)
+        self.n = len(jobs)
+        lib = _lib()
+        with torch.cuda.device(device):
+            nbytes = int(lib.rvq_gemv_workspace_size(self.jobs, self.n))
+        self.workspace = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        self.workspace_bytes = nbytes
+
+    def launch(self, stream: Optional[int] = None) -> None:
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = _lib().rvq_gemv(self.jobs, self.n, ctypes.c_void_p(self.workspace.data_ptr()),
+                             self.workspace_bytes, ctypes.c_void_p(stream))
+        if rc:
+            _native.check(rc, "rvq_gemv")
+
+
+def rvq_linear(x: torch.Tensor, entry: Dict[str, object], codebook: torch.Tensor,
+               out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """``F.linear(x, W)`` for one token (x of ``cols`` elements) with W the
+    RVQ entry, without materialising W."""
+    rows = int(entry["shape"][0])
+    if out is None:
+        out = torch.empty(rows, dtype=out_dtype or x.dtype, device=x.device)
+    GemvPlan([(entry, codebook, x.reshape(-1).contiguous(), out)]).launch()
+    return out
