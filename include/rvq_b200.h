@@ -115,7 +115,7 @@ int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* co
  * reference, which reconstructs W into the slot and then calls F.linear:
  * infer_compressed_layerwise_triton.py:290-292 / lines 296-297).  W is an
  * RVQ entry with K=4 stages, 256 codes, uint8 codes, no tail; `rows` x `cols`
- * is its shape (cols a multiple of 32, code planes 4-byte aligned).  The product is computed through
+ * is its shape (cols a multiple of 8).  The product is computed through
  * per-stage lookup tables of codeword . x dot products, i.e. W is never
  * materialised and never rounded to bf16: results match "reconstruct, round
  * to bf16, matmul" to within the bf16 rounding of W (about 1e-3 relative). */
@@ -127,19 +127,28 @@ typedef struct rvq_gemv_job {
     int64_t cols;
     int32_t x_kind;           /* RVQ_BF16, RVQ_F16 or RVQ_F32 */
     int32_t y_kind;           /* RVQ_BF16, RVQ_F16 or RVQ_F32 */
+    int32_t codes_interleaved;/* 0: weight.indices are the artifact's planes [4][stage_stride];
+                                 1: [nvec][4] bytes as written by rvq_interleave_codes */
+    int32_t reserved;
 } rvq_gemv_job;
 
-/* Bytes of device workspace rvq_gemv needs for these jobs (per-tile row
- * partials and row-range tickets).  The workspace must be zero-filled once
+/* Bytes of device workspace rvq_gemv needs for these jobs (lookup tables,
+ * per-tile row partials and row-range tickets).  The workspace must be zero-filled once
  * when it is allocated; every launch leaves its tickets at zero again.
  * Launches that share a workspace must not overlap on the GPU. */
 size_t rvq_gemv_workspace_size(const rvq_gemv_job* jobs, int n_jobs);
 
-/* Up to 16 GEMVs (e.g. q, k and v of one layer, sharing x) in one launch.
+/* Up to 4 GEMVs (e.g. q, k and v of one layer, sharing x) in one launch.
  * Deterministic: partial sums over 256-column tiles are added in tile order.
  * `workspace` is 256-byte aligned device memory of at least
  * rvq_gemv_workspace_size() bytes. */
 int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Repack uint8 code planes [4][stage_stride] into one 32-bit word per vector
+ * ([nvec][4] bytes, stage k in byte k), the layout rvq_gemv reads with one
+ * load per vector (codes_interleaved = 1).  `out` holds nvec * 4 bytes,
+ * 4-byte aligned.  A layout of this library, not of the reference artifact. */
+int rvq_interleave_codes(const void* planes, int64_t stage_stride, int64_t nvec, void* out, void* stream);
 
 /* Reads and clears the sticky device flag that kernels set when an index is
  * outside [0, ncodes) (the decoded element then uses code 0).  Synchronises

@@ -2,8 +2,10 @@
 
     python -m rvq_b200.bench_linear [--reps 200]
 
-Times, with CUDA events on one stream and weights rotated over 16 resident
-copies (so no copy's codes stay in L2 between uses):
+Times device work per call -- each measured loop is captured in a CUDA graph
+and the replay timed with CUDA events, so host launch cost is excluded --
+with weights rotated over 16 resident copies (no copy's codes stay in L2
+between uses):
 
 * ``fused``:  rvq_gemv (batch 1), W never materialised;
 * ``decode+gemm``: rvq_decode_layer into a bf16 slot, then torch.matmul
@@ -23,21 +25,29 @@ import torch
 
 from . import synthetic
 from .engine import LayerDecodePlan
-from .gemv import GemvPlan
+from .gemv import GemvPlan, interleave_codes
 
 ROWS, COLS = 9728, 2560
 COPIES = 16
 
 
 def _time(fn, reps, stream):
+    """Device time per call: ``reps`` calls captured in one CUDA graph,
+    replayed after a warm-up replay, timed with events (no host launch cost
+    in the measurement)."""
     for i in range(3):
         fn(i)
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(reps):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record(stream)
-    for i in range(reps):
-        fn(i)
-    e.record(stream)
+    s.record()
+    graph.replay()
+    e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / reps * 1e3      # us
 
@@ -58,11 +68,16 @@ def run(reps: int = 200, device="cuda:0"):
     # fused GEMV, batch 1
     x1 = torch.randn(COLS, generator=g).to(device, torch.bfloat16)
     ys = [torch.empty(ROWS, dtype=torch.bfloat16, device=device) for _ in range(COPIES)]
-    plans = [GemvPlan([(c, cbd, x1, y)]) for c, y in zip(copies, ys)]
-    t = _time(lambda i: plans[i % COPIES].launch(stream.cuda_stream), reps, stream)
     algo = code_bytes + COLS * 2 + ROWS * 2
+    plans = [GemvPlan([(c, cbd, x1, y)]) for c, y in zip(copies, ys)]
+    t = _time(lambda i: plans[i % COPIES].launch(), reps, stream)
+    out["results"]["fused_b1_planes"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
+                                         "algorithmic_bytes": algo}
+    il = [dict(c, codes_il=interleave_codes(c["indices"])) for c in copies]
+    plans = [GemvPlan([(c, cbd, x1, y)]) for c, y in zip(il, ys)]
+    t = _time(lambda i: plans[i % COPIES].launch(), reps, stream)
     out["results"]["fused_b1"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
-                                  "algorithmic_bytes": algo}
+                                  "algorithmic_bytes": algo, "codes": "interleaved"}
 
     # decode + GEMM (slot then cuBLAS), and dense
     slot = torch.empty(ROWS, COLS, dtype=torch.bfloat16, device=device)
@@ -71,17 +86,20 @@ def run(reps: int = 200, device="cuda:0"):
     for i in range(COPIES):
         dplans[i].launch(stream.cuda_stream)
         dense.append(slot.clone())
-    t_dec = _time(lambda i: dplans[i % COPIES].launch(stream.cuda_stream), reps, stream)
+    t_dec = _time(lambda i: dplans[i % COPIES].launch(), reps, stream)
     out["results"]["decode_only"] = {"us": round(t_dec, 2)}
     for b in (1, 8, 64, 2048):
         x = torch.randn(b, COLS, generator=g).to(device, torch.bfloat16)
 
-        def dec_gemm(i, x=x):
-            dplans[i % COPIES].launch(stream.cuda_stream)
-            torch.matmul(x, slot.t())
+        y_dg = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)
+        y_dn = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)
 
-        def dense_mm(i, x=x):
-            torch.matmul(x, dense[i % COPIES].t())
+        def dec_gemm(i, x=x, y=y_dg):
+            dplans[i % COPIES].launch()
+            torch.matmul(x, slot.t(), out=y)
+
+        def dense_mm(i, x=x, y=y_dn):
+            torch.matmul(x, dense[i % COPIES].t(), out=y)
 
         r = reps if b < 2048 else max(20, reps // 10)
         t_dg = _time(dec_gemm, r, stream)

@@ -2,10 +2,9 @@
 // materialising W.
 //
 // W is an RVQ entry (K=4 stages x 256 codes, d=8, uint8 codes; any scale
-// grouping).  Per column group j (8 columns) and stage k the kernel builds a
-// lookup table LUT_k[c][j] = dot(cb_k[c], x[8j .. 8j+8]) in shared memory, so
-// an 8-weight vector costs 4 table lookups and 3 adds instead of 32 codebook
-// element reconstructions:
+// grouping).  For column group j (8 columns) and stage k, a lookup table
+// LUT_k[c][j] = dot(cb_k[c], x[8j .. 8j+8]) turns every 8-weight vector into
+// 4 table lookups and 3 adds instead of 32 element reconstructions:
 //
 //   y[r] = sum_j  scale(r, j) * (((LUT_0[c0] + LUT_1[c1]) + LUT_2[c2]) + LUT_3[c3])
 //
@@ -14,13 +13,19 @@
 // rounding of each weight (relative 2^-9 per weight), which is why this path
 // is compared against the reference reconstruct + matmul with a tolerance.
 //
-// Work split: column tiles of 32 groups (256 columns) x row ranges.  A CTA
-// builds the 128 KB table of its tile (lane j of every warp owns group j, so
-// table reads are conflict-free), then each warp takes rows, reads the 4 code
-// bytes of its lane's group (32 consecutive bytes per plane per warp) and
-// reduces the row over the 32 lanes with shuffles.  Per-tile row partials go
-// to a workspace; the last CTA of a row range (atomic ticket) sums the tiles
-// in tile order, so results are deterministic run to run.
+// Two launches per call:
+// 1. rvq_lut_kernel builds every 256-column tile's table once ([4][256][32]
+//    fp32 = 128 KB per tile) into the workspace: thread (code c, group g)
+//    forms dot(cb[k][c], x of group g), so a warp writes 128 contiguous bytes.
+// 2. rvq_gemv_kernel: CTA (tile, row range) copies its tile's table into
+//    shared memory, then each warp walks 8 rows at a time.  Lane g owns column
+//    group g of the tile: the codes of (row, group) come as one 32-bit word when
+//    the codes are interleaved ([nvec][4], see rvq_interleave_codes), 4 bytes
+//    from the 4 planes otherwise; table reads are conflict-free (lane g reads
+//    bank g).  The 8 rows are reduced over the 32 lanes with a transpose
+//    reduction (9 shuffles); per-tile row partials go to the workspace and the
+//    last CTA of a row range (atomic ticket) sums the tiles in tile order, so
+//    results are deterministic run to run.
 
 #include <string.h>
 
@@ -33,32 +38,34 @@ namespace gemv {
 
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
+constexpr int kLutThreads = 256;
 constexpr int kGroupsPerTile = 32;               // 256 columns per tile
 constexpr int kStages = 4;
 constexpr int kCodes = 256;
 constexpr int kRowBatch = 8;                     // rows a warp decodes and reduces together
-constexpr int kMaxJobs = 16;
+constexpr int kMaxJobs = 4;                       // q/k/v or gate/up share one launch
 constexpr size_t kLutBytes = (size_t)kStages * kCodes * kGroupsPerTile * sizeof(float);   // 128 KB
-constexpr size_t kCbBytes = (size_t)kStages * kCodes * 8 * sizeof(float);                  // 32 KB
-constexpr size_t kSmemBytes = kLutBytes + kCbBytes;                                        // 160 KB
 
 struct Job {
-    const uint8_t* idx;        // [4][stage_stride] codes
+    const uint8_t* idx;        // planar [4][stage_stride] or interleaved [nvec][4] codes
     const void* cb;            // [4][256][8] fp16 or fp32
     const void* scales;        // scale per group_vecs vectors
     const void* x;             // [cols]
     void* y;                   // [rows]
     float* partial;            // [ntiles][rows] workspace
     unsigned int* tickets;     // [nranges] workspace, zero between launches
+    float* lut;                // [ntiles][4][256][32] workspace
     uint32_t rows;
     uint32_t groups;           // cols / 8
     uint32_t stage_stride;
     FastDiv gv;                // group_vecs
     uint32_t ntiles;           // ceil(groups / 32)
     uint32_t nranges;          // row ranges per tile
-    uint32_t cta_begin;        // first CTA of this job
+    uint32_t cta_begin;        // first CTA of this job (product launch)
+    uint32_t lut_cta_begin;    // first CTA of this job (table launch)
     uint8_t cb_kind, scale_kind, x_kind, y_kind;
     uint8_t row_scales;        // one scale per row: applied once, after the tile sum
+    uint8_t interleaved;       // codes are [nvec][4]
 };
 
 struct Params {
@@ -72,116 +79,107 @@ __device__ __forceinline__ float ldf(const void* p, uint32_t i, int kind) {
     return __ldg(reinterpret_cast<const float*>(p) + i);
 }
 
-// d += a * b on two fp32 lanes at once (sm_100 packed fp32 FMA).
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-    asm("{.reg .b64 ra, rb, rd; mov.b64 ra, {%2,%3}; mov.b64 rb, {%4,%5}; mov.b64 rd, {%0,%1};"
-        " fma.rn.f32x2 rd, ra, rb, rd; mov.b64 {%0,%1}, rd;}"
-        : "+f"(d0), "+f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
+// ---------------------------------------------------------------------------
+// 1. tables
+// ---------------------------------------------------------------------------
 
-// Code words of 4 consecutive rows, one plane: lanes 8q..8q+7 read row rb+q,
-// lane L reads groups 4(L%8)..4(L%8)+3 of the tile (a 32-byte row segment per
-// 8 lanes).  `valid` masks rows past the range and groups past the matrix.
-__device__ __forceinline__ uint32_t load_quad(const Job& job, int k, uint32_t rb, uint32_t r1, uint32_t g0,
-                                              int lane) {
-    const uint32_t row = rb + (lane >> 3);
-    const uint32_t grp = g0 + 4 * (lane & 7);
-    if (row >= r1 || grp >= job.groups) return 0u;
-    const uint8_t* src = job.idx + (size_t)k * job.stage_stride + (size_t)row * job.groups + grp;
-    return __ldg(reinterpret_cast<const uint32_t*>(src));
-}
-
-__global__ void __launch_bounds__(kThreads, 1) rvq_gemv_kernel(const __grid_constant__ Params p) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    float* lut = reinterpret_cast<float*>(smem);                         // [4][256][32]
-    float* cbs = reinterpret_cast<float*>(smem + kLutBytes);             // [4][256][8]
-    __shared__ int s_last;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// CTA (job, tile, stage): LUT[stage][c][g] for 256 codes x 32 groups.
+__global__ void __launch_bounds__(kLutThreads) rvq_lut_kernel(const __grid_constant__ Params p) {
+    __shared__ float xs[kGroupsPerTile * 8];
+    __shared__ float4 cw[kCodes * 2];
     int ji = 0;
-    while (ji + 1 < p.njobs && blockIdx.x >= p.jobs[ji + 1].cta_begin) ++ji;
+    while (ji + 1 < p.njobs && blockIdx.x >= p.jobs[ji + 1].lut_cta_begin) ++ji;
     const Job& job = p.jobs[ji];
-    const uint32_t local = blockIdx.x - job.cta_begin;
-    const uint32_t tile = local / job.nranges, range = local % job.nranges;
+    const uint32_t local = blockIdx.x - job.lut_cta_begin;
+    const uint32_t tile = local / kStages, k = local % kStages;
     const uint32_t g0 = tile * kGroupsPerTile;
-    const uint32_t j = g0 + lane;                       // this lane's column group
-    const bool active = j < job.groups;
-    const uint32_t r0 = (uint32_t)(((uint64_t)job.rows * range) / job.nranges);
-    const uint32_t r1 = (uint32_t)(((uint64_t)job.rows * (range + 1)) / job.nranges);
-
-    // ---- codebook (fp32) and this lane's 8 activations first ----
-    for (int e = threadIdx.x; e < kStages * kCodes * 2; e += kThreads) {
+    // activations of the tile's 32 groups (zero past the matrix) and stage k's codebook
+    {
+        const uint32_t col = g0 * 8 + threadIdx.x;
+        xs[threadIdx.x] = col < job.groups * 8 ? ldf(job.x, col, job.x_kind) : 0.0f;
+    }
+    for (int e = threadIdx.x; e < kCodes * 2; e += kLutThreads) {
         float4 v;
         if (job.cb_kind == RVQ_F32) {
-            v = __ldg(reinterpret_cast<const float4*>(job.cb) + e);
+            v = __ldg(reinterpret_cast<const float4*>(job.cb) + (size_t)k * kCodes * 2 + e);
         } else {
-            const uint2 h = __ldg(reinterpret_cast<const uint2*>(job.cb) + e);
+            const uint2 h = __ldg(reinterpret_cast<const uint2*>(job.cb) + (size_t)k * kCodes * 2 + e);
             v.x = __half2float(__ushort_as_half((uint16_t)(h.x & 0xFFFFu)));
             v.y = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
             v.z = __half2float(__ushort_as_half((uint16_t)(h.y & 0xFFFFu)));
             v.w = __half2float(__ushort_as_half((uint16_t)(h.y >> 16)));
         }
-        reinterpret_cast<float4*>(cbs)[e] = v;
+        cw[e] = v;
     }
-    float xs[8];
+    __syncthreads();
+    const int g = threadIdx.x & 31, w = threadIdx.x >> 5;
+    float xg[8];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) xs[t] = active ? ldf(job.x, j * 8 + t, job.x_kind) : 0.0f;
+    for (int t = 0; t < 8; ++t) xg[t] = xs[g * 8 + t];
+    float* out = job.lut + ((size_t)tile * kStages + k) * kCodes * kGroupsPerTile;
+#pragma unroll 4
+    for (int c = w; c < kCodes; c += kLutThreads / 32) {
+        const float4 a = cw[2 * c], b = cw[2 * c + 1];
+        float d = a.x * xg[0];
+        d = fmaf(a.y, xg[1], d);
+        d = fmaf(a.z, xg[2], d);
+        d = fmaf(a.w, xg[3], d);
+        d = fmaf(b.x, xg[4], d);
+        d = fmaf(b.y, xg[5], d);
+        d = fmaf(b.z, xg[6], d);
+        d = fmaf(b.w, xg[7], d);
+        out[c * kGroupsPerTile + g] = d;
+    }
+}
 
-    // first batch of code words in flight while the table is built
-    uint32_t rb = r0 + warp * kRowBatch;
-    uint32_t w[kStages][2];
+// ---------------------------------------------------------------------------
+// 2. the product
+// ---------------------------------------------------------------------------
+
+// Codes of (row, this lane's group), one stage per byte.
+__device__ __forceinline__ uint32_t load_codes(const Job& job, uint32_t row, uint32_t r1, uint32_t j, bool active) {
+    if (!active || row >= r1) return 0u;
+    const size_t n = (size_t)row * job.groups + j;
+    if (job.interleaved) return __ldg(reinterpret_cast<const uint32_t*>(job.idx) + n);
+    const uint8_t* s = job.idx + n;
+    return (uint32_t)__ldg(s) | ((uint32_t)__ldg(s + job.stage_stride) << 8) |
+           ((uint32_t)__ldg(s + 2 * (size_t)job.stage_stride) << 16) |
+           ((uint32_t)__ldg(s + 3 * (size_t)job.stage_stride) << 24);
+}
+
+// The product for job J; J is a compile-time slot so the job's fields are
+// read straight from the parameter bank instead of occupying registers.
+template <int J>
+__device__ __forceinline__ void gemv_job(const Params& p, float* lut, int* s_last_ptr) {
+    int& s_last = *s_last_ptr;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const Job& job = p.jobs[J];
+    const uint32_t local = blockIdx.x - job.cta_begin;
+    const uint32_t tile = local / job.nranges, range = local % job.nranges;
+    const uint32_t j = tile * kGroupsPerTile + lane;    // this lane's column group
+    const bool active = j < job.groups;
+    const uint32_t r0 = (uint32_t)(((uint64_t)job.rows * range) / job.nranges);
+    const uint32_t r1 = (uint32_t)(((uint64_t)job.rows * (range + 1)) / job.nranges);
+
+    // the tile's table into shared memory
+    {
+        const float4* src = reinterpret_cast<const float4*>(job.lut + (size_t)tile * kStages * kCodes * kGroupsPerTile);
+        float4* dst = reinterpret_cast<float4*>(lut);
+        constexpr int kPer = (int)(kLutBytes / 16) / kThreads;          // 8 float4 per thread
+        float4 v[kPer];
 #pragma unroll
-    for (int k = 0; k < kStages; ++k) {
-        w[k][0] = load_quad(job, k, rb, r1, g0, lane);
-        w[k][1] = load_quad(job, k, rb + 4, r1, g0, lane);
+        for (int i = 0; i < kPer; ++i) v[i] = __ldcg(src + threadIdx.x + i * kThreads);
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) dst[threadIdx.x + i * kThreads] = v[i];
     }
     __syncthreads();
 
-    // ---- table of this tile: LUT[k][c][lane] = dot(cb[k][c], x[8j..8j+8]) ----
-    for (int e = warp; e < kStages * kCodes; e += 2 * kWarps) {
-        const float4* c0 = reinterpret_cast<const float4*>(cbs) + 2 * e;
-        const float4* c1 = c0 + 2 * kWarps;
-        const float4 a0 = c0[0], b0 = c0[1], a1 = c1[0], b1 = c1[1];
-        float d0 = 0.0f, d0b = 0.0f, d1 = 0.0f, d1b = 0.0f;
-        fma2(d0, d0b, a0.x, a0.y, xs[0], xs[1]);
-        fma2(d1, d1b, a1.x, a1.y, xs[0], xs[1]);
-        fma2(d0, d0b, a0.z, a0.w, xs[2], xs[3]);
-        fma2(d1, d1b, a1.z, a1.w, xs[2], xs[3]);
-        fma2(d0, d0b, b0.x, b0.y, xs[4], xs[5]);
-        fma2(d1, d1b, b1.x, b1.y, xs[4], xs[5]);
-        fma2(d0, d0b, b0.z, b0.w, xs[6], xs[7]);
-        fma2(d1, d1b, b1.z, b1.w, xs[6], xs[7]);
-        lut[e * kGroupsPerTile + lane] = d0 + d0b;
-        lut[(e + kWarps) * kGroupsPerTile + lane] = d1 + d1b;
-    }
-    __syncthreads();                                    // table ready
-
-    // ---- rows: 8 per warp per step, next step's code words prefetched ----
     const uint32_t G = job.groups;
     float* part = job.partial + (size_t)tile * job.rows;
-    const uint32_t bsel = 0x4440u | (lane & 3);
+    const float* lut_lane = lut + lane;
     bool wrote = false;
-    for (; rb < r1; rb += kWarps * kRowBatch) {
-        uint32_t wn[kStages][2];
-        const uint32_t nb = rb + kWarps * kRowBatch;
-#pragma unroll
-        for (int k = 0; k < kStages; ++k) {
-            wn[k][0] = load_quad(job, k, nb, r1, g0, lane);
-            wn[k][1] = load_quad(job, k, nb + 4, r1, g0, lane);
-        }
-        float v[kRowBatch];
-#pragma unroll
-        for (int i = 0; i < kRowBatch; ++i) {
-            const int src = (i & 3) * 8 + (lane >> 2);  // lane holding this row's word for my group
-            float a = lut[(0 * kCodes + __byte_perm(__shfl_sync(0xffffffffu, w[0][i >> 2], src), 0, bsel)) * kGroupsPerTile + lane];
-            a += lut[(1 * kCodes + __byte_perm(__shfl_sync(0xffffffffu, w[1][i >> 2], src), 0, bsel)) * kGroupsPerTile + lane];
-            a += lut[(2 * kCodes + __byte_perm(__shfl_sync(0xffffffffu, w[2][i >> 2], src), 0, bsel)) * kGroupsPerTile + lane];
-            a += lut[(3 * kCodes + __byte_perm(__shfl_sync(0xffffffffu, w[3][i >> 2], src), 0, bsel)) * kGroupsPerTile + lane];
-            const uint32_t row = rb + i;
-            if (!job.row_scales)
-                a *= (active && row < r1) ? ldf(job.scales, fastdiv(row * G + j, job.gv), job.scale_kind) : 0.0f;
-            v[i] = (active && row < r1) ? a : 0.0f;
-        }
-        // transpose-reduce 8 rows over 32 lanes: lanes 4m..4m+3 end with row m
+    // Lane sums of 8 rows -> row (rb + lane/4 % 8) complete in lanes 4m..4m+3.
+    auto reduce8 = [&](float (&v)[kRowBatch]) -> float {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const bool up = lane & 16;
@@ -194,22 +192,80 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_kernel(const __grid_cons
             const float send = up ? v[i] : v[i + 2], keep = up ? v[i + 2] : v[i];
             v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
         }
-        {
-            const bool up = lane & 4;
-            const float send = up ? v[0] : v[1], keep = up ? v[1] : v[0];
-            v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        const bool up = lane & 4;
+        const float send = up ? v[0] : v[1], keep = up ? v[1] : v[0];
+        float r = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        r += __shfl_xor_sync(0xffffffffu, r, 2);
+        r += __shfl_xor_sync(0xffffffffu, r, 1);
+        return r;
+    };
+    // ((LUT_0[c0] + LUT_1[c1]) + LUT_2[c2]) + LUT_3[c3] for one code word
+    auto lookup = [&](uint32_t cw) -> float {
+        float a = lut_lane[(cw & 0xFFu) * kGroupsPerTile];
+        a += lut_lane[((cw >> 8) & 0xFFu) * kGroupsPerTile + 1 * kCodes * kGroupsPerTile];
+        a += lut_lane[((cw >> 16) & 0xFFu) * kGroupsPerTile + 2 * kCodes * kGroupsPerTile];
+        a += lut_lane[(cw >> 24) * kGroupsPerTile + 3 * kCodes * kGroupsPerTile];
+        return a;
+    };
+
+    const uint32_t step = kWarps * kRowBatch;
+    uint32_t rb = r0 + warp * kRowBatch;
+    // warp-uniform: every lane of a full tile has a live column
+    const bool fast = job.interleaved && job.row_scales && (tile + 1) * kGroupsPerTile <= job.groups;
+    if (fast) {
+        // interleaved codes, one scale per row, a full tile: full batches
+        // need no masks; the lane's code word of row r is codes[r * G]
+        const uint32_t* codes = reinterpret_cast<const uint32_t*>(job.idx) + j;
+        const uint32_t full_end = r1 >= kRowBatch ? r1 - kRowBatch + 1 : 0;     // rb < full_end: 8 rows in range
+        uint32_t wa[kRowBatch];
+        if (rb < full_end) {
+#pragma unroll
+            for (int i = 0; i < kRowBatch; ++i) wa[i] = __ldg(codes + (size_t)(rb + i) * G);
         }
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
-        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+        while (rb < full_end) {
+            const uint32_t nb = rb + step;
+            uint32_t wb[kRowBatch];
+            if (nb < full_end) {
+#pragma unroll
+                for (int i = 0; i < kRowBatch; ++i) wb[i] = __ldg(codes + (size_t)(nb + i) * G);
+            }
+            float v[kRowBatch];
+#pragma unroll
+            for (int i = 0; i < kRowBatch; ++i) v[i] = lookup(wa[i]);
+            const float r = reduce8(v);
+            if ((lane & 3) == 0) part[rb + ((lane >> 2) & 7)] = r;
+            wrote = true;
+            rb = nb;
+            if (rb >= full_end) break;
+            const uint32_t nb2 = rb + step;
+            if (nb2 < full_end) {
+#pragma unroll
+                for (int i = 0; i < kRowBatch; ++i) wa[i] = __ldg(codes + (size_t)(nb2 + i) * G);
+            }
+#pragma unroll
+            for (int i = 0; i < kRowBatch; ++i) v[i] = lookup(wb[i]);
+            const float r2 = reduce8(v);
+            if ((lane & 3) == 0) part[rb + ((lane >> 2) & 7)] = r2;
+            rb = nb2;
+        }
+    }
+    // general rows (and the last partial batch of the fast path): masked
+    for (; rb < r1; rb += step) {
+        float v[kRowBatch];
+#pragma unroll
+        for (int i = 0; i < kRowBatch; ++i) {
+            const uint32_t row = rb + i;
+            const uint32_t cw = load_codes(job, row, r1, j, active);
+            float a = lookup(cw);
+            if (!job.row_scales)
+                a *= (active && row < r1) ? ldf(job.scales, fastdiv(row * G + j, job.gv), job.scale_kind) : 0.0f;
+            v[i] = (active && row < r1) ? a : 0.0f;
+        }
+        const float r = reduce8(v);
         const uint32_t row = rb + ((lane >> 2) & 7);
         if ((lane & 3) == 0 && row < r1) {
-            part[row] = v[0];
+            part[row] = r;
             wrote = true;
-        }
-#pragma unroll
-        for (int k = 0; k < kStages; ++k) {
-            w[k][0] = wn[k][0];
-            w[k][1] = wn[k][1];
         }
     }
 
@@ -230,6 +286,28 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_kernel(const __grid_cons
         store_from_f32(job.y, r, job.y_kind, acc);
     }
     if (threadIdx.x == 0) job.tickets[range] = 0u;      // ready for the next launch
+}
+
+__global__ void __launch_bounds__(kThreads, 1) rvq_gemv_kernel(const __grid_constant__ Params p) {
+    extern __shared__ __align__(16) float lut[];                         // [4][256][32]
+    __shared__ int s_last;
+    int ji = 0;
+    while (ji + 1 < p.njobs && blockIdx.x >= p.jobs[ji + 1].cta_begin) ++ji;
+    switch (ji) {
+        case 0: gemv_job<0>(p, lut, &s_last); break;
+        case 1: gemv_job<1>(p, lut, &s_last); break;
+        case 2: gemv_job<2>(p, lut, &s_last); break;
+        default: gemv_job<3>(p, lut, &s_last); break;
+    }
+}
+
+// codes[n] = planes[0][n] | planes[1][n] << 8 | planes[2][n] << 16 | planes[3][n] << 24
+__global__ void rvq_interleave_kernel(const uint8_t* planes, uint64_t stage_stride, uint64_t nvec, uint32_t* out) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t n = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; n < nvec; n += stride) {
+        out[n] = (uint32_t)planes[n] | ((uint32_t)planes[n + stage_stride] << 8) |
+                 ((uint32_t)planes[n + 2 * stage_stride] << 16) | ((uint32_t)planes[n + 3 * stage_stride] << 24);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -255,7 +333,7 @@ static int dev_info(DevInfo** out) {
         e = cudaGetDeviceProperties(&prop, dev);
         if (e == cudaSuccess && prop.major == 10) {
             d.sms = prop.multiProcessorCount;
-            e = cudaFuncSetAttribute(rvq_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+            e = cudaFuncSetAttribute(rvq_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLutBytes);
             d.ok = e == cudaSuccess;
         }
         if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
@@ -274,8 +352,7 @@ static int check_job(const rvq_gemv_job* g) {
     if (w.stages != kStages || w.ncodes != kCodes || w.index_kind != RVQ_U8) return RVQ_ERR_UNSUPPORTED;
     if (g->rows < 1 || g->cols < 8 || g->cols % 8) return RVQ_ERR_UNSUPPORTED;
     if (g->rows * g->cols / 8 != w.nvec || w.trimmed != w.nvec * 8 || w.tail_numel != 0) return RVQ_ERR_UNSUPPORTED;
-    // code words are read 4 bytes at a time: 4-byte aligned planes and rows
-    if ((g->cols / 8) % 4 || w.stage_stride % 4 || ((uintptr_t)w.indices & 3)) return RVQ_ERR_UNSUPPORTED;
+    if (g->codes_interleaved && ((uintptr_t)w.indices & 3)) return RVQ_ERR_INVALID;
     if (g->rows >= (1ll << 31) || g->cols / 8 >= (1ll << 24)) return RVQ_ERR_TOO_LARGE;
     if (!g->x || !g->y) return RVQ_ERR_INVALID;
     if (g->x_kind != RVQ_BF16 && g->x_kind != RVQ_F16 && g->x_kind != RVQ_F32) return RVQ_ERR_UNSUPPORTED;
@@ -283,17 +360,15 @@ static int check_job(const rvq_gemv_job* g) {
     return RVQ_OK;
 }
 
-// CTAs per job: tiles x row ranges.  One CTA fits per SM (192 KB of shared
+// CTAs per job: tiles x row ranges.  One CTA fits per SM (128 KB of shared
 // memory), so the launch is kept to one wave: every job gets row ranges in
-// proportion to its vectors, rounded down, at least one, and the total never
-// exceeds the SM count unless the tiles alone do.
+// proportion to its vectors, rounded down, at least one, and what is left of
+// the wave goes to the jobs with the most rows per CTA.
 static void plan(const rvq_gemv_job* jobs, int n, int sms, uint32_t* ntiles, uint32_t* nranges) {
     double total = 0;
-    uint32_t tiles_total = 0;
     for (int i = 0; i < n; ++i) {
         total += (double)jobs[i].rows * (jobs[i].cols / 8);
         ntiles[i] = (uint32_t)((jobs[i].cols / 8 + kGroupsPerTile - 1) / kGroupsPerTile);
-        tiles_total += ntiles[i];
     }
     uint32_t used = 0;
     for (int i = 0; i < n; ++i) {
@@ -305,7 +380,6 @@ static void plan(const rvq_gemv_job* jobs, int n, int sms, uint32_t* ntiles, uin
         nranges[i] = r;
         used += r * ntiles[i];
     }
-    // spend what is left of the wave on the jobs with the most rows per CTA
     while (used < (uint32_t)sms) {
         int best = -1;
         double worst = 0;
@@ -317,15 +391,20 @@ static void plan(const rvq_gemv_job* jobs, int n, int sms, uint32_t* ntiles, uin
         ++nranges[best];
         used += ntiles[best];
     }
-    (void)tiles_total;
 }
 
-static size_t workspace_layout(const rvq_gemv_job* jobs, int n, const uint32_t* ntiles, const uint32_t* nranges,
-                               size_t* ticket_off, size_t* partial_off) {
+struct Layout {
+    size_t tickets[kMaxJobs], partial[kMaxJobs], lut[kMaxJobs], total;
+};
+
+static Layout workspace_layout(const rvq_gemv_job* jobs, int n, const uint32_t* ntiles, const uint32_t* nranges) {
+    Layout L;
     size_t off = 0;
-    for (int i = 0; i < n; ++i) { ticket_off[i] = off; off = align256(off + nranges[i] * sizeof(unsigned int)); }
-    for (int i = 0; i < n; ++i) { partial_off[i] = off; off = align256(off + (size_t)ntiles[i] * jobs[i].rows * 4); }
-    return off;
+    for (int i = 0; i < n; ++i) { L.tickets[i] = off; off = align256(off + nranges[i] * sizeof(unsigned int)); }
+    for (int i = 0; i < n; ++i) { L.partial[i] = off; off = align256(off + (size_t)ntiles[i] * jobs[i].rows * 4); }
+    for (int i = 0; i < n; ++i) { L.lut[i] = off; off = align256(off + (size_t)ntiles[i] * kLutBytes); }
+    L.total = off;
+    return L;
 }
 
 }  // namespace gemv
@@ -341,9 +420,8 @@ size_t rvq_gemv_workspace_size(const rvq_gemv_job* jobs, int n_jobs) {
     DevInfo* d = nullptr;
     int sms = dev_info(&d) == RVQ_OK ? d->sms : 148;
     uint32_t nt[kMaxJobs], nr[kMaxJobs];
-    size_t to[kMaxJobs], po[kMaxJobs];
     plan(jobs, n_jobs, sms, nt, nr);
-    return workspace_layout(jobs, n_jobs, nt, nr, to, po);
+    return workspace_layout(jobs, n_jobs, nt, nr).total;
 }
 
 int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t workspace_bytes, void* stream) {
@@ -356,14 +434,14 @@ int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t works
     int rc = dev_info(&d);
     if (rc != RVQ_OK) return rc;
     uint32_t nt[kMaxJobs], nr[kMaxJobs];
-    size_t to[kMaxJobs], po[kMaxJobs];
     plan(jobs, n_jobs, d->sms, nt, nr);
-    const size_t need = workspace_layout(jobs, n_jobs, nt, nr, to, po);
-    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255)) return RVQ_ERR_INVALID;
+    const Layout L = workspace_layout(jobs, n_jobs, nt, nr);
+    if (!workspace || workspace_bytes < L.total || ((uintptr_t)workspace & 255)) return RVQ_ERR_INVALID;
     Params p;
     memset(&p, 0, sizeof(p));
     p.njobs = n_jobs;
-    uint32_t ctas = 0;
+    uint32_t ctas = 0, lut_ctas = 0;
+    char* ws = reinterpret_cast<char*>(workspace);
     for (int i = 0; i < n_jobs; ++i) {
         const rvq_gemv_job& g = jobs[i];
         Job& j = p.jobs[i];
@@ -372,8 +450,9 @@ int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t works
         j.scales = g.weight.scales;
         j.x = g.x;
         j.y = g.y;
-        j.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + po[i]);
-        j.tickets = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(workspace) + to[i]);
+        j.partial = reinterpret_cast<float*>(ws + L.partial[i]);
+        j.tickets = reinterpret_cast<unsigned int*>(ws + L.tickets[i]);
+        j.lut = reinterpret_cast<float*>(ws + L.lut[i]);
         j.rows = (uint32_t)g.rows;
         j.groups = (uint32_t)(g.cols / 8);
         j.stage_stride = (uint32_t)g.weight.stage_stride;
@@ -381,14 +460,33 @@ int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t works
         j.ntiles = nt[i];
         j.nranges = nr[i];
         j.cta_begin = ctas;
+        j.lut_cta_begin = lut_ctas;
         j.cb_kind = (uint8_t)g.weight.codebook_kind;
         j.scale_kind = (uint8_t)g.weight.scale_kind;
         j.x_kind = (uint8_t)g.x_kind;
         j.y_kind = (uint8_t)g.y_kind;
         j.row_scales = (uint64_t)g.weight.group_vecs == (uint64_t)(g.cols / 8);
+        j.interleaved = g.codes_interleaved ? 1 : 0;
         ctas += nt[i] * nr[i];
+        lut_ctas += nt[i] * kStages;
     }
-    rvq_gemv_kernel<<<ctas, kThreads, kSmemBytes, (cudaStream_t)stream>>>(p);
+    rvq_lut_kernel<<<lut_ctas, kLutThreads, 0, (cudaStream_t)stream>>>(p);
+    rvq_gemv_kernel<<<ctas, kThreads, kLutBytes, (cudaStream_t)stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return RVQ_ERR_CUDA; }
+    return RVQ_OK;
+}
+
+int rvq_interleave_codes(const void* planes, int64_t stage_stride, int64_t nvec, void* out, void* stream) {
+    if (!planes || !out || nvec < 0 || stage_stride < nvec || ((uintptr_t)out & 3)) return RVQ_ERR_INVALID;
+    if (nvec == 0) return RVQ_OK;
+    DevInfo* d = nullptr;
+    int rc = dev_info(&d);
+    if (rc != RVQ_OK) return rc;
+    const uint64_t blocks = ((uint64_t)nvec + 255) / 256;
+    const unsigned grid = (unsigned)(blocks < (uint64_t)d->sms * 16 ? blocks : (uint64_t)d->sms * 16);
+    rvq_interleave_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint8_t*>(planes), (uint64_t)stage_stride, (uint64_t)nvec, reinterpret_cast<uint32_t*>(out));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return RVQ_ERR_CUDA; }
     return RVQ_OK;

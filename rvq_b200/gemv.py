@@ -1,6 +1,6 @@
 """Fused RVQ dequant-GEMV (batch 1) from Python.
 
-``GemvPlan`` binds up to 16 (entry, codebook, x, y) products -- e.g. the q, k
+``GemvPlan`` binds up to 4 (entry, codebook, x, y) products -- e.g. the q, k
 and v projections of a layer that share x -- to one ``rvq_gemv`` launch
 (include/rvq_b200.h), with the C descriptors and the zero-filled workspace
 built once and reused.  ``rvq_linear`` is the one-shot form.
@@ -28,6 +28,8 @@ class RvqGemvJob(ctypes.Structure):
         ("cols", ctypes.c_int64),
         ("x_kind", ctypes.c_int32),
         ("y_kind", ctypes.c_int32),
+        ("codes_interleaved", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -43,28 +45,51 @@ def _lib():
         lib.rvq_gemv.restype = ctypes.c_int
         lib.rvq_gemv.argtypes = [ctypes.POINTER(RvqGemvJob), ctypes.c_int, ctypes.c_void_p,
                                  ctypes.c_size_t, ctypes.c_void_p]
+        lib.rvq_interleave_codes.restype = ctypes.c_int
+        lib.rvq_interleave_codes.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                             ctypes.c_void_p, ctypes.c_void_p]
         _bound = True
     return lib
 
 
+def interleave_codes(indices: torch.Tensor) -> torch.Tensor:
+    """The [4, nvec] uint8 code planes of an entry as one 32-bit word per
+    vector (``[nvec * 4]`` uint8, stage k in byte k): the layout ``rvq_gemv``
+    reads with a single load per vector.  Runs on the device."""
+    if indices.dtype != torch.uint8 or indices.dim() != 2 or int(indices.shape[0]) != 4:
+        raise NotImplementedError("interleaving takes [4, nvec] uint8 code planes")
+    indices = indices.contiguous()
+    nvec = int(indices.shape[1])
+    out = torch.empty(nvec * 4, dtype=torch.uint8, device=indices.device)
+    with torch.cuda.device(indices.device):
+        rc = _lib().rvq_interleave_codes(ctypes.c_void_p(indices.data_ptr()), nvec, nvec,
+                                         ctypes.c_void_p(out.data_ptr()),
+                                         ctypes.c_void_p(torch.cuda.current_stream(indices.device).cuda_stream))
+    if rc:
+        _native.check(rc, "rvq_interleave_codes")
+    return out
+
+
 def gemv_supported(entry: Dict[str, object]) -> bool:
     """Whether ``rvq_gemv`` takes this entry (K=4, 256 codes, uint8 codes,
-    no tail, d=8, columns a multiple of 32 -- code words are read 4 groups at
-    a time)."""
+    no tail, d=8, columns a multiple of 8)."""
     idx = entry["indices"]
     shape = entry["shape"]
     return (entry["method"] in ("rvq_groupwise", "rvq_mlp") and int(entry["d"]) == 8
-            and len(shape) == 2 and int(shape[1]) % 32 == 0 and idx.dtype == torch.uint8
+            and len(shape) == 2 and int(shape[1]) % 8 == 0 and idx.dtype == torch.uint8
             and int(idx.shape[0]) == 4 and entry["tail"].numel() == 0
             and int(entry["trimmed_numel"]) == int(shape[0]) * int(shape[1]))
 
 
 class GemvPlan:
-    """One launch computing ``y_i = W_i x_i`` for every bound product."""
+    """One launch computing ``y_i = W_i x_i`` for every bound product.
+
+    An entry that carries ``"codes_il"`` (from ``interleave_codes``) is read
+    in the interleaved layout, else from its artifact code planes."""
 
     def __init__(self, products: Sequence[Tuple[Dict[str, object], torch.Tensor, torch.Tensor, torch.Tensor]]):
-        if not 1 <= len(products) <= 16:
-            raise ValueError("a GEMV launch takes 1 to 16 products")
+        if not 1 <= len(products) <= 4:
+            raise ValueError("a GEMV launch takes 1 to 4 products")
         self._keep: list = []
         jobs: List[RvqGemvJob] = []
         device = None
@@ -80,12 +105,18 @@ class GemvPlan:
                 codebook = codebook.contiguous().clone()
             scales = entry["scales"] if entry["scales"].is_contiguous() else entry["scales"].contiguous()
             indices = entry["indices"] if entry["indices"].is_contiguous() else entry["indices"].contiguous()
-            self._keep.append((codebook, scales, indices, x, y))
+            codes_il = entry.get("codes_il")
+            self._keep.append((codebook, scales, indices, x, y, codes_il))
             w = _native.make_entry(indices, codebook, scales, None, y.view(-1), d=8,
                                    group_size=int(entry["group_size"]),
                                    trimmed=int(entry["trimmed_numel"]))
+            if codes_il is not None:
+                if codes_il.numel() != indices.numel() or codes_il.dtype != torch.uint8:
+                    raise ValueError("codes_il does not match the entry's code planes")
+                w.indices = codes_il.data_ptr()
             jobs.append(RvqGemvJob(w, x.data_ptr(), y.data_ptr(), rows, cols,
-                                   _native.kind_of(x), _native.kind_of(y)))
+                                   _native.kind_of(x), _native.kind_of(y),
+                                   1 if codes_il is not None else 0, 0))
             device = y.device
         self.device = device
         self.jobs = (RvqGemvJob * len(jobs))(*jobs)

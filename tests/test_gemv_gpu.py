@@ -14,7 +14,7 @@ import torch
 
 from oracle.rvq_oracle import OUT_F32, RVQEntryNP, decode_rvq
 from rvq_b200 import synthetic
-from rvq_b200.gemv import GemvPlan, gemv_supported, rvq_linear
+from rvq_b200.gemv import GemvPlan, gemv_supported, interleave_codes, rvq_linear
 
 pytestmark = pytest.mark.gpu
 
@@ -41,18 +41,21 @@ def rel_err(got, want):
     (9728, 2560, None),          # config-1 gate projection, per-row scales
     (2560, 9728, None),          # down projection (38 column tiles)
     (1024, 2560, 128),           # compressor default: group 128 -> 16 vectors per scale
-    (333, 544, None),            # ragged last column tile (68 groups), odd row count
+    (333, 520, None),            # ragged last column tile (65 groups), odd row count
     (64, 64, 64),
 ])
 @pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float32])
-def test_gemv_matches_reconstruction(rows, cols, group, x_dtype, cuda_device):
+@pytest.mark.parametrize("layout", ["planes", "interleaved"])
+def test_gemv_matches_reconstruction(rows, cols, group, x_dtype, layout, cuda_device):
     g = torch.Generator().manual_seed(rows * 7 + cols)
     cb = synthetic.make_codebook(4, 256, 8, g)
     entry = synthetic.make_rvq_entry(rows, cols, g, group_size=group)
     assert gemv_supported(entry)
     x = torch.randn(cols, generator=g).to(x_dtype)
-    y = rvq_linear(x.to(cuda_device), to_dev(entry, cuda_device), cb.to(cuda_device, torch.float32),
-                   out_dtype=torch.float32)
+    dev_entry = to_dev(entry, cuda_device)
+    if layout == "interleaved":
+        dev_entry["codes_il"] = interleave_codes(dev_entry["indices"])
+    y = rvq_linear(x.to(cuda_device), dev_entry, cb.to(cuda_device, torch.float32), out_dtype=torch.float32)
     torch.cuda.synchronize()
     w = oracle_w(entry, cb)
     xd = x.float().numpy().astype(np.float64)
@@ -78,6 +81,13 @@ def test_gemv_is_deterministic_and_reusable(cuda_device):
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
 
 
+def test_interleave_codes_layout(cuda_device):
+    g = torch.Generator().manual_seed(8)
+    idx = torch.randint(0, 256, (4, 1000), dtype=torch.uint8, generator=g)
+    il = interleave_codes(idx.to(cuda_device)).cpu().view(1000, 4)
+    assert torch.equal(il, idx.t().contiguous())
+
+
 def test_gemv_multi_job_shared_x(cuda_device):
     """q, k, v of one 2560-wide layer in one launch, sharing x."""
     g = torch.Generator().manual_seed(4)
@@ -99,7 +109,6 @@ def test_gemv_multi_job_shared_x(cuda_device):
 
 def test_gemv_rejects_unsupported(cuda_device):
     g = torch.Generator().manual_seed(5)
-    assert not gemv_supported(synthetic.make_rvq_entry(16, 520, g))       # 65 groups
     entry = synthetic.make_rvq_entry(64, 64, g, stages=3)
     assert not gemv_supported(entry)
     with pytest.raises(NotImplementedError):
