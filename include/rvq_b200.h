@@ -144,6 +144,26 @@ size_t rvq_gemv_workspace_size(const rvq_gemv_job* jobs, int n_jobs);
  * rvq_gemv_workspace_size() bytes. */
 int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t workspace_bytes, void* stream);
 
+/* rvq_gemv without a caller-supplied workspace, for callers that cannot
+ * allocate device memory: e.g. a serving process that reserves its whole
+ * memory budget at start-up and forbids allocation afterwards, or a plug-in
+ * running inside a host runtime that owns every device allocation.  No
+ * counterpart in the reference.  The workspace is a fixed array of
+ * rvq_gemv_noalloc_max_workspace() bytes (8 MiB) in this library's device
+ * memory, held by every device that loads the library until exit; jobs whose
+ * workspace would exceed it return RVQ_ERR_TOO_LARGE.  Nothing is allocated:
+ * no cudaMalloc/cudaFree and no allocating library routine.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * All calls share the one array, which keeps the last call's contents (each
+ * call clears the part that must start at zero), so calls that overlap on the
+ * GPU -- concurrent streams, or several host threads -- race with each other
+ * and must be serialised by the caller. */
+int rvq_gemv_noalloc(const rvq_gemv_job* jobs, int n_jobs, void* stream);
+
+/* Size of the fixed workspace rvq_gemv_noalloc uses. */
+size_t rvq_gemv_noalloc_max_workspace(void);
+
 /* Repack uint8 code planes [4][stage_stride] into one 32-bit word per vector
  * ([nvec][4] bytes, stage k in byte k), the layout rvq_gemv reads with one
  * load per vector (codes_interleaved = 1).  `out` holds nvec * 4 bytes,

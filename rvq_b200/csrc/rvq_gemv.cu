@@ -407,6 +407,35 @@ static Layout workspace_layout(const rvq_gemv_job* jobs, int n, const uint32_t* 
     return L;
 }
 
+// Scratch for rvq_gemv_noalloc: a fixed array in the module's device memory,
+// so that entry point never asks the CUDA allocator (or any other) for
+// memory.  Every device that loads this library holds it until exit.
+constexpr size_t kStaticScratchBytes = (size_t)8 << 20;          // 8 MiB
+static __device__ __align__(256) unsigned char g_gemv_scratch[kStaticScratchBytes];
+
+static void* g_scratch_addr[64];
+static bool g_scratch_ready[64];
+
+// Device address of g_gemv_scratch on the current device.  Host code may not
+// use the array's name as a device pointer (it names a host-side stand-in),
+// so the address is asked from the runtime once per device, with that device
+// current, and kept.
+static int static_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) { last_cuda_error_slot() = (int)e; return RVQ_ERR_UNAVAILABLE; }
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_scratch_ready[dev]) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_gemv_scratch);
+        if (e != cudaSuccess || !ptr) { last_cuda_error_slot() = (int)e; return RVQ_ERR_CUDA; }
+        g_scratch_addr[dev] = ptr;
+        g_scratch_ready[dev] = true;
+    }
+    *out = g_scratch_addr[dev];
+    return RVQ_OK;
+}
+
 }  // namespace gemv
 }  // namespace rvq
 
@@ -475,6 +504,31 @@ int rvq_gemv(const rvq_gemv_job* jobs, int n_jobs, void* workspace, size_t works
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return RVQ_ERR_CUDA; }
     return RVQ_OK;
+}
+
+size_t rvq_gemv_noalloc_max_workspace(void) { return kStaticScratchBytes; }
+
+int rvq_gemv_noalloc(const rvq_gemv_job* jobs, int n_jobs, void* stream) {
+    if (n_jobs < 1 || n_jobs > kMaxJobs || !jobs) return RVQ_ERR_INVALID;
+    for (int i = 0; i < n_jobs; ++i) {
+        int rc = check_job(&jobs[i]);
+        if (rc != RVQ_OK) return rc;
+    }
+    DevInfo* d = nullptr;
+    int rc = dev_info(&d);
+    if (rc != RVQ_OK) return rc;
+    uint32_t nt[kMaxJobs], nr[kMaxJobs];
+    plan(jobs, n_jobs, d->sms, nt, nr);
+    const Layout L = workspace_layout(jobs, n_jobs, nt, nr);
+    if (L.total > kStaticScratchBytes) return RVQ_ERR_TOO_LARGE;
+    void* ws = nullptr;
+    rc = static_scratch(&ws);
+    if (rc != RVQ_OK) return rc;
+    // the row-range tickets come first in the layout and must start at zero;
+    // the previous call's tables and partials are overwritten before use
+    cudaError_t e = cudaMemsetAsync(ws, 0, L.partial[0], (cudaStream_t)stream);
+    if (e != cudaSuccess) { last_cuda_error_slot() = (int)e; return RVQ_ERR_CUDA; }
+    return rvq_gemv(jobs, n_jobs, ws, kStaticScratchBytes, stream);
 }
 
 int rvq_interleave_codes(const void* planes, int64_t stage_stride, int64_t nvec, void* out, void* stream) {
