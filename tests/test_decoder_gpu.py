@@ -1,0 +1,139 @@
+"""GPU: the graph-captured batch-1 decoder against the drop-in layerwise engine.
+
+The engine (``_layerwise_logits`` through HF modules on slot weights) is the
+reference's forward; it is itself bit-identical to the oracle engine.  The
+decoder's prefill runs the engine's very ops, so its prompt logits are
+bit-identical in ``slot`` and ``dense`` modes.  Decode steps attend over a
+static cache (fixed shapes for the CUDA graph) and, in ``fused`` mode, use
+unrounded fp32 weights instead of bf16 slots, so their logits agree within a
+tolerance and greedy ids agree wherever the engine's top-1 / top-2 margin is
+above that noise.
+"""
+
+import pytest
+import torch
+
+from rvq_b200 import synthetic
+from rvq_b200.decoder import Qwen3Decoder
+from rvq_b200.layerwise import (build_layer_plan, build_meta_model, generate_greedy_ids,
+                                materialize_always_hot, upload_artifact)
+
+pytestmark = pytest.mark.gpu
+
+MID = synthetic.BlockShape(hidden=512, intermediate=1536, n_heads=8, n_kv_heads=2, head_dim=64)
+QW = synthetic.BlockShape()          # the 2560 / 9728 / 32q / 8kv / 128 block
+
+
+def engine_run(art, cfg, prompt, new_tokens, device):
+    model = build_meta_model(cfg)
+    cbs, entries = upload_artifact(art, device)
+    plan = build_layer_plan(model, entries)
+    embed, lm_head = materialize_always_hot(model, plan, cbs, device, torch.bfloat16)
+    ids, logits = generate_greedy_ids(model, plan, cbs, embed, lm_head, prompt.view(1, -1), new_tokens,
+                                      device, torch.bfloat16)
+    return ids.view(-1), [l.view(-1).float() for l in logits]
+
+
+def teacher_forced(dec, prompt, ids):
+    """Decoder logits for the prompt and then each of ``ids`` fed in turn."""
+    out = [dec.prefill(prompt).float().clone()]
+    for i, t in enumerate(ids[:-1].tolist()):
+        out.append(dec.step(torch.tensor([t], device=prompt.device), prompt.numel() + i).float().clone())
+    return out
+
+
+def rel(a, b):
+    return float((a - b).norm() / b.norm())
+
+
+def margin(logits):
+    top = torch.topk(logits, 2).values
+    return float(top[0] - top[1])
+
+
+def assert_greedy_agrees(ids, ref_ids, ref_logits, noise):
+    """Equal ids up to the first step whose reference margin is below ``noise``."""
+    for i in range(ref_ids.numel()):
+        if int(ids[i]) != int(ref_ids[i]):
+            assert margin(ref_logits[i]) < noise, (i, margin(ref_logits[i]))
+            return i
+    return ref_ids.numel()
+
+
+@pytest.mark.parametrize("shape,n_layers,vocab,seed", [(MID, 4, 4096, 3), (QW, 2, 8192, 4)])
+def test_decoder_matches_layerwise_engine(shape, n_layers, vocab, seed, cuda_device):
+    art = synthetic.make_model_artifact(shape, n_layers, vocab, seed=seed)
+    cfg = synthetic.qwen3_config(shape, n_layers, vocab)
+    prompt = torch.randint(0, vocab, (24,), generator=torch.Generator().manual_seed(seed)).to(cuda_device)
+    new = 10
+    ref_ids, ref_logits = engine_run(art, cfg, prompt, new, cuda_device)
+    res = {}
+    for mode in ("dense", "slot", "fused"):
+        dec = Qwen3Decoder(cfg, art, cuda_device, mode=mode, max_len=64)
+        res[mode] = (teacher_forced(dec, prompt, ref_ids), dec.generate(prompt, new))
+    # slot and dense use the same bf16 weights and the same kernels: identical
+    for a, b in zip(res["slot"][0], res["dense"][0]):
+        assert torch.equal(a, b)
+    assert torch.equal(res["slot"][1], res["dense"][1])
+    # prefill is the dense contraction in every mode, with the engine's own ops
+    assert torch.equal(res["fused"][0][0], res["slot"][0][0])
+    assert torch.equal(res["slot"][0][0], ref_logits[0])
+    for mode, tol in (("slot", 2e-2), ("fused", 3e-2)):
+        logits, ids = res[mode]
+        for i, (a, b) in enumerate(zip(logits, ref_logits)):
+            assert rel(a, b) < tol, (mode, i, rel(a, b))
+        noise = 4 * max(float((a - b).abs().max()) for a, b in zip(logits, ref_logits))
+        assert_greedy_agrees(ids, ref_ids, ref_logits, noise)
+
+
+def test_causal_mode_matches_hf_model(cuda_device):
+    """``causal=True`` is the standard Qwen3 forward: prompt logits against
+    HF's Qwen3ForCausalLM (eager attention, causal mask) on the same bf16
+    weights, then a few greedy steps."""
+    from transformers import Qwen3ForCausalLM
+    from oracle.engine_ref import oracle_weight
+    art = synthetic.make_model_artifact(MID, 3, 2048, seed=21)
+    cfg = synthetic.qwen3_config(MID, 3, 2048)
+    hf = Qwen3ForCausalLM(cfg).to(torch.bfloat16)
+    sd = {k: oracle_weight(e, art["shared_codebooks"], torch.bfloat16, "cpu") for k, e in art["entries"].items()}
+    hf.load_state_dict(sd, strict=False)
+    hf = hf.to(cuda_device).eval()
+    prompt = torch.randint(0, 2048, (16,), generator=torch.Generator().manual_seed(5)).to(cuda_device)
+    dec = Qwen3Decoder(cfg, art, cuda_device, mode="slot", max_len=48, causal=True)
+    ids = dec.generate(prompt, 6)
+    with torch.inference_mode():
+        full = hf(torch.cat([prompt, ids[:-1]]).view(1, -1)).logits[0].float()
+    got = teacher_forced(dec, prompt, ids)
+    T = prompt.numel()
+    for i, a in enumerate(got):
+        assert rel(a, full[T - 1 + i]) < 2e-2, (i, rel(a, full[T - 1 + i]))
+    # the reference's mask (non-causal prefill) gives other logits
+    other = Qwen3Decoder(cfg, art, cuda_device, mode="slot", max_len=48).prefill(prompt).float()
+    assert rel(other, full[T - 1]) > 5e-2
+
+
+def test_graph_replay_is_repeatable(cuda_device):
+    """Two generations from the same prompt (cache reset by the prefill)
+    give identical ids and logits."""
+    art = synthetic.make_model_artifact(MID, 3, 2048, seed=8)
+    cfg = synthetic.qwen3_config(MID, 3, 2048)
+    dec = Qwen3Decoder(cfg, art, cuda_device, mode="fused", max_len=48)
+    prompt = torch.randint(0, 2048, (16,), generator=torch.Generator().manual_seed(1)).to(cuda_device)
+    a_ids, a_logits = dec.generate(prompt, 12, return_logits=True)
+    b_ids, b_logits = dec.generate(prompt, 12, return_logits=True)
+    assert torch.equal(a_ids, b_ids)
+    for a, b in zip(a_logits, b_logits):
+        assert torch.equal(a, b)
+
+
+def test_fused_steps_track_slot_steps(cuda_device):
+    """Same tokens fed to fused and slot decoders: per-step logits within the
+    weight-rounding noise (fp32 reconstruction vs bf16 slot)."""
+    art = synthetic.make_model_artifact(MID, 4, 4096, seed=12)
+    cfg = synthetic.qwen3_config(MID, 4, 4096)
+    prompt = torch.randint(0, 4096, (20,), generator=torch.Generator().manual_seed(2)).to(cuda_device)
+    ids = torch.randint(0, 4096, (16,), generator=torch.Generator().manual_seed(3)).to(cuda_device)
+    f = teacher_forced(Qwen3Decoder(cfg, art, cuda_device, mode="fused", max_len=64), prompt, ids)
+    s = teacher_forced(Qwen3Decoder(cfg, art, cuda_device, mode="slot", max_len=64), prompt, ids)
+    for i, (a, b) in enumerate(zip(f, s)):
+        assert rel(a, b) < 2e-2, (i, rel(a, b))
