@@ -170,6 +170,108 @@ size_t rvq_gemv_noalloc_max_workspace(void);
  * 4-byte aligned.  A layout of this library, not of the reference artifact. */
 int rvq_interleave_codes(const void* planes, int64_t stage_stride, int64_t nvec, void* out, void* stream);
 
+/* ---- Batch-1 decode-step operations --------------------------------------
+ * The reference runs each Qwen3 decoder layer through the HF module
+ * (functional_call of Qwen3DecoderLayer, infer_compressed_layerwise_triton.py:
+ * 279-294), i.e. dozens of small PyTorch kernels per layer.  These entry points
+ * are that layer's non-GEMM work as a few launches, for a CUDA-graph-captured
+ * batch-1 decode step; they have no counterpart entry point in the reference.
+ * Every value is rounded to bf16 where the HF module rounds it (RMSNorm:
+ * modeling_qwen3.Qwen3RMSNorm; attention: eager_attention_forward; MLP:
+ * Qwen3MLP), so only fp32 summation order differs. */
+
+/* A vector operand.  kind RVQ_BF16 / RVQ_F16: a plain [n] vector (ntiles 1).
+ * kind RVQ_F32: fp32 partial sums [ntiles][n]; the operand is their sum in
+ * tile order, rounded to bf16 (a projection's output). */
+typedef struct rvq_vec {
+    const void* ptr;          /* device */
+    int64_t n;
+    int32_t ntiles;
+    int32_t kind;
+} rvq_vec;
+
+/* Residual add + RMSNorm of one token:
+ *   h <- token ? embed[*token] : h + add      (bf16, in place)
+ *   x <- weight * bf16(h * rsqrt(mean(h^2) + eps))   (bf16)
+ * One launch of an 8-CTA cluster.  hidden <= 16384. */
+typedef struct rvq_norm_args {
+    void* h;                  /* device bf16 [hidden], the residual stream */
+    rvq_vec add;              /* added to h first; add.ptr NULL: nothing added */
+    const int64_t* token;     /* device; non-NULL: h = embed row *token (first layer) */
+    const void* embed;        /* device bf16 [vocab][hidden], read when token is set */
+    const void* weight;       /* device bf16 [hidden] */
+    void* x;                  /* device bf16 [hidden] output */
+    int64_t hidden;
+    float eps;
+    int32_t vocab;            /* rows of embed; a token outside [0, vocab) reads row 0 */
+} rvq_norm_args;
+
+int rvq_step_norm(const rvq_norm_args* a, void* stream);
+
+/* Attention of one new token at position *pos (device int64) for one layer:
+ * per-head RMSNorm of q and k (q_norm / k_norm), rotary embedding with the
+ * given cos / sin tables, append k and v to the cache at *pos, then for
+ * every query head (GQA: head h reads kv head h / (n_heads / n_kv))
+ *   s_j = bf16(bf16(bf16(q . k_j) * scaling) + valid_bias),  j = 0..*pos
+ *   out = bf16(sum_j bf16(softmax(s)_j) * v_j).
+ * valid_bias is 1.0 to reproduce the reference engine's all-ones additive mask,
+ * 0.0 for the plain causal forward.  A cluster of 8 CTAs per kv head.
+ * A position outside [0, max_len) touches no cache row and yields zeros.
+ * head_dim 64, 128 or 256; n_heads / n_kv <= 16; *pos < max_len. */
+typedef struct rvq_attn_args {
+    rvq_vec q, k, v;          /* q [n_heads*head_dim], k and v [n_kv*head_dim] */
+    const void* q_norm;       /* device bf16 [head_dim] */
+    const void* k_norm;       /* device bf16 [head_dim] */
+    const void* cos;          /* device bf16 [max_len][head_dim] */
+    const void* sin;          /* device bf16 [max_len][head_dim] */
+    const int64_t* pos;       /* device, one value */
+    void* k_cache;            /* device bf16 [n_kv][max_len][head_dim], this layer */
+    void* v_cache;            /* device bf16 [n_kv][max_len][head_dim] */
+    void* out;                /* device bf16 [n_heads*head_dim] */
+    int32_t n_heads;
+    int32_t n_kv;
+    int32_t head_dim;
+    int32_t max_len;
+    float eps;
+    float scaling;
+    float valid_bias;
+    int32_t reserved;
+} rvq_attn_args;
+
+int rvq_step_attention(const rvq_attn_args* a, void* stream);
+
+/* out = bf16(bf16(silu(gate)) * up), [n] bf16 (Qwen3MLP's act_fn(gate) * up). */
+int rvq_step_silu_mul(const rvq_vec* gate, const rvq_vec* up, void* out, void* stream);
+
+/* Fused dequant-GEMV of a batch of one that leaves the cross-tile reduction to
+ * its consumer: for every 256-column tile t of W,
+ *   partials[t][r] = sum over the columns c of tile t of W[r][c] * x[c]
+ * with W never materialised (per-tile tables of codeword . x products, 4
+ * lookups per 8 weights).  The partials are an rvq_vec operand (kind RVQ_F32,
+ * ntiles = rvq_gemv_tiles_count(cols)) of rvq_step_norm / rvq_step_attention
+ * / rvq_step_silu_mul or of another rvq_gemv_tiles job, which add them in tile
+ * order: deterministic, and no reduction launch or cross-CTA fence.
+ * No counterpart in the reference (it reconstructs W into the slot and calls
+ * F.linear: infer_compressed_layerwise_triton.py:290-292).
+ * W: K=4, 256 codes, uint8 codes in the interleaved layout of
+ * rvq_interleave_codes (weight.indices, 4-byte aligned), no tail, d = 8,
+ * cols a multiple of 8; codebook fp32 (16-byte aligned), fp16 or bf16. */
+typedef struct rvq_gemv_tile_job {
+    rvq_entry weight;         /* weight.out is ignored */
+    rvq_vec x;                /* [cols] operand */
+    rvq_vec gate;             /* gate.ptr non-NULL: the operand is bf16(bf16(silu(gate)) * x),
+                                 Qwen3MLP's down-projection input */
+    float* partials;          /* device, [rvq_gemv_tiles_count(cols)][rows] */
+    int64_t rows;
+    int64_t cols;
+} rvq_gemv_tile_job;
+
+/* Number of 256-column tiles (rows of the partials) for `cols` columns. */
+int64_t rvq_gemv_tiles_count(int64_t cols);
+
+/* Up to 4 jobs in one launch (e.g. q, k and v).  No workspace, no allocation. */
+int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream);
+
 /* Reads and clears the sticky device flag that kernels set when an index is
  * outside [0, ncodes) (the decoded element then uses code 0).  Synchronises
  * the current device.  Returns 1 if the flag was set, 0 if not, or -RVQ_ERR_CUDA. */

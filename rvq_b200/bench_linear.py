@@ -25,7 +25,7 @@ import torch
 
 from . import synthetic
 from .engine import LayerDecodePlan
-from .gemv import GemvPlan, interleave_codes
+from .gemv import GemvPlan, GemvTilesPlan, interleave_codes, tiles_count
 
 ROWS, COLS = 9728, 2560
 COPIES = 16
@@ -78,6 +78,21 @@ def run(reps: int = 200, device="cuda:0"):
     t = _time(lambda i: plans[i % COPIES].launch(), reps, stream)
     out["results"]["fused_b1"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
                                   "algorithmic_bytes": algo, "codes": "interleaved"}
+
+    # per-tile partials (the form the decode step consumes), and with the tile sum
+    parts = [torch.empty(tiles_count(COLS), ROWS, dtype=torch.float32, device=device) for _ in range(COPIES)]
+    tplans = [GemvTilesPlan([(c, cbd, x1, p)]) for c, p in zip(il, parts)]
+    t = _time(lambda i: tplans[i % COPIES].launch(), reps, stream)
+    out["results"]["fused_tiles_b1"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
+                                        "algorithmic_bytes": algo, "output": "fp32 partials [10, rows]"}
+    y1 = torch.empty(ROWS, dtype=torch.float32, device=device)
+
+    def tiles_sum(i):
+        tplans[i % COPIES].launch()
+        torch.sum(parts[i % COPIES], 0, out=y1)
+
+    t = _time(tiles_sum, reps, stream)
+    out["results"]["fused_tiles_b1+sum"] = {"us": round(t, 2)}
 
     # decode + GEMM (slot then cuBLAS), and dense
     slot = torch.empty(ROWS, COLS, dtype=torch.bfloat16, device=device)

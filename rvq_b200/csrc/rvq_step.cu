@@ -1,0 +1,505 @@
+// Batch-1 decode-step operations of a Qwen3 decoder layer (sm_100a):
+// residual add + RMSNorm, GQA decode attention over a static KV cache, and
+// SiLU-gated product.  They replace the small PyTorch kernels that the HF
+// modules launch per layer (modeling_qwen3: Qwen3RMSNorm, eager_attention_
+// forward, Qwen3MLP), rounding to bf16 where those modules round.
+//
+// Operands that are projection outputs arrive either as bf16 vectors or as
+// fp32 per-tile partial sums ([ntiles][n], summed in tile order then rounded
+// to bf16), so the GEMV that produced them needs no reduction pass of its own.
+
+#include <cooperative_groups.h>
+#include <type_traits>
+
+#include "rvq_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace rvq {
+namespace {
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ float bf16_at(const void* p, int64_t i) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+__device__ __forceinline__ void put_bf16(void* p, int64_t i, float v) {
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// Value i of a vector operand (see rvq_vec).  Partials are added in tile
+// order; their loads are issued 8 at a time ahead of the adds, so a 38-tile
+// sum costs 5 memory round trips instead of 38.
+__device__ __forceinline__ float vec_value(const rvq_vec& v, int64_t i) {
+    if (v.kind == RVQ_F32) {
+        const float* p = reinterpret_cast<const float*>(v.ptr) + i;
+        const int64_t n = v.n;
+        const int nt = v.ntiles;
+        float s = __ldg(p);
+        int t = 1;
+        for (; t + 8 <= nt; t += 8) {
+            float c[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) c[k] = __ldg(p + (int64_t)(t + k) * n);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s += c[k];
+        }
+        float c[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) c[k] = (t + k < nt) ? __ldg(p + (int64_t)(t + k) * n) : 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (t + k < nt) s += c[k];
+        return bf16r(s);
+    }
+    return load_as_f32(v.ptr, i, v.kind);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// Residual add + RMSNorm.  8 CTAs in one cluster each own a slice of the
+// hidden vector; the sum of squares is combined through distributed shared
+// memory in rank order (deterministic).
+// ---------------------------------------------------------------------------
+constexpr int kNormCtas = 8;
+constexpr int kNormThreads = 512;
+constexpr int kNormMaxSlice = 2048;     // hidden <= 16384
+
+__global__ void __cluster_dims__(kNormCtas, 1, 1) __launch_bounds__(kNormThreads)
+step_norm_kernel(rvq_norm_args a) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    __shared__ float hbuf[kNormMaxSlice];
+    __shared__ float warp_ss[kNormThreads / 32];
+    __shared__ float cta_ss;
+    const int64_t H = a.hidden;
+    const int64_t slice = (H + kNormCtas - 1) / kNormCtas;
+    const int64_t lo = rank * slice;
+    const int64_t hi = lo + slice < H ? lo + slice : H;
+    const int tid = threadIdx.x;
+
+    float ss = 0.f;
+    if (a.token != nullptr) {
+        const int64_t tok = *a.token;
+        const int64_t row = (tok >= 0 && tok < a.vocab ? tok : 0) * H;
+        for (int64_t i = lo + tid; i < hi; i += kNormThreads) {
+            const float hv = bf16_at(a.embed, row + i);
+            hbuf[i - lo] = hv;
+            ss = fmaf(hv, hv, ss);
+        }
+    } else {
+        for (int64_t i = lo + tid; i < hi; i += kNormThreads) {
+            float hv = bf16_at(a.h, i);
+            if (a.add.ptr != nullptr) hv = bf16r(hv + vec_value(a.add, i));
+            hbuf[i - lo] = hv;
+            ss = fmaf(hv, hv, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) warp_ss[tid >> 5] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (int w = 0; w < kNormThreads / 32; ++w) t += warp_ss[w];
+        cta_ss = t;
+    }
+    cluster.sync();
+    float total = 0.f;
+    for (int r = 0; r < kNormCtas; ++r) total += *cluster.map_shared_rank(&cta_ss, r);
+    const float inv = rsqrtf(total / (float)H + a.eps);
+    for (int64_t i = lo + tid; i < hi; i += kNormThreads) {
+        const float hv = hbuf[i - lo];
+        put_bf16(a.h, i, hv);
+        put_bf16(a.x, i, bf16_at(a.weight, i) * bf16r(hv * inv));
+    }
+    cluster.sync();       // no CTA leaves while another may still read its cta_ss
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention.  A cluster of kAttnCtas CTAs per kv head splits the keys
+// 0..pos into contiguous ranges; every CTA normalises and rotates q (the kv
+// head's `rep` query heads) and the new k itself.  Within a CTA each warp
+// takes keys w, w + 8, ...: its lanes hold head_dim / 32 consecutive
+// elements, so a key's K and V rows are read with one coalesced load per warp
+// and a score is a warp sum.  Softmax max and sum, and the P V partial
+// products, are combined through distributed shared memory in rank order, so
+// the result does not depend on scheduling.
+// ---------------------------------------------------------------------------
+constexpr int kAttnCtas = 8;
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kMaxRep = 16;
+constexpr int kKeyChunk = 4;          // keys whose rows a warp loads before using them
+
+// RMSNorm (weight w) + rotary embedding of one head held by one warp:
+// lane holds elements d = lane + 32 j, j < hd / 32.  Returns through `o`.
+template <int HD>
+__device__ __forceinline__ void norm_rope_head(const float* x, const void* w, float eps, const void* cosp,
+                                               const void* sinp, int64_t pos, float* o) {
+    constexpr int J = HD / 32;
+    const int lane = threadIdx.x & 31;
+    float v[J], wv[J], cv[J], sv[J];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        v[j] = x[lane + 32 * j];
+        wv[j] = bf16_at(w, lane + 32 * j);
+        cv[j] = bf16_at(cosp, pos * HD + lane + 32 * j);
+        sv[j] = bf16_at(sinp, pos * HD + lane + 32 * j);
+        ss = fmaf(v[j], v[j], ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)HD + eps);
+#pragma unroll
+    for (int j = 0; j < J; ++j) v[j] = bf16r(wv[j] * bf16r(v[j] * inv));
+    // rotate_half: d < HD/2 -> -v[d + HD/2], else v[d - HD/2]; held by the same lane
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const float rot = j < J / 2 ? -v[j + J / 2] : v[j - J / 2];
+        o[j] = bf16r(bf16r(v[j] * cv[j]) + bf16r(rot * sv[j]));
+    }
+}
+
+// E consecutive bf16 of a cache row as floats.
+template <int E>
+__device__ __forceinline__ void load_row_slice(const __nv_bfloat16* src, float (&out)[E]) {
+    if constexpr (E == 2) {
+        const __nv_bfloat162 w = *reinterpret_cast<const __nv_bfloat162*>(src);
+        out[0] = __low2float(w);
+        out[1] = __high2float(w);
+    } else {
+        using V = typename std::conditional<E == 4, uint2, uint4>::type;
+        const V w = *reinterpret_cast<const V*>(src);
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+        for (int t = 0; t < E; ++t) out[t] = __bfloat162float(e[t]);
+    }
+}
+
+// Shared-memory floats of one CTA (host sizes the dynamic allocation with it).
+__host__ __device__ constexpr int attn_smem_floats(int hd, int rep, int keys_per_cta) {
+    return (rep + 2) * hd                  // raw operands: q heads, k, v
+         + rep * hd                        // q after norm + rope
+         + 2 * hd                          // new k (rotated), new v
+         + kAttnWarps * rep * hd           // P V partial of each warp
+         + rep * hd                        // P V partial of this CTA
+         + rep * keys_per_cta              // scores, then probabilities
+         + 2 * kMaxRep;                    // local max, local sum
+}
+
+template <int HD>
+__global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kAttnThreads)
+step_attn_kernel(rvq_attn_args a) {
+    constexpr int E = HD / 32;                 // elements per lane in the key loops
+    constexpr int RG = 32 / E < kMaxRep ? 32 / E : kMaxRep;   // heads per P V register group
+    extern __shared__ __align__(16) float smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int kv = blockIdx.y;
+    const int rep = a.n_heads / a.n_kv;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t pos = *a.pos;
+    if (pos < 0 || pos >= a.max_len) {               // same decision in every CTA of the cluster
+        for (int i = rank * kAttnThreads + tid; i < rep * HD; i += kAttnCtas * kAttnThreads)
+            put_bf16(a.out, (int64_t)kv * rep * HD + i, 0.f);
+        return;
+    }
+    const int L = (int)pos + 1;
+    const int kpc_max = (a.max_len + kAttnCtas - 1) / kAttnCtas;
+    const int kpc = (L + kAttnCtas - 1) / kAttnCtas;
+    const int j0 = rank * kpc;
+    const int j1 = min(L, j0 + kpc);
+    float* raw = smem;
+    float* qs = raw + (rep + 2) * HD;
+    float* knew = qs + rep * HD;
+    float* vnew = knew + HD;
+    float* pw = vnew + HD;
+    float* pout = pw + kAttnWarps * rep * HD;
+    float* sc = pout + rep * HD;
+    float* mloc = sc + rep * kpc_max;
+    float* sloc = mloc + kMaxRep;
+    __shared__ float red[kMaxRep][kAttnWarps];
+    __shared__ float gmax[kMaxRep], gsum[kMaxRep];
+
+    // 1. operands (6 per thread in flight before their stores)
+    for (int base = 0; base < (rep + 2) * HD; base += 6 * kAttnThreads) {
+        float val[6];
+#pragma unroll
+        for (int m = 0; m < 6; ++m) {
+            const int i = base + tid + m * kAttnThreads;
+            const int r = i / HD, d = i - r * HD;
+            val[m] = 0.f;
+            if (r < rep) val[m] = vec_value(a.q, ((int64_t)kv * rep + r) * HD + d);
+            else if (r == rep) val[m] = vec_value(a.k, (int64_t)kv * HD + d);
+            else if (r == rep + 1) val[m] = vec_value(a.v, (int64_t)kv * HD + d);
+        }
+#pragma unroll
+        for (int m = 0; m < 6; ++m) {
+            const int i = base + tid + m * kAttnThreads;
+            if (i < (rep + 2) * HD) raw[i] = val[m];
+        }
+    }
+    __syncthreads();
+
+    // 2. norm + rope (warp per head); the CTA whose range holds pos appends to the cache
+    const bool owner = j0 <= pos && pos < j1;
+    const int64_t cache_row = ((int64_t)kv * a.max_len + pos) * HD;
+    for (int hh = warp; hh <= rep; hh += kAttnWarps) {
+        float o[HD / 32];
+        const bool is_k = hh == rep;
+        norm_rope_head<HD>(raw + hh * HD, is_k ? a.k_norm : a.q_norm, a.eps, a.cos, a.sin, pos, o);
+#pragma unroll
+        for (int j = 0; j < HD / 32; ++j) {
+            const int d = lane + 32 * j;
+            if (!is_k) {
+                qs[hh * HD + d] = o[j];
+            } else {
+                knew[d] = o[j];
+                vnew[d] = raw[(rep + 1) * HD + d];
+                if (owner) {
+                    put_bf16(a.k_cache, cache_row + d, o[j]);
+                    put_bf16(a.v_cache, cache_row + d, vnew[d]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // 3. scores: warp per key, lanes over head_dim; rows of kKeyChunk keys loaded first
+    const int d0 = lane * E;
+    const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache) + (int64_t)kv * a.max_len * HD;
+    const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache) + (int64_t)kv * a.max_len * HD;
+    float mx[kMaxRep];
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) mx[r] = -INFINITY;
+    for (int jb = j0 + warp; jb < j1; jb += kAttnWarps * kKeyChunk) {
+        float kd[kKeyChunk][E];
+#pragma unroll
+        for (int c = 0; c < kKeyChunk; ++c) {
+            const int j = jb + c * kAttnWarps;
+            if (j < j1 && j != pos) load_row_slice<E>(kc + (int64_t)j * HD + d0, kd[c]);
+            else {
+#pragma unroll
+                for (int e = 0; e < E; ++e) kd[c][e] = knew[d0 + e];
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < kKeyChunk; ++c) {
+            const int j = jb + c * kAttnWarps;
+            if (j >= j1) break;                               // warp-uniform
+#pragma unroll
+            for (int r = 0; r < kMaxRep; ++r) {
+                if (r < rep) {
+                    float t = 0.f;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) t = fmaf(qs[r * HD + d0 + e], kd[c][e], t);
+                    t = warp_sum(t);
+                    const float sv = bf16r(bf16r(bf16r(t) * a.scaling) + a.valid_bias);
+                    if (lane == 0) sc[r * kpc_max + (j - j0)] = sv;
+                    mx[r] = fmaxf(mx[r], sv);
+                }
+            }
+        }
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kMaxRep; ++r)
+            if (r < rep) red[r][warp] = mx[r];
+    }
+    __syncthreads();
+    if (tid < rep) {
+        float m = red[tid][0];
+        for (int w = 1; w < kAttnWarps; ++w) m = fmaxf(m, red[tid][w]);
+        mloc[tid] = m;
+    }
+    cluster.sync();
+
+    // 4. softmax: global max, exponentials, global sum (rank order), bf16 probabilities
+    if (tid < rep) {
+        float m = -INFINITY;
+        for (int c = 0; c < kAttnCtas; ++c) m = fmaxf(m, cluster.map_shared_rank(mloc, c)[tid]);
+        gmax[tid] = m;
+    }
+    __syncthreads();
+    float sm[kMaxRep];
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) sm[r] = 0.f;
+    for (int j = j0 + tid; j < j1; j += kAttnThreads) {
+#pragma unroll
+        for (int r = 0; r < kMaxRep; ++r) {
+            if (r < rep) {
+                const float e = expf(sc[r * kpc_max + (j - j0)] - gmax[r]);
+                sc[r * kpc_max + (j - j0)] = e;
+                sm[r] += e;
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxRep; ++r) {
+        if (r < rep) {
+            const float t = warp_sum(sm[r]);
+            if (lane == 0) red[r][warp] = t;
+        }
+    }
+    __syncthreads();
+    if (tid < rep) {
+        float t = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) t += red[tid][w];
+        sloc[tid] = t;
+    }
+    cluster.sync();
+    if (tid < rep) {
+        float t = 0.f;
+        for (int c = 0; c < kAttnCtas; ++c) t += cluster.map_shared_rank(sloc, c)[tid];
+        gsum[tid] = t;
+    }
+    __syncthreads();
+    for (int j = j0 + tid; j < j1; j += kAttnThreads) {
+#pragma unroll
+        for (int r = 0; r < kMaxRep; ++r)
+            if (r < rep) sc[r * kpc_max + (j - j0)] = bf16r(sc[r * kpc_max + (j - j0)] / gsum[r]);
+    }
+    __syncthreads();
+
+    // 5. P V: warp per key again; RG heads' accumulators per register pass
+    for (int rg = 0; rg < rep; rg += RG) {
+        float acc[RG][E];
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[r][e] = 0.f;
+        for (int jb = j0 + warp; jb < j1; jb += kAttnWarps * kKeyChunk) {
+            float vd[kKeyChunk][E];
+#pragma unroll
+            for (int c = 0; c < kKeyChunk; ++c) {
+                const int j = jb + c * kAttnWarps;
+                if (j < j1 && j != pos) load_row_slice<E>(vc + (int64_t)j * HD + d0, vd[c]);
+                else {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) vd[c][e] = vnew[d0 + e];
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < kKeyChunk; ++c) {
+                const int j = jb + c * kAttnWarps;
+                if (j >= j1) break;
+#pragma unroll
+                for (int r = 0; r < RG; ++r) {
+                    if (rg + r < rep) {
+                        const float pr = sc[(rg + r) * kpc_max + (j - j0)];
+#pragma unroll
+                        for (int e = 0; e < E; ++e) acc[r][e] = fmaf(pr, vd[c][e], acc[r][e]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+            if (rg + r < rep)
+#pragma unroll
+                for (int e = 0; e < E; ++e) pw[(warp * rep + rg + r) * HD + d0 + e] = acc[r][e];
+    }
+    __syncthreads();
+    for (int i = tid; i < rep * HD; i += kAttnThreads) {
+        float t = pw[i];
+        for (int w = 1; w < kAttnWarps; ++w) t += pw[w * rep * HD + i];
+        pout[i] = t;
+    }
+    cluster.sync();
+
+    // 6. sum the CTAs' partials in rank order; CTA c writes its slice of the output
+    const int total = rep * HD;
+    const int chunk = (total + kAttnCtas - 1) / kAttnCtas;
+    for (int i = rank * chunk + tid; i < min(total, (rank + 1) * chunk); i += kAttnThreads) {
+        float t = 0.f;
+        for (int c = 0; c < kAttnCtas; ++c) t += cluster.map_shared_rank(pout, c)[i];
+        put_bf16(a.out, (int64_t)kv * rep * HD + i, t);
+    }
+    cluster.sync();       // keep this CTA's shared memory alive until every reader is done
+}
+
+__global__ void step_silu_mul_kernel(rvq_vec g, rvq_vec u, void* out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= g.n) return;
+    const float gv = vec_value(g, i);
+    const float act = bf16r(gv / (1.0f + expf(-gv)));
+    put_bf16(out, i, act * vec_value(u, i));
+}
+
+bool vec_ok(const rvq_vec& v, int64_t n) {
+    if (v.ptr == nullptr || v.n != n || v.ntiles < 1) return false;
+    if (v.kind == RVQ_F32) return true;
+    return (v.kind == RVQ_BF16 || v.kind == RVQ_F16) && v.ntiles == 1;
+}
+
+int launch_status() {
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) {
+        last_cuda_error_slot() = (int)err;
+        return RVQ_ERR_CUDA;
+    }
+    return RVQ_OK;
+}
+
+template <int HD>
+int launch_attn(const rvq_attn_args& a, cudaStream_t s) {
+    const int rep = a.n_heads / a.n_kv;
+    const int kpc_max = (a.max_len + kAttnCtas - 1) / kAttnCtas;
+    const size_t smem = (size_t)attn_smem_floats(HD, rep, kpc_max) * sizeof(float);
+    if (smem > 200 * 1024) return RVQ_ERR_UNSUPPORTED;
+    if (cudaFuncSetAttribute(step_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return launch_status();
+    step_attn_kernel<HD><<<dim3(kAttnCtas, a.n_kv), kAttnThreads, smem, s>>>(a);
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace rvq
+
+using namespace rvq;
+
+extern "C" int rvq_step_norm(const rvq_norm_args* a, void* stream) {
+    if (a == nullptr || a->h == nullptr || a->weight == nullptr || a->x == nullptr) return RVQ_ERR_INVALID;
+    if (a->hidden < 1 || a->hidden > (int64_t)kNormCtas * kNormMaxSlice) return RVQ_ERR_UNSUPPORTED;
+    if (a->token != nullptr && (a->embed == nullptr || a->vocab < 1)) return RVQ_ERR_INVALID;
+    if (a->token == nullptr && a->add.ptr != nullptr && !vec_ok(a->add, a->hidden)) return RVQ_ERR_INVALID;
+    step_norm_kernel<<<kNormCtas, kNormThreads, 0, (cudaStream_t)stream>>>(*a);
+    return launch_status();
+}
+
+extern "C" int rvq_step_attention(const rvq_attn_args* a, void* stream) {
+    if (a == nullptr || a->q_norm == nullptr || a->k_norm == nullptr || a->cos == nullptr ||
+        a->sin == nullptr || a->pos == nullptr || a->k_cache == nullptr || a->v_cache == nullptr ||
+        a->out == nullptr)
+        return RVQ_ERR_INVALID;
+    if (a->n_kv < 1 || a->n_heads < a->n_kv || a->n_heads % a->n_kv != 0 || a->max_len < 1)
+        return RVQ_ERR_INVALID;
+    if (a->n_heads / a->n_kv > kMaxRep) return RVQ_ERR_UNSUPPORTED;
+    const int64_t hd = a->head_dim;
+    if (!vec_ok(a->q, (int64_t)a->n_heads * hd) || !vec_ok(a->k, (int64_t)a->n_kv * hd) ||
+        !vec_ok(a->v, (int64_t)a->n_kv * hd))
+        return RVQ_ERR_INVALID;
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (a->head_dim) {
+        case 64: return launch_attn<64>(*a, s);
+        case 128: return launch_attn<128>(*a, s);
+        case 256: return launch_attn<256>(*a, s);
+        default: return RVQ_ERR_UNSUPPORTED;
+    }
+}
+
+extern "C" int rvq_step_silu_mul(const rvq_vec* gate, const rvq_vec* up, void* out, void* stream) {
+    if (gate == nullptr || up == nullptr || out == nullptr) return RVQ_ERR_INVALID;
+    if (!vec_ok(*gate, gate->n) || !vec_ok(*up, gate->n) || gate->n < 1) return RVQ_ERR_INVALID;
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((gate->n + threads - 1) / threads);
+    step_silu_mul_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(*gate, *up, out);
+    return launch_status();
+}

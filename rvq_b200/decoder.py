@@ -89,9 +89,15 @@ class Qwen3Decoder:
     ``_attention``), True the standard causal one."""
 
     def __init__(self, config, artifact, device, mode: str = "fused", max_len: int = 512,
-                 runtime_dtype: torch.dtype = torch.bfloat16, causal: bool = False):
+                 runtime_dtype: torch.dtype = torch.bfloat16, causal: bool = False,
+                 step_impl: str = "native"):
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
+        if step_impl not in ("native", "torch"):
+            raise ValueError("step_impl is 'native' (rvq_step kernels) or 'torch'")
+        if runtime_dtype != torch.bfloat16 and step_impl == "native":
+            raise NotImplementedError("the native decode step computes in bf16")
+        self.step_impl = step_impl
         self.mode = mode
         self.device = dev = torch.device(device)
         self.dtype = dt = runtime_dtype
@@ -125,7 +131,11 @@ class Qwen3Decoder:
         self.valid_bias = torch.tensor(0.0 if causal else 1.0, dtype=dt, device=dev)
         self.neg_inf = torch.tensor(float("-inf"), dtype=dt, device=dev)
         self.causal_bias = torch.full((max_len, max_len), float("-inf"), dtype=dt, device=dev).triu(1)
+        self._tok = torch.zeros(1, dtype=torch.long, device=dev)
+        self._pos = torch.zeros(1, dtype=torch.long, device=dev)
         self._setup_weights()
+        if step_impl == "native":
+            self._build_step_ops()
         self.graph: Optional[torch.cuda.CUDAGraph] = None
 
     # -- weights -----------------------------------------------------------------
@@ -156,6 +166,8 @@ class Qwen3Decoder:
                     raise NotImplementedError(f"fused mode needs rvq_gemv-compatible entries ({n})")
                 E[n]["codes_il"] = interleave_codes(E[n]["indices"])
             cb = lambda n: self.codebooks[E[n]["codebook_id"]]
+            if self.step_impl == "native":
+                continue                        # rvq_gemv_tiles plans: _build_step_ops
             L["gemv_qkv"] = GemvPlan([(E[PROJ[0]], cb(PROJ[0]), self.x_attn, self.q),
                                       (E[PROJ[1]], cb(PROJ[1]), self.x_attn, self.k),
                                       (E[PROJ[2]], cb(PROJ[2]), self.x_attn, self.v)])
@@ -243,40 +255,131 @@ class Qwen3Decoder:
             dn = F.linear(F.silu(F.linear(x, w[PROJ[4]])) * F.linear(x, w[PROJ[5]]), w[PROJ[6]])
         return h + dn
 
+    def _layer_weights(self, slots: bool):
+        """Yield (layer, weights) in order.  With ``slots``, layer l+1 is decoded
+        into the other slot on the side stream while layer l computes: the
+        main stream waits for ready[l % 2], the side stream for free[(l+1) % 2]
+        (recorded after the last reader of that slot)."""
+        d = self.dims
+        if not slots:
+            for l in range(d.n_layers):
+                yield l, (self.layers[l]["w"] if self.mode == "dense" else None)
+            return
+        main = torch.cuda.current_stream(self.device)
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            self.decode_plans[0].launch()
+            ready[0].record(self.side)
+        for l in range(d.n_layers):
+            main.wait_event(ready[l % 2])
+            if l + 1 < d.n_layers:
+                with torch.cuda.stream(self.side):
+                    if l >= 1:
+                        self.side.wait_event(free[(l + 1) % 2])
+                    self.decode_plans[l + 1].launch()
+                    ready[(l + 1) % 2].record(self.side)
+            yield l, self.arena.views(l)
+            free[l % 2].record(main)
+        main.wait_stream(self.side)
+
     def _forward(self, ids: torch.Tensor, pos: Optional[torch.Tensor]) -> torch.Tensor:
-        """ids [T] -> logits of the last position [vocab]."""
+        """ids [T] -> logits of the last position [vocab] with PyTorch ops
+        (the prompt; and decode steps when ``step_impl == "torch"``)."""
         d = self.dims
         h = self.embed.index_select(0, ids)
         gemv = self.mode == "fused" and pos is not None
-        slots = self.mode != "dense" and not gemv
-        if slots:
-            main = torch.cuda.current_stream(self.device)
-            ready = [torch.cuda.Event() for _ in range(2)]
-            free = [torch.cuda.Event() for _ in range(2)]
-            self.side.wait_stream(main)
-            with torch.cuda.stream(self.side):
-                self.decode_plans[0].launch()
-                ready[0].record(self.side)
-        for l in range(d.n_layers):
-            w = None
-            if self.mode == "dense":
-                w = self.layers[l]["w"]
-            elif slots:
-                main.wait_event(ready[l % 2])
-                if l + 1 < d.n_layers:                     # decode-ahead into the other slot
-                    with torch.cuda.stream(self.side):
-                        if l >= 1:
-                            self.side.wait_event(free[(l + 1) % 2])
-                        self.decode_plans[l + 1].launch()
-                        ready[(l + 1) % 2].record(self.side)
-                w = self.arena.views(l)
+        for l, w in self._layer_weights(self.mode != "dense" and not gemv):
             h = self._layer(l, h, pos, w, gemv)
-            if slots:
-                free[l % 2].record(main)
-        if slots:
-            main.wait_stream(self.side)
         h = rmsnorm(h[-1:], self.final_norm, d.eps)
         return F.linear(h, self.lm_head).view(-1)
+
+    # -- the native decode step --------------------------------------------------------
+    def _build_step_ops(self) -> None:
+        """Kernel descriptors of the native decode step (one token at ``self._pos``)."""
+        from .step import AttentionOp, NormOp, SiluMulOp
+        d, dev, dt = self.dims, self.device, self.dtype
+        self.h = torch.zeros(d.hidden, dtype=dt, device=dev)
+        self.x_final = torch.zeros(d.hidden, dtype=dt, device=dev)
+        self.logits_buf = torch.zeros(d.vocab, dtype=dt, device=dev)
+        self.step_ops = []
+        fused = self.mode == "fused"
+        if fused:
+            # projection outputs stay as per-tile fp32 partials; consumers add the tiles
+            from .gemv import GemvTilesPlan, tiles_count
+            part = lambda rows, cols: torch.zeros(tiles_count(cols), rows, dtype=torch.float32, device=dev)
+            qd, kvd = d.n_heads * d.head_dim, d.n_kv * d.head_dim
+            self.q_part, self.k_part, self.v_part = part(qd, d.hidden), part(kvd, d.hidden), part(kvd, d.hidden)
+            self.o_part = part(d.hidden, qd)
+            self.gate_part, self.up_part = part(d.intermediate, d.hidden), part(d.intermediate, d.hidden)
+            self.down_part = part(d.hidden, d.intermediate)
+            q, k, v, o, down = self.q_part, self.k_part, self.v_part, self.o_part, self.down_part
+        else:
+            q, k, v, o, down = self.q, self.k, self.v, self.o, self.down
+        tiles = lambda t: t.shape[0] if t.dim() == 2 else 1
+        for l, L in enumerate(self.layers):
+            first = l == 0
+            ops = {
+                "norm1": NormOp(self.h, L["input_layernorm.weight"], self.x_attn, d.eps,
+                                add=None if first else down, add_tiles=tiles(down),
+                                token=self._tok if first else None, embed=self.embed if first else None),
+                "attn": AttentionOp(q, k, v, L["self_attn.q_norm.weight"],
+                                    L["self_attn.k_norm.weight"], self.cos, self.sin, self._pos,
+                                    self.k_cache[l], self.v_cache[l], self.attn_out, n_heads=d.n_heads,
+                                    n_kv=d.n_kv, head_dim=d.head_dim, eps=d.eps, scaling=self.scaling,
+                                    valid_bias=0.0 if self.causal else 1.0, q_tiles=tiles(q), kv_tiles=tiles(k)),
+                "norm2": NormOp(self.h, L["post_attention_layernorm.weight"], self.x_mlp, d.eps, add=o,
+                                add_tiles=tiles(o)),
+            }
+            if fused:
+                E = L["entries"]
+                cb = lambda n: self.codebooks[E[n]["codebook_id"]]
+                ops["qkv"] = GemvTilesPlan([(E[PROJ[0]], cb(PROJ[0]), self.x_attn, self.q_part),
+                                            (E[PROJ[1]], cb(PROJ[1]), self.x_attn, self.k_part),
+                                            (E[PROJ[2]], cb(PROJ[2]), self.x_attn, self.v_part)])
+                ops["o"] = GemvTilesPlan([(E[PROJ[3]], cb(PROJ[3]), self.attn_out, self.o_part)])
+                ops["gu"] = GemvTilesPlan([(E[PROJ[4]], cb(PROJ[4]), self.x_mlp, self.gate_part),
+                                           (E[PROJ[5]], cb(PROJ[5]), self.x_mlp, self.up_part)])
+                ops["down"] = GemvTilesPlan([(E[PROJ[6]], cb(PROJ[6]), self.up_part, self.down_part,
+                                              self.gate_part)])      # silu(gate) * up fused in
+            else:
+                ops["silu"] = SiluMulOp(self.gate, self.up, self.act)
+            self.step_ops.append(ops)
+        self.final_op = NormOp(self.h, self.final_norm, self.x_final, d.eps, add=down, add_tiles=tiles(down))
+
+    @staticmethod
+    def _mv(w: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> None:
+        torch.mm(x.view(1, -1), w.t(), out=y.view(1, -1))         # = F.linear(x, w)
+
+    def _step_native(self) -> torch.Tensor:
+        fused = self.mode == "fused"
+        for l, w in self._layer_weights(self.mode == "slot"):
+            ops = self.step_ops[l]
+            ops["norm1"].launch()
+            if fused:
+                ops["qkv"].launch()
+            else:
+                self._mv(w[PROJ[0]], self.x_attn, self.q)
+                self._mv(w[PROJ[1]], self.x_attn, self.k)
+                self._mv(w[PROJ[2]], self.x_attn, self.v)
+            ops["attn"].launch()
+            if fused:
+                ops["o"].launch()
+            else:
+                self._mv(w[PROJ[3]], self.attn_out, self.o)
+            ops["norm2"].launch()
+            if fused:
+                ops["gu"].launch()
+                ops["down"].launch()
+            else:
+                self._mv(w[PROJ[4]], self.x_mlp, self.gate)
+                self._mv(w[PROJ[5]], self.x_mlp, self.up)
+                ops["silu"].launch()
+                self._mv(w[PROJ[6]], self.act, self.down)
+        self.final_op.launch()
+        self._mv(self.lm_head, self.x_final, self.logits_buf)
+        return self.logits_buf
 
     # -- prefill (eager) and graph-replayed decode steps -------------------------------
     def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
@@ -288,20 +391,19 @@ class Qwen3Decoder:
 
     def capture(self) -> "Qwen3Decoder":
         """Record one decode step (token ``self._tok`` at ``self._pos``) as a CUDA graph."""
-        self._tok = torch.zeros(1, dtype=torch.long, device=self.device)
-        self._pos = torch.zeros(1, dtype=torch.long, device=self.device)
         kv = (self.k_cache.clone(), self.v_cache.clone())
+        run = self._step_native if self.step_impl == "native" else (lambda: self._forward(self._tok, self._pos))
         with torch.inference_mode():
             s = torch.cuda.Stream(self.device)
             s.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(s):
                 for _ in range(2):
-                    self._logits = self._forward(self._tok, self._pos)
+                    self._logits = run()
             torch.cuda.current_stream(self.device).wait_stream(s)
             torch.cuda.synchronize(self.device)
             self.graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph):
-                self._logits = self._forward(self._tok, self._pos)
+                self._logits = run()
         self.k_cache.copy_(kv[0])                         # warm-up steps wrote row 0
         self.v_cache.copy_(kv[1])
         return self

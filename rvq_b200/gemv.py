@@ -17,6 +17,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 
 from . import _native
+from . import step as _step
 
 
 class RvqGemvJob(ctypes.Structure):
@@ -145,3 +146,90 @@ def rvq_linear(x: torch.Tensor, entry: Dict[str, object], codebook: torch.Tensor
         out = torch.empty(rows, dtype=out_dtype or x.dtype, device=x.device)
     GemvPlan([(entry, codebook, x.reshape(-1).contiguous(), out)]).launch()
     return out
+
+
+# ---------------------------------------------------------------------------
+# rvq_gemv_tiles: per-tile partial sums, reduced by the consumer
+# ---------------------------------------------------------------------------
+
+class RvqGemvTileJob(ctypes.Structure):
+    _fields_ = [
+        ("weight", _native.RvqEntry),
+        ("x", _step.RvqVec),
+        ("gate", _step.RvqVec),
+        ("partials", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+    ]
+
+
+_tiles_bound = False
+
+
+def _tiles_lib():
+    global _tiles_bound
+    lib = _native.load()
+    if not _tiles_bound:
+        lib.rvq_gemv_tiles.restype = ctypes.c_int
+        lib.rvq_gemv_tiles.argtypes = [ctypes.POINTER(RvqGemvTileJob), ctypes.c_int, ctypes.c_void_p]
+        lib.rvq_gemv_tiles_count.restype = ctypes.c_int64
+        lib.rvq_gemv_tiles_count.argtypes = [ctypes.c_int64]
+        _tiles_bound = True
+    return lib
+
+
+def tiles_count(cols: int) -> int:
+    """Rows of the partials ``rvq_gemv_tiles`` writes for ``cols`` columns."""
+    return int(_tiles_lib().rvq_gemv_tiles_count(cols))
+
+
+class GemvTilesPlan:
+    """One ``rvq_gemv_tiles`` launch over up to 4 products.
+
+    ``products``: ``(entry, codebook, x, partials)`` or ``(entry, codebook, x,
+    partials, gate)`` tuples.  ``entry["codes_il"]`` (from ``interleave_codes``)
+    is required.  ``x`` / ``gate`` are bf16 vectors or fp32 partials
+    ``[ntiles, cols]``; ``partials`` is fp32 ``[tiles_count(cols), rows]``.
+    With ``gate`` the operand is ``bf16(bf16(silu(gate)) * x)``.
+    """
+
+    def __init__(self, products):
+        if not 1 <= len(products) <= 4:
+            raise ValueError("a GEMV launch takes 1 to 4 products")
+        self._keep: list = []
+        jobs = []
+        for prod in products:
+            entry, codebook, x, part = prod[:4]
+            gate = prod[4] if len(prod) > 4 else None
+            if not gemv_supported(entry) or entry.get("codes_il") is None:
+                raise NotImplementedError("rvq_gemv_tiles needs a K=4 uint8 entry with codes_il")
+            rows, cols = int(entry["shape"][0]), int(entry["shape"][1])
+            nt = tiles_count(cols)
+            if part.dtype != torch.float32 or tuple(part.shape) != (nt, rows) or not part.is_contiguous():
+                raise ValueError(f"partials must be fp32 [{nt}, {rows}]")
+            if codebook.dtype not in (torch.float16, torch.float32):
+                codebook = codebook.to(torch.float32)
+            if not codebook.is_contiguous() or codebook.data_ptr() % 16:
+                codebook = codebook.contiguous().clone()
+            scales = entry["scales"].contiguous()
+            codes = entry["codes_il"]
+            xv = _step.vec(x, x.shape[0] if (x.dtype == torch.float32 and x.dim() == 2) else 1)
+            gv = _step.vec(gate, gate.shape[0] if (gate is not None and gate.dtype == torch.float32
+                                                    and gate.dim() == 2) else 1)
+            if xv.n != cols or (gate is not None and gv.n != cols):
+                raise ValueError("operand length must equal the weight's columns")
+            w = _native.make_entry(entry["indices"], codebook, scales, None, part.view(-1), d=8,
+                                   group_size=int(entry["group_size"]), trimmed=int(entry["trimmed_numel"]))
+            w.indices = codes.data_ptr()
+            self._keep.append((codebook, scales, codes, x, gate, part))
+            jobs.append(RvqGemvTileJob(w, xv, gv, part.data_ptr(), rows, cols))
+            self.device = part.device
+        self.jobs = (RvqGemvTileJob * len(jobs))(*jobs)
+        self.n = len(jobs)
+
+    def launch(self, stream: Optional[int] = None) -> None:
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = _tiles_lib().rvq_gemv_tiles(self.jobs, self.n, ctypes.c_void_p(stream))
+        if rc:
+            _native.check(rc, "rvq_gemv_tiles")

@@ -48,6 +48,39 @@ def test_struct_layout_matches_header(lib):
     assert ctypes.sizeof(_native.RvqCopy) == 24
 
 
+def test_step_struct_layouts():
+    from rvq_b200 import step
+    assert ctypes.sizeof(step.RvqVec) == 24
+    assert ctypes.sizeof(step.RvqNormArgs) == 8 + 24 + 4 * 8 + 8 + 4 + 4
+    assert ctypes.sizeof(step.RvqAttnArgs) == 3 * 24 + 8 * 8 + 4 * 4 + 4 * 4
+    from rvq_b200 import gemv
+    assert ctypes.sizeof(gemv.RvqGemvTileJob) == ctypes.sizeof(_native.RvqEntry) + 2 * 24 + 3 * 8
+    assert gemv.tiles_count(2560) == 10 and gemv.tiles_count(9728) == 38 and gemv.tiles_count(520) == 3
+
+
+def test_step_calls_reject_bad_arguments(lib):
+    """Host-side checks run before any launch (no device needed)."""
+    from rvq_b200 import step
+    step._lib()
+    assert lib.rvq_step_norm(None, None) == _native.RVQ_ERR_INVALID
+    a = step.RvqNormArgs(8, step.RvqVec(None, 0, 0, 0), None, None, 8, 8, 1 << 20, 1e-6, 0)
+    assert lib.rvq_step_norm(ctypes.byref(a), None) == _native.RVQ_ERR_UNSUPPORTED
+    a.hidden = 64
+    a.add = step.RvqVec(8, 32, 1, _native.RVQ_BF16)            # wrong length
+    assert lib.rvq_step_norm(ctypes.byref(a), None) == _native.RVQ_ERR_INVALID
+    v = step.RvqVec(8, 128, 1, _native.RVQ_BF16)
+    at = step.RvqAttnArgs(v, v, v, 8, 8, 8, 8, 8, 8, 8, 8, 3, 2, 64, 16, 1e-6, 0.1, 1.0, 0)
+    assert lib.rvq_step_attention(ctypes.byref(at), None) == _native.RVQ_ERR_INVALID   # 3 % 2 != 0
+    at.n_heads, at.n_kv, at.head_dim = 2, 2, 96
+    at.q = at.k = at.v = step.RvqVec(8, 192, 1, _native.RVQ_BF16)
+    assert lib.rvq_step_attention(ctypes.byref(at), None) == _native.RVQ_ERR_UNSUPPORTED
+    at.n_heads, at.n_kv, at.head_dim = 64, 2, 64                                   # 32 heads per kv head
+    assert lib.rvq_step_attention(ctypes.byref(at), None) == _native.RVQ_ERR_UNSUPPORTED
+    g = step.RvqVec(8, 100, 1, _native.RVQ_BF16)
+    u = step.RvqVec(8, 99, 1, _native.RVQ_BF16)
+    assert lib.rvq_step_silu_mul(ctypes.byref(g), ctypes.byref(u), 8, None) == _native.RVQ_ERR_INVALID
+
+
 def test_status_strings(lib):
     assert _native.status_string(0) == "ok"
     for s in range(1, 6):

@@ -137,3 +137,19 @@ def test_fused_steps_track_slot_steps(cuda_device):
     s = teacher_forced(Qwen3Decoder(cfg, art, cuda_device, mode="slot", max_len=64), prompt, ids)
     for i, (a, b) in enumerate(zip(f, s)):
         assert rel(a, b) < 2e-2, (i, rel(a, b))
+
+
+@pytest.mark.parametrize("mode", ["dense", "fused"])
+def test_native_step_tracks_torch_step(mode, cuda_device):
+    """The rvq_step kernels against the decoder's PyTorch step on the same
+    tokens: logits within summation-order noise, same greedy ids."""
+    art = synthetic.make_model_artifact(MID, 4, 4096, seed=31)
+    cfg = synthetic.qwen3_config(MID, 4, 4096)
+    prompt = torch.randint(0, 4096, (20,), generator=torch.Generator().manual_seed(4)).to(cuda_device)
+    ids = torch.randint(0, 4096, (24,), generator=torch.Generator().manual_seed(5)).to(cuda_device)
+    nat = teacher_forced(Qwen3Decoder(cfg, art, cuda_device, mode=mode, max_len=64), prompt, ids)
+    tor = teacher_forced(Qwen3Decoder(cfg, art, cuda_device, mode=mode, max_len=64, step_impl="torch"),
+                         prompt, ids)
+    assert torch.equal(nat[0], tor[0])            # the prompt runs the same PyTorch ops
+    for i, (a, b) in enumerate(zip(nat[1:], tor[1:])):
+        assert rel(a, b) < 1e-2, (i, rel(a, b))

@@ -1,0 +1,132 @@
+"""GPU: rvq_gemv_tiles (per-tile partial sums) against the oracle's reconstruction.
+
+Each tile's partial sum is compared with the fp64 product of the oracle's
+fp32 weight restricted to that tile's 256 columns; the table-based sum is
+exact up to fp32 rounding (rel. error <= 2e-5 over the whole output).
+"""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle.rvq_oracle import OUT_F32, RVQEntryNP, decode_rvq
+from rvq_b200 import synthetic
+from rvq_b200.gemv import GemvTilesPlan, interleave_codes, tiles_count
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle_w(entry, cb):
+    numel = int(np.prod(entry["shape"]))
+    e = RVQEntryNP(indices=entry["indices"].numpy(), codebook=cb.float().numpy(),
+                   scales=entry["scales"].float().numpy(), tail=entry["tail"].float().numpy(), d=8,
+                   group_size=int(entry["group_size"]), trimmed_numel=int(entry["trimmed_numel"]),
+                   numel=numel)
+    return decode_rvq(e, OUT_F32).reshape(entry["shape"]).astype(np.float64)
+
+
+def dev_entry(entry, device):
+    e = {k: (v.to(device) if torch.is_tensor(v) else v) for k, v in entry.items()}
+    e["codes_il"] = interleave_codes(e["indices"])
+    return e
+
+
+def rel_err(got, want):
+    got = np.asarray(got, np.float64)
+    return float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))
+
+
+def tile_products(w, x):
+    cols = w.shape[1]
+    return np.stack([w[:, t * 256:(t + 1) * 256] @ x[t * 256:(t + 1) * 256] for t in range(tiles_count(cols))])
+
+
+@pytest.mark.parametrize("rows,cols,group,cb_dtype", [
+    (9728, 2560, None, torch.float32),     # gate projection, per-row scales
+    (2560, 9728, None, torch.float32),     # down projection, 38 tiles
+    (4096, 2560, None, torch.float16),     # fp16 codebook
+    (1024, 2560, 128, torch.float32),      # 16 vectors per scale
+    (333, 520, None, torch.float32),       # ragged last tile (1 group), odd rows
+    (8, 8, 8, torch.float32),              # one vector per row
+    (3000, 1000, 40, torch.float32),       # G = 125: rows not 16-byte aligned, 5 vectors per scale
+])
+def test_tiles_match_reconstruction(rows, cols, group, cb_dtype, cuda_device):
+    g = torch.Generator().manual_seed(rows + 3 * cols)
+    cb = synthetic.make_codebook(4, 256, 8, g)
+    entry = synthetic.make_rvq_entry(rows, cols, g, group_size=group)
+    x = torch.randn(cols, generator=g).to(torch.bfloat16)
+    part = torch.full((tiles_count(cols), rows), float("nan"), device=cuda_device)
+    GemvTilesPlan([(dev_entry(entry, cuda_device), cb.to(cuda_device, cb_dtype), x.to(cuda_device), part)]).launch()
+    torch.cuda.synchronize()
+    assert not torch.isnan(part).any()
+    w = oracle_w(entry, cb)
+    xd = x.double().numpy()
+    tp = tile_products(w, xd)
+    assert rel_err(part.cpu().numpy(), tp) <= 2e-5
+    assert rel_err(part.sum(0).cpu().numpy(), w @ xd) <= 2e-5
+
+
+def test_multi_job_launch_and_determinism(cuda_device):
+    """q, k, v in one launch (different codebooks, shared x); repeated
+    launches give bit-identical partials."""
+    g = torch.Generator().manual_seed(11)
+    shapes = [(4096, 2560), (1024, 2560), (1024, 2560)]
+    cbs = [synthetic.make_codebook(4, 256, 8, g) for _ in shapes]
+    entries = [synthetic.make_rvq_entry(r, c, g) for r, c in shapes]
+    x = torch.randn(2560, generator=g).to(torch.bfloat16)
+    xd = x.to(cuda_device)
+    parts = [torch.zeros(tiles_count(c), r, device=cuda_device) for r, c in shapes]
+    plan = GemvTilesPlan([(dev_entry(e, cuda_device), cb.to(cuda_device, torch.float32), xd, p)
+                          for e, cb, p in zip(entries, cbs, parts)])
+    plan.launch()
+    torch.cuda.synchronize()
+    first = [p.clone() for p in parts]
+    for _ in range(3):
+        plan.launch()
+    torch.cuda.synchronize()
+    for e, cb, p, p0 in zip(entries, cbs, parts, first):
+        assert torch.equal(p, p0)
+        assert rel_err(p.cpu().numpy(), tile_products(oracle_w(e, cb), x.double().numpy())) <= 2e-5
+
+
+def test_partial_operand_and_fused_silu(cuda_device):
+    """The down projection's input straight from the gate / up partials:
+    operand = bf16(bf16(silu(gate)) * up), each the tile-ordered sum of its
+    partials rounded to bf16."""
+    g = torch.Generator().manual_seed(12)
+    rows, cols, nt = 2560, 9728, 10
+    cb = synthetic.make_codebook(4, 256, 8, g)
+    entry = synthetic.make_rvq_entry(rows, cols, g)
+    gate_p = (torch.randn(nt, cols, generator=g) / 3).to(cuda_device)
+    up_p = (torch.randn(nt, cols, generator=g) / 3).to(cuda_device)
+
+    def tile_sum(p):
+        s = p[0].clone()
+        for t in range(1, nt):
+            s += p[t]
+        return s.to(torch.bfloat16)
+
+    act = (F.silu(tile_sum(gate_p)) * tile_sum(up_p)).double().cpu().numpy()
+    part = torch.zeros(tiles_count(cols), rows, device=cuda_device)
+    GemvTilesPlan([(dev_entry(entry, cuda_device), cb.to(cuda_device, torch.float32), up_p, part, gate_p)]).launch()
+    torch.cuda.synchronize()
+    w = oracle_w(entry, cb)
+    assert rel_err(part.sum(0).cpu().numpy(), w @ act) <= 2e-5
+    # the same with the plain operand (no gate): x = up partials
+    part2 = torch.zeros_like(part)
+    GemvTilesPlan([(dev_entry(entry, cuda_device), cb.to(cuda_device, torch.float32), up_p, part2)]).launch()
+    torch.cuda.synchronize()
+    assert rel_err(part2.sum(0).cpu().numpy(), w @ tile_sum(up_p).double().cpu().numpy()) <= 2e-5
+
+
+def test_rejects_bad_jobs(cuda_device):
+    g = torch.Generator().manual_seed(13)
+    cb = synthetic.make_codebook(4, 256, 8, g).to(cuda_device, torch.float32)
+    e = dev_entry(synthetic.make_rvq_entry(64, 256, g), cuda_device)
+    x = torch.zeros(256, dtype=torch.bfloat16, device=cuda_device)
+    with pytest.raises(ValueError):
+        GemvTilesPlan([(e, cb, x, torch.zeros(2, 64, device=cuda_device))])        # wrong tile count
+    with pytest.raises(ValueError):
+        GemvTilesPlan([(e, cb, torch.zeros(128, dtype=torch.bfloat16, device=cuda_device),
+                        torch.zeros(1, 64, device=cuda_device))])                     # wrong operand length
