@@ -74,6 +74,38 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int out_kind) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (sm_90+).  A kernel launched with launch_pdl
+// may start while the previous kernel of its stream is still running, once
+// every CTA of that kernel has called pdl_launch_dependents().  It may read
+// only data that no earlier kernel of the stream writes (weights, code words,
+// codebooks) before pdl_wait(), which returns when the previous kernel has
+// completed and its writes are visible; it writes nothing before pdl_wait().
+// Every kernel calls pdl_wait() on every path, so completion is transitive
+// along the stream.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Last CUDA error seen by the library on the calling thread (shared by all
 // translation units through this inline function's static).
 inline int& last_cuda_error_slot() {

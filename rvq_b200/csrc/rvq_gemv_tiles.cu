@@ -221,73 +221,6 @@ __device__ __forceinline__ void build_lut_ffma(float* __restrict__ lut, const fl
     }
 }
 
-__device__ __forceinline__ void mma_tf32_16x8x8(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Tensor cores: D[g][c] = sum_t X[g][t] * CB[c][t] as m16n8k8 tf32 products,
-// M = the 32 groups (two m-tiles), N = 8 table rows, K = the 8 elements of a
-// group.  A quad (lanes 4r..4r+3) then holds groups r, r+8, r+16, r+24 for
-// rows 2i, 2i+1 (lane 4r+i); a 4 x 4 exchange inside the quad gives lane 4r+i
-// group r + 8i for all 8 rows, so each table store covers 32 distinct groups,
-// i.e. 32 distinct banks.
-__device__ __forceinline__ void build_lut_mma(float* __restrict__ lut, const float* __restrict__ cbs,
-                                              const float* __restrict__ xs) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gid = lane >> 2, tig = lane & 3;
-    uint32_t a0[4], a1[4];                       // X rows: groups gid (+8), m-tile 0 / 1 (+16)
-#pragma unroll
-    for (int m = 0; m < 2; ++m) {
-        uint32_t* a = m ? a1 : a0;
-        const int g = gid + 16 * m;
-        a[0] = __float_as_uint(xs[8 * g + tig]);
-        a[1] = __float_as_uint(xs[8 * (g + 8) + tig]);
-        a[2] = __float_as_uint(xs[8 * g + tig + 4]);
-        a[3] = __float_as_uint(xs[8 * (g + 8) + tig + 4]);
-    }
-    const int g_store = gid + 8 * tig;
-#pragma unroll 1
-    for (int q0 = warp * 8; q0 < kPairs; q0 += kWarps * 8) {
-        const uint32_t b0 = __float_as_uint(cbs[(q0 + gid) * 8 + tig]);
-        const uint32_t b1 = __float_as_uint(cbs[(q0 + gid) * 8 + tig + 4]);
-        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_tf32_16x8x8(d0, a0, b0, b1);
-        mma_tf32_16x8x8(d1, a1, b0, b1);
-        // v[s][h]: group gid + 8 s, row q0 + 2 tig + h
-        const float v[4][2] = {{d0[0], d0[1]}, {d0[2], d0[3]}, {d1[0], d1[1]}, {d1[2], d1[3]}};
-        float w[4][2];                           // w[j][h]: group g_store, row q0 + 2 j + h
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int s = tig ^ r;               // the slot lane tig ^ r needs from this lane
-            float send0 = v[0][0], send1 = v[0][1];
-#pragma unroll
-            for (int k = 1; k < 4; ++k) {
-                send0 = (s == k) ? v[k][0] : send0;
-                send1 = (s == k) ? v[k][1] : send1;
-            }
-            const float r0v = r ? __shfl_xor_sync(0xffffffffu, send0, r) : send0;
-            const float r1v = r ? __shfl_xor_sync(0xffffffffu, send1, r) : send1;
-            // received from lane tig ^ r: its rows 2 (tig ^ r) + h
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if (j == (tig ^ r)) {
-                    w[j][0] = r0v;
-                    w[j][1] = r1v;
-                }
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            lut[(q0 + 2 * j) * kGroups + g_store] = w[j][0];
-            lut[(q0 + 2 * j + 1) * kGroups + g_store] = w[j][1];
-        }
-    }
-}
-
 __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __grid_constant__ TParams p) {
     extern __shared__ __align__(128) float smem[];
     float* __restrict__ lut = smem;
@@ -300,6 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
 
     __shared__ int slot_done[kRing];                     // warps finished with a ring slot
     if (tid < kRing) slot_done[tid] = 0;
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < kRing; ++s) mbar_init(bar0 + 8 * s);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -342,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
         } else {
             for (int i = tid; i < kCbFloats; i += kThreads) cbs[i] = load_as_f32(J.cb, i, J.cb_kind);
         }
+        if (u == (int)blockIdx.x) pdl_wait();            // x comes from the previous kernel
         if (tid < kTileCols) {
             const int64_t col = (int64_t)tile * kTileCols + tid;
             float xv = 0.f;
@@ -357,13 +292,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
         cp_async_wait<0>();          // the codebook (and, without TMA, the first code batches)
         __syncthreads();
 
-        // 3. the tile's table.  Tensor cores when every codebook value is exact in
-        //    tf32 (always for codebooks that came from fp16; x is bf16-rounded or
-        //    fp16, exact too), FFMA otherwise.
-        bool tf32_ok = true;
-        for (int i = tid; i < kCbFloats; i += kThreads) tf32_ok &= (__float_as_uint(cbs[i]) & 0x1fffu) == 0;
-        if (__syncthreads_and(tf32_ok)) build_lut_mma(lut, cbs, xs);
-        else build_lut_ffma(lut, cbs, xs);
+        // 3. the tile's table (shared-memory bound: the codebook rows are broadcast
+        //    loads, the table 128 KB of conflict-free stores)
+        build_lut_ffma(lut, cbs, xs);
         __syncthreads();
 
         // 4. rows, batch by batch; batch b + 2 streams in while b + 1 is processed.
@@ -620,8 +551,8 @@ int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream) {
     rc = plan(jobs, n_jobs, d->sms, p);
     if (rc != RVQ_OK) return rc;
     const int grid = p.n_units < d->sms ? p.n_units : d->sms;
-    rvq_gemv_tiles_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(p);
-    const cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(rvq_gemv_tiles_kernel, dim3(grid), dim3(kThreads), kSmemBytes, (cudaStream_t)stream, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         last_cuda_error_slot() = (int)e;
         return RVQ_ERR_CUDA;

@@ -76,6 +76,7 @@ step_norm_kernel(rvq_norm_args a) {
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     __shared__ float hbuf[kNormMaxSlice];
+    __shared__ float wbuf[kNormMaxSlice];
     __shared__ float warp_ss[kNormThreads / 32];
     __shared__ float cta_ss;
     const int64_t H = a.hidden;
@@ -84,6 +85,9 @@ step_norm_kernel(rvq_norm_args a) {
     const int64_t hi = lo + slice < H ? lo + slice : H;
     const int tid = threadIdx.x;
 
+    pdl_launch_dependents();
+    for (int64_t i = lo + tid; i < hi; i += kNormThreads) wbuf[i - lo] = bf16_at(a.weight, i);
+    pdl_wait();
     float ss = 0.f;
     if (a.token != nullptr) {
         const int64_t tok = *a.token;
@@ -116,7 +120,7 @@ step_norm_kernel(rvq_norm_args a) {
     for (int64_t i = lo + tid; i < hi; i += kNormThreads) {
         const float hv = hbuf[i - lo];
         put_bf16(a.h, i, hv);
-        put_bf16(a.x, i, bf16_at(a.weight, i) * bf16r(hv * inv));
+        put_bf16(a.x, i, wbuf[i - lo] * bf16r(hv * inv));
     }
     cluster.sync();       // no CTA leaves while another may still read its cta_ss
 }
@@ -140,29 +144,27 @@ constexpr int kKeyChunk = 4;          // keys whose rows a warp loads before usi
 // RMSNorm (weight w) + rotary embedding of one head held by one warp:
 // lane holds elements d = lane + 32 j, j < hd / 32.  Returns through `o`.
 template <int HD>
-__device__ __forceinline__ void norm_rope_head(const float* x, const void* w, float eps, const void* cosp,
-                                               const void* sinp, int64_t pos, float* o) {
+__device__ __forceinline__ void norm_rope_head(const float* x, const float* w, float eps, const float* cv,
+                                               const float* sv, float* o) {
     constexpr int J = HD / 32;
     const int lane = threadIdx.x & 31;
-    float v[J], wv[J], cv[J], sv[J];
+    float v[J];
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         v[j] = x[lane + 32 * j];
-        wv[j] = bf16_at(w, lane + 32 * j);
-        cv[j] = bf16_at(cosp, pos * HD + lane + 32 * j);
-        sv[j] = bf16_at(sinp, pos * HD + lane + 32 * j);
         ss = fmaf(v[j], v[j], ss);
     }
     ss = warp_sum(ss);
     const float inv = rsqrtf(ss / (float)HD + eps);
 #pragma unroll
-    for (int j = 0; j < J; ++j) v[j] = bf16r(wv[j] * bf16r(v[j] * inv));
+    for (int j = 0; j < J; ++j) v[j] = bf16r(w[lane + 32 * j] * bf16r(v[j] * inv));
     // rotate_half: d < HD/2 -> -v[d + HD/2], else v[d - HD/2]; held by the same lane
 #pragma unroll
     for (int j = 0; j < J; ++j) {
+        const int d = lane + 32 * j;
         const float rot = j < J / 2 ? -v[j + J / 2] : v[j - J / 2];
-        o[j] = bf16r(bf16r(v[j] * cv[j]) + bf16r(rot * sv[j]));
+        o[j] = bf16r(bf16r(v[j] * cv[d]) + bf16r(rot * sv[d]));
     }
 }
 
@@ -190,11 +192,12 @@ __host__ __device__ constexpr int attn_smem_floats(int hd, int rep, int keys_per
          + kAttnWarps * rep * hd           // P V partial of each warp
          + rep * hd                        // P V partial of this CTA
          + rep * keys_per_cta              // scores, then probabilities
-         + 2 * kMaxRep;                    // local max, local sum
+         + 2 * kMaxRep                     // local max, local sum
+         + 4 * hd;                         // q_norm, k_norm, cos and sin rows of pos
 }
 
 template <int HD>
-__global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kAttnThreads)
+__global__ void __cluster_dims__(kAttnCtas, 1, 1) __launch_bounds__(kAttnThreads, 1)
 step_attn_kernel(rvq_attn_args a) {
     constexpr int E = HD / 32;                 // elements per lane in the key loops
     constexpr int RG = 32 / E < kMaxRep ? 32 / E : kMaxRep;   // heads per P V register group
@@ -204,8 +207,10 @@ step_attn_kernel(rvq_attn_args a) {
     const int kv = blockIdx.y;
     const int rep = a.n_heads / a.n_kv;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_launch_dependents();
     const int64_t pos = *a.pos;
     if (pos < 0 || pos >= a.max_len) {               // same decision in every CTA of the cluster
+        pdl_wait();
         for (int i = rank * kAttnThreads + tid; i < rep * HD; i += kAttnCtas * kAttnThreads)
             put_bf16(a.out, (int64_t)kv * rep * HD + i, 0.f);
         return;
@@ -224,10 +229,31 @@ step_attn_kernel(rvq_attn_args a) {
     float* sc = pout + rep * HD;
     float* mloc = sc + rep * kpc_max;
     float* sloc = mloc + kMaxRep;
+    float* wsm = sloc + kMaxRep;                // [4][HD]: q_norm, k_norm, cos[pos], sin[pos]
     __shared__ float red[kMaxRep][kAttnWarps];
     __shared__ float gmax[kMaxRep], gsum[kMaxRep];
 
-    // 1. operands (6 per thread in flight before their stores)
+    // 1. everything that does not depend on q, k, v is requested first: this warp's
+    //    first kKeyChunk K and V rows, the norm weights and this position's cos / sin;
+    //    then the operands (6 per thread in flight before their stores)
+    const int d0 = lane * E;
+    const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache) + (int64_t)kv * a.max_len * HD;
+    const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache) + (int64_t)kv * a.max_len * HD;
+    float kd0[kKeyChunk][E], vd0[kKeyChunk][E];
+#pragma unroll
+    for (int c = 0; c < kKeyChunk; ++c) {
+        const int j = j0 + warp + c * kAttnWarps;
+        if (j < j1 && j != pos) {
+            load_row_slice<E>(kc + (int64_t)j * HD + d0, kd0[c]);
+            load_row_slice<E>(vc + (int64_t)j * HD + d0, vd0[c]);
+        }
+    }
+    for (int i = tid; i < 4 * HD; i += kAttnThreads) {
+        const int which = i / HD, d = i - which * HD;
+        const void* src = which == 0 ? a.q_norm : which == 1 ? a.k_norm : which == 2 ? a.cos : a.sin;
+        wsm[i] = bf16_at(src, (which >= 2 ? pos * HD : 0) + d);
+    }
+    pdl_wait();                                      // q, k, v come from the previous kernel
     for (int base = 0; base < (rep + 2) * HD; base += 6 * kAttnThreads) {
         float val[6];
 #pragma unroll
@@ -253,7 +279,7 @@ step_attn_kernel(rvq_attn_args a) {
     for (int hh = warp; hh <= rep; hh += kAttnWarps) {
         float o[HD / 32];
         const bool is_k = hh == rep;
-        norm_rope_head<HD>(raw + hh * HD, is_k ? a.k_norm : a.q_norm, a.eps, a.cos, a.sin, pos, o);
+        norm_rope_head<HD>(raw + hh * HD, wsm + (is_k ? HD : 0), a.eps, wsm + 2 * HD, wsm + 3 * HD, o);
 #pragma unroll
         for (int j = 0; j < HD / 32; ++j) {
             const int d = lane + 32 * j;
@@ -272,9 +298,6 @@ step_attn_kernel(rvq_attn_args a) {
     __syncthreads();
 
     // 3. scores: warp per key, lanes over head_dim; rows of kKeyChunk keys loaded first
-    const int d0 = lane * E;
-    const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache) + (int64_t)kv * a.max_len * HD;
-    const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache) + (int64_t)kv * a.max_len * HD;
     float mx[kMaxRep];
 #pragma unroll
     for (int r = 0; r < kMaxRep; ++r) mx[r] = -INFINITY;
@@ -283,10 +306,14 @@ step_attn_kernel(rvq_attn_args a) {
 #pragma unroll
         for (int c = 0; c < kKeyChunk; ++c) {
             const int j = jb + c * kAttnWarps;
-            if (j < j1 && j != pos) load_row_slice<E>(kc + (int64_t)j * HD + d0, kd[c]);
-            else {
+            if (j == pos || j >= j1) {
 #pragma unroll
                 for (int e = 0; e < E; ++e) kd[c][e] = knew[d0 + e];
+            } else if (jb == j0 + warp) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) kd[c][e] = kd0[c][e];
+            } else {
+                load_row_slice<E>(kc + (int64_t)j * HD + d0, kd[c]);
             }
         }
 #pragma unroll
@@ -379,10 +406,14 @@ step_attn_kernel(rvq_attn_args a) {
 #pragma unroll
             for (int c = 0; c < kKeyChunk; ++c) {
                 const int j = jb + c * kAttnWarps;
-                if (j < j1 && j != pos) load_row_slice<E>(vc + (int64_t)j * HD + d0, vd[c]);
-                else {
+                if (j == pos || j >= j1) {
 #pragma unroll
                     for (int e = 0; e < E; ++e) vd[c][e] = vnew[d0 + e];
+                } else if (jb == j0 + warp) {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) vd[c][e] = vd0[c][e];
+                } else {
+                    load_row_slice<E>(vc + (int64_t)j * HD + d0, vd[c]);
                 }
             }
 #pragma unroll
@@ -425,6 +456,8 @@ step_attn_kernel(rvq_attn_args a) {
 }
 
 __global__ void step_silu_mul_kernel(rvq_vec g, rvq_vec u, void* out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= g.n) return;
     const float gv = vec_value(g, i);
@@ -456,8 +489,9 @@ int launch_attn(const rvq_attn_args& a, cudaStream_t s) {
     if (cudaFuncSetAttribute(step_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
         return launch_status();
-    step_attn_kernel<HD><<<dim3(kAttnCtas, a.n_kv), kAttnThreads, smem, s>>>(a);
-    return launch_status();
+    const cudaError_t e = launch_pdl(step_attn_kernel<HD>, dim3(kAttnCtas, a.n_kv), dim3(kAttnThreads), smem, s, a);
+    if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
+    return e == cudaSuccess ? launch_status() : RVQ_ERR_CUDA;
 }
 
 }  // namespace
@@ -470,8 +504,10 @@ extern "C" int rvq_step_norm(const rvq_norm_args* a, void* stream) {
     if (a->hidden < 1 || a->hidden > (int64_t)kNormCtas * kNormMaxSlice) return RVQ_ERR_UNSUPPORTED;
     if (a->token != nullptr && (a->embed == nullptr || a->vocab < 1)) return RVQ_ERR_INVALID;
     if (a->token == nullptr && a->add.ptr != nullptr && !vec_ok(a->add, a->hidden)) return RVQ_ERR_INVALID;
-    step_norm_kernel<<<kNormCtas, kNormThreads, 0, (cudaStream_t)stream>>>(*a);
-    return launch_status();
+    const cudaError_t e = launch_pdl(step_norm_kernel, dim3(kNormCtas), dim3(kNormThreads), 0,
+                                     (cudaStream_t)stream, *a);
+    if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
+    return e == cudaSuccess ? launch_status() : RVQ_ERR_CUDA;
 }
 
 extern "C" int rvq_step_attention(const rvq_attn_args* a, void* stream) {
@@ -500,6 +536,8 @@ extern "C" int rvq_step_silu_mul(const rvq_vec* gate, const rvq_vec* up, void* o
     if (!vec_ok(*gate, gate->n) || !vec_ok(*up, gate->n) || gate->n < 1) return RVQ_ERR_INVALID;
     const int threads = 256;
     const unsigned blocks = (unsigned)((gate->n + threads - 1) / threads);
-    step_silu_mul_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(*gate, *up, out);
-    return launch_status();
+    const cudaError_t e = launch_pdl(step_silu_mul_kernel, dim3(blocks), dim3(threads), 0, (cudaStream_t)stream,
+                                     *gate, *up, out);
+    if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
+    return e == cudaSuccess ? launch_status() : RVQ_ERR_CUDA;
 }
