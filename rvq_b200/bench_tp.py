@@ -1,0 +1,129 @@
+"""Tensor-parallel batch-1 generation benchmark: random-init 64-layer model.
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N \\
+        --master-addr 127.0.0.1 --master-port 29511 -m rvq_b200.bench_tp [--layers 64]
+
+Model: hidden 5120, intermediate 25600, 64 query / 8 kv heads of 128, 64
+layers, vocab 151936, tied bf16 embeddings, RoPE theta 1e6; every projection
+RVQ (K=4, 256 codes, d=8, per-row fp16 scales).  q/k/v/gate/up are
+column-parallel, o/down row-parallel followed by an NCCL all-reduce (inside
+the captured CUDA graph).  Each rank generates its own shard on its GPU
+(rank-seeded projections, common-seeded codebooks, norms and embedding), so
+the ranks' shards form one consistent model.  Prompt: 128 seeded ids;
+128 greedy tokens.  Rank 0 prints one JSON object: TTFT, ms/token (device
+time, max over ranks), and per-GPU decode GB/s (the code bytes each GPU
+reads per token / ms per token).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import gc
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+from . import synthetic
+from .decoder import Qwen3Decoder
+
+SHAPE = synthetic.BlockShape(hidden=5120, intermediate=25600, n_heads=64, n_kv_heads=8, head_dim=128)
+
+
+def _max_over_ranks(v: float, device) -> float:
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run(layers=64, prompt_len=128, new=128, vocab=151936, modes=("fused",)):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=180))
+    group = dist.group.WORLD if world > 1 else None
+    cfg = synthetic.qwen3_config(SHAPE, layers, vocab)
+    art = synthetic.make_tp_shard_artifact(SHAPE, layers, vocab, rank, world, seed=0, device=device)
+    prompt = torch.randint(0, vocab, (prompt_len,), generator=torch.Generator().manual_seed(1234)).to(device)
+    per_layer = SHAPE.weights_per_block() // world
+    rows_per_layer = sum(o for _, o, _ in SHAPE.projections())
+    code_bytes = layers * (per_layer // 8 * 4)
+    out = {"workload": f"Qwen3-style {SHAPE.hidden}/{SHAPE.intermediate}/{SHAPE.n_heads}q/{SHAPE.n_kv_heads}kv/"
+                       f"{SHAPE.head_dim} x {layers} layers, vocab {vocab}, K=4 256-code d=8 RVQ, per-row scales, "
+                       f"prompt {prompt_len}, {new} greedy tokens",
+           "tp": world, "data": "synthetic random-init shards generated per rank, seeded", "modes": {}}
+    for mode in modes:
+        dec = Qwen3Decoder(cfg, art, device, mode=mode, max_len=prompt_len + new + 8, tp_group=group,
+                           artifact_is_shard=True)
+        dec.capture()
+        dec.generate(prompt, 4)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ttft = []
+        for _ in range(3):
+            s.record()
+            dec.prefill(prompt).argmax()
+            e.record()
+            torch.cuda.synchronize()
+            ttft.append(s.elapsed_time(e))
+        logits = dec.prefill(prompt)
+        tok = logits.argmax().view(1)
+        toks = [tok]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s.record()
+        pos = prompt_len
+        for _ in range(new - 1):
+            tok = dec.step(tok, pos).argmax().view(1)
+            toks.append(tok)
+            pos += 1
+        e.record()
+        torch.cuda.synchronize()
+        ms_tok = _max_over_ranks(s.elapsed_time(e) / (new - 1), device)
+        ttft_ms = _max_over_ranks(sorted(ttft)[1], device)
+        ids = torch.cat(toks)
+        same = torch.tensor([1.0], device=device)
+        if world > 1:
+            ref = ids.clone()
+            dist.broadcast(ref, 0)
+            same = torch.tensor([float(torch.equal(ref, ids))], device=device)
+            dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        res = {"ttft_ms": round(ttft_ms, 3), "ms_per_token": round(ms_tok, 4),
+               "ranks_agree_on_ids": bool(same.item() == 1.0)}
+        if mode == "fused":
+            res["code_bytes_per_gpu_per_token"] = code_bytes
+            res["per_gpu_decode_GB/s"] = round(code_bytes / (ms_tok * 1e6), 1)
+            res["allreduces_per_token"] = 2 * layers
+        out["modes"][mode] = res
+        del dec                      # releases the graph (it holds NCCL calls) before the group goes
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=64)
+    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--new", type=int, default=128)
+    ap.add_argument("--vocab", type=int, default=151936)
+    ap.add_argument("--modes", default="fused")
+    a = ap.parse_args(argv)
+    res = run(a.layers, a.prompt, a.new, a.vocab, tuple(a.modes.split(",")))
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(res))
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

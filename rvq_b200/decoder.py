@@ -30,10 +30,12 @@ dtype (bf16), rounding at the same points as the HF modules.
 
 from __future__ import annotations
 
+import dataclasses
 from dataclasses import dataclass
 from typing import Dict, List, Optional
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from .engine import LayerDecodePlan, decode_to_tensor
@@ -86,11 +88,14 @@ class Qwen3Decoder:
     """Greedy batch-1 generation.  ``artifact``: the compressor's artifact
     dict (``shared_codebooks``, ``entries``); ``config``: an HF Qwen3 config;
     ``causal``: False reproduces the reference engine's attention mask (see
-    ``_attention``), True the standard causal one."""
+    ``_attention``), True the standard causal one.  ``tp_group``: a NCCL
+    process group to run tensor-parallel over (one rank per GPU); the
+    artifact is the full model, or this rank's shard when
+    ``artifact_is_shard`` (rvq_b200/shard.py layout)."""
 
     def __init__(self, config, artifact, device, mode: str = "fused", max_len: int = 512,
                  runtime_dtype: torch.dtype = torch.bfloat16, causal: bool = False,
-                 step_impl: str = "native"):
+                 step_impl: str = "native", tp_group=None, artifact_is_shard: bool = False):
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
         if step_impl not in ("native", "torch"):
@@ -102,6 +107,17 @@ class Qwen3Decoder:
         self.device = dev = torch.device(device)
         self.dtype = dt = runtime_dtype
         self.dims = d = Dims.from_config(config)
+        # tensor parallelism: column-parallel q/k/v/gate/up, row-parallel o/down
+        # followed by an all-reduce of their outputs (rvq_b200/shard.py)
+        self.tp_group = tp_group
+        self.tp = dist.get_world_size(tp_group) if tp_group is not None else 1
+        if self.tp > 1:
+            from .shard import shard_artifact, sharded_dims
+            rank = dist.get_rank(tp_group)
+            nh, nkv, inter = sharded_dims(d.n_heads, d.n_kv, d.intermediate, self.tp)
+            if not artifact_is_shard:
+                artifact = shard_artifact(artifact, d.n_layers, rank, self.tp)
+            self.dims = d = dataclasses.replace(d, n_heads=nh, n_kv=nkv, intermediate=inter)
         self.max_len = max_len
         self.codebooks = {k: v.to(dev, torch.float32) for k, v in artifact["shared_codebooks"].items()}
         self.entries = {k: {ek: (ev.to(dev) if torch.is_tensor(ev) else ev) for ek, ev in e.items()}
@@ -176,6 +192,12 @@ class Qwen3Decoder:
                                      (E[PROJ[5]], cb(PROJ[5]), self.x_mlp, self.up)])
             L["gemv_d"] = GemvPlan([(E[PROJ[6]], cb(PROJ[6]), self.act, self.down)])
 
+    def _allreduce(self, t: torch.Tensor) -> torch.Tensor:
+        """Sum a row-parallel projection's output over the tensor-parallel ranks."""
+        if self.tp > 1:
+            dist.all_reduce(t, group=self.tp_group)
+        return t
+
     # -- the layer ------------------------------------------------------------------
     def _attention(self, l: int, q, k, v, pos: Optional[torch.Tensor]) -> torch.Tensor:
         """q [T, nh*hd], k/v [T, nkv*hd] -> [T, nh*hd], as HF's eager attention
@@ -243,7 +265,7 @@ class Qwen3Decoder:
             o = self.o.view(1, -1)
         else:
             o = F.linear(a, w[PROJ[3]])
-        h = h + o
+        h = h + self._allreduce(o)
         x = rmsnorm(h, L["post_attention_layernorm.weight"], d.eps)
         if gemv:
             self.x_mlp.copy_(x.view(-1))
@@ -253,7 +275,7 @@ class Qwen3Decoder:
             dn = self.down.view(1, -1)
         else:
             dn = F.linear(F.silu(F.linear(x, w[PROJ[4]])) * F.linear(x, w[PROJ[5]]), w[PROJ[6]])
-        return h + dn
+        return h + self._allreduce(dn)
 
     def _layer_weights(self, slots: bool):
         """Yield (layer, weights) in order.  With ``slots``, layer l+1 is decoded
@@ -366,17 +388,21 @@ class Qwen3Decoder:
             ops["attn"].launch()
             if fused:
                 ops["o"].launch()
+                self._allreduce(self.o_part)
             else:
                 self._mv(w[PROJ[3]], self.attn_out, self.o)
+                self._allreduce(self.o)
             ops["norm2"].launch()
             if fused:
                 ops["gu"].launch()
                 ops["down"].launch()
+                self._allreduce(self.down_part)
             else:
                 self._mv(w[PROJ[4]], self.x_mlp, self.gate)
                 self._mv(w[PROJ[5]], self.x_mlp, self.up)
                 ops["silu"].launch()
                 self._mv(w[PROJ[6]], self.act, self.down)
+                self._allreduce(self.down)
         self.final_op.launch()
         self._mv(self.lm_head, self.x_final, self.logits_buf)
         return self.logits_buf

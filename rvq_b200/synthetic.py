@@ -217,3 +217,42 @@ def make_model_artifact(shape: BlockShape, n_layers: int, vocab: int, seed: int 
                                           group_size=group_size))
     entries["model.norm.weight"] = make_raw_entry(1.0 + 0.02 * torch.randn(shape.hidden, generator=gen))
     return {"format_version": 1, "model_type": "qwen3", "shared_codebooks": cbs, "entries": entries}
+
+
+def make_tp_shard_artifact(shape: BlockShape, n_layers: int, vocab: int, rank: int, tp: int, seed: int = 0,
+                           device="cpu", embed_std: float = 0.02) -> Dict[str, object]:
+    """One rank's shard of a random-init tensor-parallel model, generated on
+    ``device`` without building the full model: q/k/v/gate/up hold this rank's
+    output rows, o/down its input columns (per-rank seed), while codebooks,
+    norms and the tied embedding are replicated (common seed).  The shards of
+    all ranks together are one consistent model."""
+    if shape.n_heads % tp or shape.n_kv_heads % tp or shape.intermediate % tp:
+        raise ValueError("heads and intermediate must split evenly")
+    local = BlockShape(hidden=shape.hidden, intermediate=shape.intermediate // tp,
+                       n_heads=shape.n_heads // tp, n_kv_heads=shape.n_kv_heads // tp, head_dim=shape.head_dim)
+    dev = torch.device(device)
+    common = torch.Generator(device=dev).manual_seed(seed)
+    mine = torch.Generator(device=dev).manual_seed(seed * 1009 + 7919 * (rank + 1))
+    cpu_common = torch.Generator().manual_seed(seed)
+    cbs = make_family_codebooks(cpu_common)
+    entries: Dict[str, Dict[str, object]] = {}
+    embed = torch.randn(vocab, shape.hidden, generator=common, device=dev) * embed_std
+    entries["model.embed_tokens.weight"] = make_raw_entry(embed)
+    del embed
+    for l in range(n_layers):
+        base = f"model.layers.{l}."
+        for name, o, i in local.projections():
+            nvec = o * i // 8
+            e = {
+                "method": "rvq_groupwise", "codebook_id": FAMILY_OF[name], "shape": [o, i],
+                "dtype": "bfloat16", "group_size": int(i), "d": 8, "trimmed_numel": int(o * i),
+                "indices": torch.randint(0, 256, (4, nvec), dtype=torch.uint8, generator=mine, device=dev),
+                "scales": torch.empty(o, device=dev).uniform_(0.5, 1.5, generator=mine).to(torch.float16),
+                "tail": torch.zeros(0, dtype=torch.bfloat16, device=dev), "mse": 0.0, "rel_rmse": 0.0,
+            }
+            entries[base + name] = e
+        for norm, n in (("input_layernorm.weight", shape.hidden), ("post_attention_layernorm.weight", shape.hidden),
+                        ("self_attn.q_norm.weight", shape.head_dim), ("self_attn.k_norm.weight", shape.head_dim)):
+            entries[base + norm] = make_raw_entry(1.0 + 0.02 * torch.randn(n, generator=common, device=dev))
+    entries["model.norm.weight"] = make_raw_entry(1.0 + 0.02 * torch.randn(shape.hidden, generator=common, device=dev))
+    return {"format_version": 1, "model_type": "qwen3", "shared_codebooks": cbs, "entries": entries}
