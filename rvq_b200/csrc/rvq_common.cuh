@@ -65,6 +65,15 @@ __device__ __forceinline__ float add_f16_f32(uint16_t h, float c) {
     return d;
 }
 
+// Both halves of a packed fp16 pair added into two fp32 accumulators, each
+// with one IEEE round-to-nearest add (add.rn.f32.f16 on the register halves:
+// no separate unpacking instructions).
+__device__ __forceinline__ void add_f16x2_f32(float& lo_acc, float& hi_acc, uint32_t w) {
+    asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %2;\n add.rn.f32.f16 %0, lo, %0;\n add.rn.f32.f16 %1, hi, %1;\n}\n"
+        : "+f"(lo_acc), "+f"(hi_acc)
+        : "r"(w));
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, int out_kind) {
     if (out_kind == RVQ_BF16) {
         __nv_bfloat162 v = __floats2bfloat162_rn(a, b);

@@ -182,15 +182,17 @@ __device__ int stage_codebook(const Job& job, uint4* smem) {
 }
 
 // Fast path: u8 indices over 256 codes, fp16 staging with 8 copies, KT = 4
-// stages (the compressor's default), 16-bit output, every vector of every tile complete.  Each warp
+// stages (the compressor's default), 16-bit output (bf16 or fp16 fixed at
+// compile time, so each pack is one conversion), every vector of every tile
+// complete.  The staged fp16 pairs are added into the fp32 accumulators with
+// add.rn.f32.f16 on their register halves (no unpacking instructions).  Each warp
 // walks tiles ta+warp, ta+warp+32, ... and prefetches the next tile's index
 // words and scales while it decodes the current one.  Codes travel by
 // shuffle: lane L loads index word L of a plane (codes of vectors 4L..4L+3)
 // and lane l takes byte (l & 3) of lane 8j + l/4's word for vector 32j + l.
-template <int KT>
+template <int KT, bool OUT_BF16>
 __device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane,
                                          const uint4* smem) {
-    const int out_kind = job.out_kind;
     // the few job fields the loop needs, read once from parameter space
     const uint32_t* idx32 = reinterpret_cast<const uint32_t*>(job.idx);
     const uint32_t plane32 = job.stage_stride >> 2;
@@ -219,23 +221,21 @@ __device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t t
         for (int j = 0; j < kJ; ++j) {
             const uint32_t n = v0 + 32 * j + lane;
             const float s = __half2float(__ushort_as_half(__ldg(scales + fastdiv(n, gv))));
-            float acc[8];
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int k = 0; k < KT; ++k) {
                 const uint32_t c = __byte_perm(__shfl_sync(0xffffffffu, w[k], 8 * j + (lane >> 2)), 0, bsel);
                 const uint4 q = smem[((k * 256u + c) << 3) + cpy];
-                const uint32_t ws[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[2 * i] = add_f16_f32((uint16_t)(ws[i] & 0xFFFFu), k == 0 ? 0.0f : acc[2 * i]);
-                    acc[2 * i + 1] = add_f16_f32((uint16_t)(ws[i] >> 16), k == 0 ? 0.0f : acc[2 * i + 1]);
-                }
+                add_f16x2_f32(acc[0], acc[1], q.x);
+                add_f16x2_f32(acc[2], acc[3], q.y);
+                add_f16x2_f32(acc[4], acc[5], q.z);
+                add_f16x2_f32(acc[6], acc[7], q.w);
             }
             uint4 q;
-            q.x = pack2(__fmul_rn(acc[0], s), __fmul_rn(acc[1], s), out_kind);
-            q.y = pack2(__fmul_rn(acc[2], s), __fmul_rn(acc[3], s), out_kind);
-            q.z = pack2(__fmul_rn(acc[4], s), __fmul_rn(acc[5], s), out_kind);
-            q.w = pack2(__fmul_rn(acc[6], s), __fmul_rn(acc[7], s), out_kind);
+            q.x = pack2(__fmul_rn(acc[0], s), __fmul_rn(acc[1], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
+            q.y = pack2(__fmul_rn(acc[2], s), __fmul_rn(acc[3], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
+            q.z = pack2(__fmul_rn(acc[4], s), __fmul_rn(acc[5], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
+            q.w = pack2(__fmul_rn(acc[6], s), __fmul_rn(acc[7], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
             out[n] = q;
         }
 #pragma unroll
@@ -336,7 +336,8 @@ __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t
     if (mode == GATHER_SMEM_F16 && job.fast_ok) {
         const uint32_t fe = min(e, job.full_tiles);
         if (a < fe) {
-            run_fast<4>(job, a, fe, warp, lane, smem);
+            if (job.out_kind == RVQ_BF16) run_fast<4, true>(job, a, fe, warp, lane, smem);
+            else run_fast<4, false>(job, a, fe, warp, lane, smem);
             g = fe;
         }
     }
