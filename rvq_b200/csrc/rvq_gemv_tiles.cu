@@ -186,8 +186,9 @@ __device__ __forceinline__ float reduce8(const float (&v)[8]) {
 // The tile's table LUT[q][g] = cb[q] . x[8g : 8g + 8], q = stage * 256 + code.
 // ---------------------------------------------------------------------------
 
-// FFMA: warp w builds rows w + 32 j; lane = group.  Four rows' codebook entries
-// are loaded before any of their table entries is stored.
+// FFMA: warp w builds table rows w + 32 j; lane = group.  Four rows'
+// codebook entries are loaded (broadcast) before any of their table entries
+// is stored; each store is one conflict-free 128-byte row.
 __device__ __forceinline__ void build_lut_ffma(float* __restrict__ lut, const float* __restrict__ cbs,
                                                const float* __restrict__ xs) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

@@ -345,27 +345,18 @@ step_attn_kernel(rvq_attn_args a) {
         for (int w = 1; w < kAttnWarps; ++w) m = fmaxf(m, red[tid][w]);
         mloc[tid] = m;
     }
-    cluster.sync();
-
-    // 4. softmax: global max, exponentials, global sum (rank order), bf16 probabilities
-    if (tid < rep) {
-        float m = -INFINITY;
-        for (int c = 0; c < kAttnCtas; ++c) m = fmaxf(m, cluster.map_shared_rank(mloc, c)[tid]);
-        gmax[tid] = m;
-    }
     __syncthreads();
+
+    // 4. softmax with one cluster exchange: each CTA sums exp(s - its own max);
+    //    the global sum rescales those by exp(local max - global max), in rank
+    //    order; probabilities are exp(s - global max) / sum, rounded to bf16
     float sm[kMaxRep];
 #pragma unroll
     for (int r = 0; r < kMaxRep; ++r) sm[r] = 0.f;
     for (int j = j0 + tid; j < j1; j += kAttnThreads) {
 #pragma unroll
-        for (int r = 0; r < kMaxRep; ++r) {
-            if (r < rep) {
-                const float e = expf(sc[r * kpc_max + (j - j0)] - gmax[r]);
-                sc[r * kpc_max + (j - j0)] = e;
-                sm[r] += e;
-            }
-        }
+        for (int r = 0; r < kMaxRep; ++r)
+            if (r < rep) sm[r] += expf(sc[r * kpc_max + (j - j0)] - mloc[r]);
     }
 #pragma unroll
     for (int r = 0; r < kMaxRep; ++r) {
@@ -382,15 +373,22 @@ step_attn_kernel(rvq_attn_args a) {
     }
     cluster.sync();
     if (tid < rep) {
+        float m = -INFINITY;
+        for (int c = 0; c < kAttnCtas; ++c) m = fmaxf(m, cluster.map_shared_rank(mloc, c)[tid]);
         float t = 0.f;
-        for (int c = 0; c < kAttnCtas; ++c) t += cluster.map_shared_rank(sloc, c)[tid];
+        for (int c = 0; c < kAttnCtas; ++c) {
+            const float mc = cluster.map_shared_rank(mloc, c)[tid];
+            const float sc_ = cluster.map_shared_rank(sloc, c)[tid];
+            if (sc_ > 0.f) t += sc_ * expf(mc - m);
+        }
+        gmax[tid] = m;
         gsum[tid] = t;
     }
     __syncthreads();
     for (int j = j0 + tid; j < j1; j += kAttnThreads) {
 #pragma unroll
         for (int r = 0; r < kMaxRep; ++r)
-            if (r < rep) sc[r * kpc_max + (j - j0)] = bf16r(sc[r * kpc_max + (j - j0)] / gsum[r]);
+            if (r < rep) sc[r * kpc_max + (j - j0)] = bf16r(expf(sc[r * kpc_max + (j - j0)] - gmax[r]) / gsum[r]);
     }
     __syncthreads();
 
