@@ -272,6 +272,36 @@ int64_t rvq_gemv_tiles_count(int64_t cols);
 /* Up to 4 jobs in one launch (e.g. q, k and v).  No workspace, no allocation. */
 int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream);
 
+/* Prefill GEMM with the weight decoded into shared memory, never into HBM:
+ *   y[m][n] = bf16( sum_k x[m][k] * W[n][k] )
+ * with W the RVQ entry reconstructed exactly as rvq_decode would (bit-identical
+ * bf16 values) and the products accumulated in fp32 by tcgen05 tensor-core
+ * MMAs in TMEM.  Replaces decode-into-slot + F.linear for a prompt
+ * (infer_compressed_layerwise_triton.py:263, 290-292); no counterpart entry
+ * point in the reference.  W: K=4 stages, 256 codes, uint8 codes in the
+ * interleaved layout of rvq_interleave_codes (weight.indices), fp32 codebook
+ * (16-byte aligned), no tail; k a multiple of 64, n a multiple of 8; x and y
+ * bf16 row-major, 16-byte aligned. */
+typedef struct rvq_gemm_job {
+    rvq_entry weight;         /* weight.out is ignored */
+    const void* x;            /* device, [m][k] */
+    void* y;                  /* device, [m][n] */
+    int64_t m;
+    int64_t n;
+    int64_t k;
+    int32_t x_kind;           /* RVQ_BF16 */
+    int32_t y_kind;           /* RVQ_BF16 */
+} rvq_gemm_job;
+
+int rvq_gemm_prefill(const rvq_gemm_job* job, void* stream);
+
+/* Reads and clears the sticky flag set when an rvq_gemm_prefill or
+ * rvq_gemv_tiles wait on an mbarrier gave up (bounded waits; the result of
+ * that launch is then invalid).  Synchronises the current device.
+ * Returns 1 if set, 0 if not, or -RVQ_ERR_CUDA. */
+int rvq_take_gemm_timeout(void);
+int rvq_take_wait_timeout(void);
+
 /* Reads and clears the sticky device flag that kernels set when an index is
  * outside [0, ncodes) (the decoded element then uses code 0).  Synchronises
  * the current device.  Returns 1 if the flag was set, 0 if not, or -RVQ_ERR_CUDA. */

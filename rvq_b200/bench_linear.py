@@ -25,6 +25,7 @@ import torch
 
 from . import synthetic
 from .engine import LayerDecodePlan
+from .gemm import GemmPlan
 from .gemv import GemvPlan, GemvTilesPlan, interleave_codes, tiles_count
 
 ROWS, COLS = 9728, 2560
@@ -117,6 +118,13 @@ def run(reps: int = 200, device="cuda:0"):
             torch.matmul(x, dense[i % COPIES].t(), out=y)
 
         r = reps if b < 2048 else max(20, reps // 10)
+        if b >= 64:
+            # prefill-style: weight decoded into shared memory feeding tcgen05 MMAs
+            y_fg = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)
+            gplans = [GemmPlan(c, cbd, x, y_fg) for c in il]
+            t_fg = _time(lambda i: gplans[i % COPIES].launch(), r, stream)
+            out["results"][f"fused_gemm_b{b}"] = {"us": round(t_fg, 2),
+                                                  "TFLOP/s": round(2.0 * b * ROWS * COLS / t_fg / 1e6, 2)}
         t_dg = _time(dec_gemm, r, stream)
         t_dn = _time(dense_mm, r, stream)
         flops = 2.0 * b * ROWS * COLS
