@@ -337,6 +337,11 @@ class Qwen3Decoder:
             self.gate_part, self.up_part = part(d.intermediate, d.hidden), part(d.intermediate, d.hidden)
             self.down_part = part(d.hidden, d.intermediate)
             q, k, v, o, down = self.q_part, self.k_part, self.v_part, self.o_part, self.down_part
+            if self.tp > 1:
+                # row-parallel outputs: tiles summed locally, then one fp32 vector all-reduced
+                self.o_red = torch.zeros(d.hidden, dtype=torch.float32, device=dev)
+                self.down_red = torch.zeros(d.hidden, dtype=torch.float32, device=dev)
+                o, down = self.o_red, self.down_red
         else:
             q, k, v, o, down = self.q, self.k, self.v, self.o, self.down
         tiles = lambda t: t.shape[0] if t.dim() == 2 else 1
@@ -388,7 +393,9 @@ class Qwen3Decoder:
             ops["attn"].launch()
             if fused:
                 ops["o"].launch()
-                self._allreduce(self.o_part)
+                if self.tp > 1:
+                    torch.sum(self.o_part, 0, out=self.o_red)
+                    self._allreduce(self.o_red)
             else:
                 self._mv(w[PROJ[3]], self.attn_out, self.o)
                 self._allreduce(self.o)
@@ -396,7 +403,9 @@ class Qwen3Decoder:
             if fused:
                 ops["gu"].launch()
                 ops["down"].launch()
-                self._allreduce(self.down_part)
+                if self.tp > 1:
+                    torch.sum(self.down_part, 0, out=self.down_red)
+                    self._allreduce(self.down_red)
             else:
                 self._mv(w[PROJ[4]], self.x_mlp, self.gate)
                 self._mv(w[PROJ[5]], self.x_mlp, self.up)
