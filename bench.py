@@ -57,6 +57,8 @@ def parse_args():
                     help="CPU-baseline sample budget (rank 0, N=1)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch1", action="store_true",
+                    help="skip the batch-1 generation ms/token leg")
     return ap.parse_args()
 
 
@@ -342,6 +344,28 @@ def time_e2e(rel, cbs_host, device, steps, warmup, stream):
     return start.elapsed_time(end), h2d, d2h, launches * steps
 
 
+def batch1_leg(world, device):
+    """Batch-1 greedy generation, ms/token (the metric's second half).  N=1:
+    the 36-layer 2560/9728 model (fused RVQ GEMV and the dense bf16 model)
+    and the 64-layer 5120/25600 model; N>1: the 64-layer model tensor-parallel
+    over the N GPUs (NCCL all-reduce after the row-parallel projections)."""
+    from rvq_b200 import bench_tp, synthetic
+    out = {"prompt_tokens": 128, "new_tokens": 128, "timing": "device time per token, max over ranks",
+           "data": "synthetic random-init weights generated on the GPU, seeded"}
+    try:
+        group = torch.distributed.group.WORLD if world > 1 else None
+        if world == 1:
+            c2 = synthetic.BlockShape()
+            out["config2_36_layers"] = {
+                "fused": bench_tp.measure(c2, 36, 151936, "fused", device),
+                "dense_bf16": bench_tp.measure(c2, 36, 151936, "dense", device)}
+        out[f"config4_64_layers_tp{world}"] = {"fused": bench_tp.measure(bench_tp.SHAPE, 64, 151936, "fused",
+                                                                        device, group)}
+    except Exception as exc:                     # reported in the line; the decode figures above stand
+        out["error"] = f"{type(exc).__name__}: {exc}"[:300]
+    return out
+
+
 def run_ours(args, world, rank, local):
     from rvq_b200 import _native
     device = torch.device("cuda", local)
@@ -396,6 +420,10 @@ def run_ours(args, world, rank, local):
                "sample": f"{reps} full config-1 block decode(s) ({algo} algorithmic bytes each), "
                          f"C/OpenMP port of the reference reconstruction, bf16 out, {el:.1f} s"}
 
+    batch1 = None
+    if not args.no_batch1:
+        batch1 = batch1_leg(world, device)
+
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -421,6 +449,7 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
+        "batch1": batch1,
     }
     print(json.dumps(line), flush=True)
 

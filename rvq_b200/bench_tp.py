@@ -39,6 +39,58 @@ def _max_over_ranks(v: float, device) -> float:
     return float(t.item())
 
 
+def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=128, seed=0):
+    """TTFT and ms/token (device time, max over the group's ranks) of greedy
+    generation for the rank's shard of a random model of ``shape``."""
+    world = dist.get_world_size(group) if group is not None else 1
+    rank = dist.get_rank(group) if group is not None else 0
+    cfg = synthetic.qwen3_config(shape, layers, vocab)
+    art = synthetic.make_tp_shard_artifact(shape, layers, vocab, rank, world, seed=seed, device=device)
+    prompt = torch.randint(0, vocab, (prompt_len,), generator=torch.Generator().manual_seed(1234)).to(device)
+    dec = Qwen3Decoder(cfg, art, device, mode=mode, max_len=prompt_len + new + 8, tp_group=group,
+                       artifact_is_shard=True)
+    del art
+    dec.capture()
+    dec.generate(prompt, 4)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ttft = []
+    for _ in range(3):
+        s.record()
+        dec.prefill(prompt).argmax()
+        e.record()
+        torch.cuda.synchronize()
+        ttft.append(s.elapsed_time(e))
+    tok = dec.prefill(prompt).argmax().view(1)
+    toks = [tok]
+    if world > 1:
+        dist.barrier(group)
+    torch.cuda.synchronize()
+    s.record()
+    pos = prompt_len
+    for _ in range(new - 1):
+        tok = dec.step(tok, pos).argmax().view(1)
+        toks.append(tok)
+        pos += 1
+    e.record()
+    torch.cuda.synchronize()
+    ms_tok = _max_over_ranks(s.elapsed_time(e) / (new - 1), device)
+    ttft_ms = _max_over_ranks(sorted(ttft)[1], device)
+    ids = torch.cat(toks)
+    same = True
+    if world > 1:
+        ref = ids.clone()
+        dist.broadcast(ref, 0, group=group)
+        flag = torch.tensor([float(torch.equal(ref, ids))], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        same = bool(flag.item() == 1.0)
+    del dec                          # releases the graph (it holds NCCL calls) before the group goes
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {"ttft_ms": round(ttft_ms, 3), "ms_per_token": round(ms_tok, 4), "ranks_agree_on_ids": same}
+
+
 def run(layers=64, prompt_len=128, new=128, vocab=151936, modes=("fused",)):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -48,64 +100,19 @@ def run(layers=64, prompt_len=128, new=128, vocab=151936, modes=("fused",)):
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=180))
     group = dist.group.WORLD if world > 1 else None
-    cfg = synthetic.qwen3_config(SHAPE, layers, vocab)
-    art = synthetic.make_tp_shard_artifact(SHAPE, layers, vocab, rank, world, seed=0, device=device)
-    prompt = torch.randint(0, vocab, (prompt_len,), generator=torch.Generator().manual_seed(1234)).to(device)
     per_layer = SHAPE.weights_per_block() // world
-    rows_per_layer = sum(o for _, o, _ in SHAPE.projections())
     code_bytes = layers * (per_layer // 8 * 4)
     out = {"workload": f"Qwen3-style {SHAPE.hidden}/{SHAPE.intermediate}/{SHAPE.n_heads}q/{SHAPE.n_kv_heads}kv/"
                        f"{SHAPE.head_dim} x {layers} layers, vocab {vocab}, K=4 256-code d=8 RVQ, per-row scales, "
                        f"prompt {prompt_len}, {new} greedy tokens",
            "tp": world, "data": "synthetic random-init shards generated per rank, seeded", "modes": {}}
     for mode in modes:
-        dec = Qwen3Decoder(cfg, art, device, mode=mode, max_len=prompt_len + new + 8, tp_group=group,
-                           artifact_is_shard=True)
-        dec.capture()
-        dec.generate(prompt, 4)
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ttft = []
-        for _ in range(3):
-            s.record()
-            dec.prefill(prompt).argmax()
-            e.record()
-            torch.cuda.synchronize()
-            ttft.append(s.elapsed_time(e))
-        logits = dec.prefill(prompt)
-        tok = logits.argmax().view(1)
-        toks = [tok]
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        s.record()
-        pos = prompt_len
-        for _ in range(new - 1):
-            tok = dec.step(tok, pos).argmax().view(1)
-            toks.append(tok)
-            pos += 1
-        e.record()
-        torch.cuda.synchronize()
-        ms_tok = _max_over_ranks(s.elapsed_time(e) / (new - 1), device)
-        ttft_ms = _max_over_ranks(sorted(ttft)[1], device)
-        ids = torch.cat(toks)
-        same = torch.tensor([1.0], device=device)
-        if world > 1:
-            ref = ids.clone()
-            dist.broadcast(ref, 0)
-            same = torch.tensor([float(torch.equal(ref, ids))], device=device)
-            dist.all_reduce(same, op=dist.ReduceOp.MIN)
-        res = {"ttft_ms": round(ttft_ms, 3), "ms_per_token": round(ms_tok, 4),
-               "ranks_agree_on_ids": bool(same.item() == 1.0)}
+        res = measure(SHAPE, layers, vocab, mode, device, group, prompt_len, new)
         if mode == "fused":
             res["code_bytes_per_gpu_per_token"] = code_bytes
-            res["per_gpu_decode_GB/s"] = round(code_bytes / (ms_tok * 1e6), 1)
-            res["allreduces_per_token"] = 2 * layers
+            res["per_gpu_decode_GB/s"] = round(code_bytes / (res["ms_per_token"] * 1e6), 1)
+            res["allreduces_per_token"] = 2 * layers if world > 1 else 0
         out["modes"][mode] = res
-        del dec                      # releases the graph (it holds NCCL calls) before the group goes
-        gc.collect()
-        torch.cuda.synchronize()
-        torch.cuda.empty_cache()
     return out
 
 
