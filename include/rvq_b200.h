@@ -204,6 +204,14 @@ typedef struct rvq_norm_args {
     int64_t hidden;
     float eps;
     int32_t vocab;            /* rows of embed; a token outside [0, vocab) reads row 0 */
+    /* Tensor-parallel landing buffer (rvq_tp_push): when `arrivals` is set, the
+     * kernel first waits (bounded) until *arrivals has advanced by
+     * arrivals_per_use past *consumed, reads `add` (the [tp][hidden] fp32
+     * landing buffer, ntiles = tp) through L2, and then advances *consumed. */
+    const uint32_t* arrivals; /* device; NULL: no wait */
+    uint32_t* consumed;       /* device, this rank's count of arrivals already used */
+    uint32_t arrivals_per_use;
+    int32_t reserved;
 } rvq_norm_args;
 
 int rvq_step_norm(const rvq_norm_args* a, void* stream);
@@ -240,6 +248,43 @@ typedef struct rvq_attn_args {
 
 int rvq_step_attention(const rvq_attn_args* a, void* stream);
 
+/* ---- Tensor parallelism over NVLink peer memory -----------------------------
+ * The all-reduce after a row-parallel projection as one push kernel: each
+ * rank sums its own projection output (fp32 partials [tiles][n] in tile order,
+ * or a bf16 vector) and stores the fp32 result into slot [rank] of every
+ * rank's landing buffer [tp][n] by plain peer stores over NVLink, then adds
+ * rvq_tp_push_ctas(n) to every rank's arrival counter (system-scope release).
+ * The consumer (rvq_step_norm with `arrivals` set) waits for all ranks and
+ * sums the tp slots in rank order, so every rank computes the same bits.
+ * Buffers and counters come from rvq_p2p_alloc on each rank and reach the
+ * other ranks through rvq_ipc_export / rvq_ipc_import.  No counterpart in the
+ * reference (it runs on one GPU). */
+#define RVQ_MAX_TP 8
+
+typedef struct rvq_tp_push_args {
+    rvq_vec src;                      /* this rank's projection output, [n] */
+    float* dst[RVQ_MAX_TP];           /* rank r's landing buffer [tp][n] (own rank: local pointer) */
+    uint32_t* arrivals[RVQ_MAX_TP];   /* rank r's arrival counter */
+    int64_t n;
+    int32_t rank;
+    int32_t tp;
+} rvq_tp_push_args;
+
+/* Arrivals one rank's push adds to every counter (its CTA count for n). */
+uint32_t rvq_tp_push_ctas(int64_t n);
+int rvq_tp_push(const rvq_tp_push_args* a, void* stream);
+
+/* Zero-filled device memory for landing buffers and counters (cudaMalloc). */
+int rvq_p2p_alloc(size_t bytes, void** out);
+int rvq_p2p_free(void* ptr);
+/* 64-byte IPC handle of an rvq_p2p_alloc allocation, and its mapping in
+ * another process on the same node (peer access enabled). */
+int rvq_ipc_export(void* ptr, void* handle64);
+int rvq_ipc_import(const void* handle64, void** out);
+int rvq_ipc_close(void* ptr);
+/* Reads and clears the sticky flag set when a landing-buffer wait gave up. */
+int rvq_take_tp_timeout(void);
+
 /* out = bf16(bf16(silu(gate)) * up), [n] bf16 (Qwen3MLP's act_fn(gate) * up). */
 int rvq_step_silu_mul(const rvq_vec* gate, const rvq_vec* up, void* out, void* stream);
 
@@ -253,9 +298,9 @@ int rvq_step_silu_mul(const rvq_vec* gate, const rvq_vec* up, void* out, void* s
  * order: deterministic, and no reduction launch or cross-CTA fence.
  * No counterpart in the reference (it reconstructs W into the slot and calls
  * F.linear: infer_compressed_layerwise_triton.py:290-292).
- * W: K=4, 256 codes, uint8 codes in the interleaved layout of
- * rvq_interleave_codes (weight.indices, 4-byte aligned), no tail, d = 8,
- * cols a multiple of 8; codebook fp32 (16-byte aligned), fp16 or bf16. */
+ * W: K=4, 256 codes, uint8 codes in the tile-major layout of rvq_tile_codes
+ * (weight.indices, 16-byte aligned), no tail, d = 8, cols a multiple of 8;
+ * codebook fp32 (16-byte aligned), fp16 or bf16. */
 typedef struct rvq_gemv_tile_job {
     rvq_entry weight;         /* weight.out is ignored */
     rvq_vec x;                /* [cols] operand */
@@ -271,6 +316,16 @@ int64_t rvq_gemv_tiles_count(int64_t cols);
 
 /* Up to 4 jobs in one launch (e.g. q, k and v).  No workspace, no allocation. */
 int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream);
+
+/* Repack uint8 code planes [4][stage_stride] of a rows x cols weight into the
+ * tile-major layout rvq_gemv_tiles reads: [tiles][rows][32] 32-bit words, word
+ * (t, r, w) = the 4 stage codes (stage k in byte k) of vector (r, 32 t + w),
+ * zero past the last vector of a row.  Every 256-column tile's rows are then
+ * one contiguous range of 128-byte lines.  `out` holds rvq_tile_codes_bytes()
+ * bytes, 16-byte aligned.  A layout of this library, not of the reference
+ * artifact. */
+int64_t rvq_tile_codes_bytes(int64_t rows, int64_t cols);
+int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64_t cols, void* out, void* stream);
 
 /* Prefill GEMM with the weight decoded into shared memory, never into HBM:
  *   y[m][n] = bf16( sum_k x[m][k] * W[n][k] )

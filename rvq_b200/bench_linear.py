@@ -26,7 +26,7 @@ import torch
 from . import synthetic
 from .engine import LayerDecodePlan
 from .gemm import GemmPlan
-from .gemv import GemvPlan, GemvTilesPlan, interleave_codes, tiles_count
+from .gemv import GemvPlan, GemvTilesPlan, interleave_codes, tile_codes, tiles_count
 
 ROWS, COLS = 9728, 2560
 COPIES = 16
@@ -82,7 +82,8 @@ def run(reps: int = 200, device="cuda:0"):
 
     # per-tile partials (the form the decode step consumes), and with the tile sum
     parts = [torch.empty(tiles_count(COLS), ROWS, dtype=torch.float32, device=device) for _ in range(COPIES)]
-    tplans = [GemvTilesPlan([(c, cbd, x1, p)]) for c, p in zip(il, parts)]
+    tl = [dict(c, codes_tiled=tile_codes(c["indices"], ROWS, COLS)) for c in copies]
+    tplans = [GemvTilesPlan([(c, cbd, x1, p)]) for c, p in zip(tl, parts)]
     t = _time(lambda i: tplans[i % COPIES].launch(), reps, stream)
     out["results"]["fused_tiles_b1"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
                                         "algorithmic_bytes": algo, "output": "fp32 partials [10, rows]"}

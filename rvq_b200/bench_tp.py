@@ -6,8 +6,9 @@
 Model: hidden 5120, intermediate 25600, 64 query / 8 kv heads of 128, 64
 layers, vocab 151936, tied bf16 embeddings, RoPE theta 1e6; every projection
 RVQ (K=4, 256 codes, d=8, per-row fp16 scales).  q/k/v/gate/up are
-column-parallel, o/down row-parallel followed by an NCCL all-reduce (inside
-the captured CUDA graph).  Each rank generates its own shard on its GPU
+column-parallel, o/down row-parallel; their outputs are summed over the
+ranks inside the captured CUDA graph, by peer stores into landing buffers
+("push", rvq_b200/tp.py) or by an NCCL all-reduce ("nccl"; ``--reduce``).  Each rank generates its own shard on its GPU
 (rank-seeded projections, common-seeded codebooks, norms and embedding), so
 the ranks' shards form one consistent model.  Prompt: 128 seeded ids;
 128 greedy tokens.  Rank 0 prints one JSON object: TTFT, ms/token (device
@@ -39,7 +40,7 @@ def _max_over_ranks(v: float, device) -> float:
     return float(t.item())
 
 
-def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=128, seed=0):
+def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=128, seed=0, tp_reduce="push"):
     """TTFT and ms/token (device time, max over the group's ranks) of greedy
     generation for the rank's shard of a random model of ``shape``."""
     world = dist.get_world_size(group) if group is not None else 1
@@ -48,7 +49,7 @@ def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=
     art = synthetic.make_tp_shard_artifact(shape, layers, vocab, rank, world, seed=seed, device=device)
     prompt = torch.randint(0, vocab, (prompt_len,), generator=torch.Generator().manual_seed(1234)).to(device)
     dec = Qwen3Decoder(cfg, art, device, mode=mode, max_len=prompt_len + new + 8, tp_group=group,
-                       artifact_is_shard=True)
+                       artifact_is_shard=True, tp_reduce=tp_reduce)
     del art
     dec.capture()
     dec.generate(prompt, 4)
@@ -84,14 +85,15 @@ def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=
         flag = torch.tensor([float(torch.equal(ref, ids))], device=device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
         same = bool(flag.item() == 1.0)
-    del dec                          # releases the graph (it holds NCCL calls) before the group goes
+    dec.close()                      # releases the graph (it may hold NCCL calls) and the landing buffers
+    del dec
     gc.collect()
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return {"ttft_ms": round(ttft_ms, 3), "ms_per_token": round(ms_tok, 4), "ranks_agree_on_ids": same}
 
 
-def run(layers=64, prompt_len=128, new=128, vocab=151936, modes=("fused",)):
+def run(layers=64, prompt_len=128, new=128, vocab=151936, modes=("fused",), reduces=("push",)):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -107,12 +109,15 @@ def run(layers=64, prompt_len=128, new=128, vocab=151936, modes=("fused",)):
                        f"prompt {prompt_len}, {new} greedy tokens",
            "tp": world, "data": "synthetic random-init shards generated per rank, seeded", "modes": {}}
     for mode in modes:
-        res = measure(SHAPE, layers, vocab, mode, device, group, prompt_len, new)
-        if mode == "fused":
-            res["code_bytes_per_gpu_per_token"] = code_bytes
-            res["per_gpu_decode_GB/s"] = round(code_bytes / (res["ms_per_token"] * 1e6), 1)
-            res["allreduces_per_token"] = 2 * layers if world > 1 else 0
-        out["modes"][mode] = res
+        for reduce in (reduces if world > 1 else ("push",)):
+            res = measure(SHAPE, layers, vocab, mode, device, group, prompt_len, new, tp_reduce=reduce)
+            if mode == "fused":
+                res["code_bytes_per_gpu_per_token"] = code_bytes
+                res["per_gpu_decode_GB/s"] = round(code_bytes / (res["ms_per_token"] * 1e6), 1)
+            if world > 1:
+                res["reductions_per_token"] = 2 * layers
+                res["tp_reduce"] = reduce
+            out["modes"][mode if world == 1 or len(reduces) == 1 else f"{mode}+{reduce}"] = res
     return out
 
 
@@ -123,8 +128,9 @@ def main(argv=None):
     ap.add_argument("--new", type=int, default=128)
     ap.add_argument("--vocab", type=int, default=151936)
     ap.add_argument("--modes", default="fused")
+    ap.add_argument("--reduce", default="push", help="push, nccl or push,nccl")
     a = ap.parse_args(argv)
-    res = run(a.layers, a.prompt, a.new, a.vocab, tuple(a.modes.split(",")))
+    res = run(a.layers, a.prompt, a.new, a.vocab, tuple(a.modes.split(",")), tuple(a.reduce.split(",")))
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(res))
     if dist.is_initialized():

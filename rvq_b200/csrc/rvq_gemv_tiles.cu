@@ -8,20 +8,29 @@
 // 3 adds.  The reference has no fused path (it reconstructs W into the slot
 // and calls F.linear, infer_compressed_layerwise_triton.py:290-292).
 //
-// One CTA owns one (job, tile, row range) unit.  Its rows' code words
-// (interleaved layout, one 32-bit word per vector) stream into a two-slot
-// shared-memory ring, 256 rows per TMA tile load (cp.async.bulk.tensor, zero
-// fill past the matrix edge), while the CTA builds the tile's 128 KB table
-// (4 stages x 256 codes x 32 groups, fp32, [stage][code][group]: lane g always
-// reads bank g, so the random-code lookups never conflict).  Rows are reduced 8
-// at a time with a warp reduce-scatter.  Nothing is shared between CTAs:
-// partial sums go to [ntiles][rows] and the consumer adds them in tile order,
-// so the result is deterministic and no cross-CTA synchronisation is needed.
-// Matrices whose rows are not 16-byte aligned (cols / 8 not a multiple of 4)
-// are staged with 4-byte cp.async instead of TMA.
-
-#include <cuda.h>
-#include <cudaTypedefs.h>
+// A unit is one (job, tile, row range).  Its rows' code words (one
+// 32-bit word per vector, stored tile-major by rvq_tile_codes so that a tile's
+// rows are contiguous 128-byte lines) stream into a four-slot shared-memory
+// ring, 256 rows (32 KB, one contiguous range) per bulk copy (cp.async.bulk),
+// while the CTA builds the tile's 64 KB table (4 stages x 256 codes x 32
+// groups, fp16).  Each CTA owns a contiguous run of (job, tile, row range)
+// units sized so that every CTA has the same work, counting a table build as
+// kSwitchRows rows; the codebook stays in shared memory across units of one
+// job.
+//
+// Table: x is first scaled by a power of two 2^-E so that max |x| over the
+// tile lies in [1, 2) (exact), every entry is rounded once to fp16 (relative
+// error <= 2^-11, below the 2^-8 of a bf16 weight), and each row's tile sum
+// is multiplied back by 2^E.  Entries are accumulated in fp32 (add.rn.f32.f16).
+// Layout [code][stage / 2][group][stage % 2]: the 32-bit word (code, pair,
+// group) holds the entries of stages 2 pair and 2 pair + 1, lane g always reads
+// bank g (conflict-free random-code lookups), and the byte offset of an entry,
+// code << 8 | (stage / 2) << 7 | g << 2 | (stage % 2) << 1, takes one byte
+// permute (prmt) of the code word.
+//
+// Rows are reduced 8 at a time with a warp reduce-scatter.  Nothing is shared
+// between CTAs: partial sums go to [ntiles][rows] and the consumer adds them in
+// tile order, so the result is deterministic and needs no cross-CTA sync.
 
 #include <mutex>
 #include <string.h>
@@ -37,22 +46,27 @@ constexpr int kGroups = 32;                                 // 8-element groups 
 constexpr int kTileCols = kGroups * 8;                      // 256 columns
 constexpr int kStages = 4;
 constexpr int kCodes = 256;
-constexpr int kPairs = kStages * kCodes;                    // (stage, code) table rows
-constexpr int kLutFloats = kPairs * kGroups;                // 32768 floats, 128 KB
+constexpr int kPairs = kStages * kCodes;                    // (stage, code) codebook rows
+constexpr int kLutWords = kCodes * (kStages / 2) * kGroups; // 16384 words (2 fp16 entries each), 64 KB
 constexpr int kCbFloats = kPairs * 8;                       // codebook, fp32, 32 KB
-constexpr int kBatchRows = 256;                             // rows per staged batch (TMA box height)
-constexpr int kRing = 2;                                    // batches in flight
-constexpr uint32_t kBatchBytes = kBatchRows * kGroups * 4;  // 32 KB
+constexpr int kBatchRows = 256;                             // rows per staged batch
+constexpr int kRing = 4;                                    // ring slots
 constexpr int kMaxJobs = 4;
 constexpr int kMaxUnits = 1024;
+constexpr int kMaxCtas = 160;
+constexpr int kSwitchRows = 768;                            // starting a unit (table build, first batch) ~ 768 rows
 constexpr long long kWaitLimit = 1ll << 22;                 // mbarrier polls before giving up
+constexpr int kLineWords = 32;                              // code words per row of a tile (128 B)
+// [table 64 KB][codebook 32 KB][ring slots 0..3][x slice][barriers]
 constexpr size_t kSmemBytes =
-    (size_t)(kLutFloats + kCbFloats + kRing * kBatchRows * kGroups + kTileCols) * 4 + 64;
+    (size_t)(kLutWords + kCbFloats + kRing * kBatchRows * kGroups + kTileCols) * 4 + 64;
+// operand partial tiles staged in the table's space before the table is built
+constexpr int kMaxStagedTiles = kLutWords / kTileCols;
 
 __device__ int g_wait_timeout;                              // sticky: a TMA wait gave up
 
 struct TJob {
-    const uint32_t* codes;      // [rows][G] interleaved code words
+    const uint32_t* codes;      // [ntiles][rows][32] code words (rvq_tile_codes)
     const void* cb;             // [4][256][8]
     const void* scales;
     rvq_vec x;                  // operand (or the "up" half when gate is set)
@@ -66,14 +80,13 @@ struct TJob {
     int32_t row_scales;         // 1: scale index = row / rows_per_scale
     int32_t cb_kind;
     int32_t scale_kind;
-    int32_t use_tma;            // rows 16-byte aligned: TMA tile loads through maps[job]
 };
 
 struct TParams {
-    CUtensorMap maps[kMaxJobs];   // [rows][G] uint32, box 32 x 256 (64-byte aligned, first)
     TJob jobs[kMaxJobs];
     int32_t n_units;
-    int32_t pad;
+    int32_t n_ctas;
+    int32_t cta_first[kMaxCtas + 1];  // CTA c runs units [cta_first[c], cta_first[c + 1])
     uint32_t unit_jt[kMaxUnits];  // job << 24 | tile
     int32_t unit_r0[kMaxUnits];
     int32_t unit_r1[kMaxUnits];
@@ -91,14 +104,63 @@ __device__ __forceinline__ float operand(const rvq_vec& v, int64_t i) {
     return load_as_f32(v.ptr, i, v.kind);
 }
 
+// All ntiles x 256 partials of the tile's operand slice into dst[t][c] (zero
+// past the matrix edge), 8 independent loads per thread in flight.
+__device__ __forceinline__ void stage_partials(const rvq_vec& v, int tile, int64_t cols, float* dst) {
+    const float* p = reinterpret_cast<const float*>(v.ptr);
+    const int total = v.ntiles * kTileCols;
+    for (int i0 = threadIdx.x; i0 < total; i0 += 8 * kThreads) {
+        float r[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = i0 + k * kThreads;
+            const int t = i >> 8;
+            const int64_t col = (int64_t)tile * kTileCols + (i & (kTileCols - 1));
+            r[k] = (i < total && col < cols) ? __ldg(p + (int64_t)t * v.n + col) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (i0 + k * kThreads < total) dst[i0 + k * kThreads] = r[k];
+    }
+}
+
+// The tile-ordered sum of staged partials for column c, rounded to bf16.
+__device__ __forceinline__ float staged_value(const float* src, int ntiles, int c) {
+    float s = src[c];
+    for (int t = 1; t < ntiles; ++t) s += src[t * kTileCols + c];
+    return bf16r(s);
+}
+
+// Byte offset in the table of the entry for the code in byte K of `w`;
+// `lane_bits` = (K / 2) << 7 | lane << 2 | (K % 2) << 1.
+template <int K>
+__device__ __forceinline__ uint32_t lut_offset(uint32_t w, uint32_t lane_bits) {
+    return __byte_perm(w, lane_bits, 0x7604 | (K << 4));
+}
+
+__device__ __forceinline__ unsigned short lut_entry(const uint32_t* lut, uint32_t byte_offset) {
+    return *reinterpret_cast<const unsigned short*>(reinterpret_cast<const char*>(lut) + byte_offset);
+}
+
+// acc + entry, one fp32 round-to-nearest add of the fp16 entry.
+__device__ __forceinline__ float add_entry(float acc, unsigned short h) {
+    asm("add.rn.f32.f16 %0, %1, %0;" : "+f"(acc) : "h"(h));
+    return acc;
+}
+
+// The four stage entries of one code word, summed in stage order.
+__device__ __forceinline__ float lookup4(const uint32_t* lut, uint32_t w, uint32_t lb0, uint32_t lb1, uint32_t lb2,
+                                         uint32_t lb3) {
+    float s = __half2float(__ushort_as_half(lut_entry(lut, lut_offset<0>(w, lb0))));
+    s = add_entry(s, lut_entry(lut, lut_offset<1>(w, lb1)));
+    s = add_entry(s, lut_entry(lut, lut_offset<2>(w, lb2)));
+    return add_entry(s, lut_entry(lut, lut_offset<3>(w, lb3)));
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
@@ -135,24 +197,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
-// One 32 x 256 box of code words (tile columns x rows) into shared memory.
-__device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    mbar_expect_tx(bar, kBatchBytes);
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
-        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
-        : "memory");
+// `bytes` (a multiple of 16) of contiguous code words into shared memory,
+// completing on the mbarrier.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    mbar_expect_tx(bar, bytes);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 
-// Fallback staging: rows [r0, r1) of a tile, 4 bytes at a time; one commit group.
-__device__ __forceinline__ void stage_batch_words(const TJob& J, int tile, int gt, int r0, int r1, uint32_t* dst) {
-    const int nrows = r1 - r0;
-    const uint32_t* src = J.codes + (int64_t)r0 * J.G + (int64_t)tile * kGroups;
-    for (int i = threadIdx.x; i < nrows * gt; i += kThreads) {
-        const int r = i / gt, g = i - r * gt;
-        cp_async4(dst + r * kGroups + g, src + (int64_t)r * J.G + g);
-    }
-    cp_async_commit();
+// Rows [r, r + n) of a tile's code lines into ring slot `dst`.
+__device__ __forceinline__ void load_batch(uint32_t dst, const uint32_t* lines, int r, int n, uint32_t bar) {
+    bulk_load(dst, lines + (int64_t)r * kLineWords, (uint32_t)n * kLineWords * 4, bar);
 }
 
 // Reduce 8 per-lane values (rows 0..7) over the warp: returns the total of row
@@ -183,26 +239,28 @@ __device__ __forceinline__ float reduce8(const float (&v)[8]) {
 }
 
 // ---------------------------------------------------------------------------
-// The tile's table LUT[q][g] = cb[q] . x[8g : 8g + 8], q = stage * 256 + code.
+// The tile's table: word (c, pair, g) = fp16 pair (cb[2 pair][c] . x'_g,
+// cb[2 pair + 1][c] . x'_g), x'_g = 2^-E x[8g : 8g + 8].
 // ---------------------------------------------------------------------------
 
-// FFMA: warp w builds table rows w + 32 j; lane = group.  Four rows'
-// codebook entries are loaded (broadcast) before any of their table entries
-// is stored; each store is one conflict-free 128-byte row.
-__device__ __forceinline__ void build_lut_ffma(float* __restrict__ lut, const float* __restrict__ cbs,
-                                               const float* __restrict__ xs) {
+// FFMA: warp w builds words p = w + 32 j (p = 2 c + pair, word index 32 p + g);
+// lane = group.  Two words' four codebook rows are loaded (broadcast) before
+// any is stored; each store is one conflict-free 128-byte row of words.
+__device__ __forceinline__ void build_lut_f16(uint32_t* __restrict__ lut, const float* __restrict__ cbs,
+                                              const float* __restrict__ xs, float xscale) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float xr[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) xr[i] = xs[lane * 8 + i];
+    for (int i = 0; i < 8; ++i) xr[i] = xs[lane * 8 + i] * xscale;
     const float4* cb4 = reinterpret_cast<const float4*>(cbs);
 #pragma unroll 1
-    for (int q0 = warp; q0 < kPairs; q0 += kWarps * 4) {
+    for (int p0 = warp; p0 < kCodes * 2; p0 += kWarps * 2) {
         float4 a[4], b[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            a[j] = cb4[(q0 + j * kWarps) * 2];
-            b[j] = cb4[(q0 + j * kWarps) * 2 + 1];
+        for (int j = 0; j < 4; ++j) {            // j = 2 * word + stage within the pair
+            const int p = p0 + (j >> 1) * kWarps, c = p >> 1, k = ((p & 1) << 1) + (j & 1);
+            a[j] = cb4[(k * kCodes + c) * 2];
+            b[j] = cb4[(k * kCodes + c) * 2 + 1];
         }
         float acc[4];
 #pragma unroll
@@ -218,21 +276,40 @@ __device__ __forceinline__ void build_lut_ffma(float* __restrict__ lut, const fl
             acc[j] = t;
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) lut[(q0 + j * kWarps) * kGroups + lane] = acc[j];
+        for (int w = 0; w < 2; ++w) {
+            const __half2 h = __floats2half2_rn(acc[2 * w], acc[2 * w + 1]);    // low half: even stage
+            lut[(p0 + w * kWarps) * kGroups + lane] = *reinterpret_cast<const uint32_t*>(&h);
+        }
     }
+}
+
+__device__ __forceinline__ uint32_t* ring_slot(uint32_t* ring, int slot) { return ring + slot * kBatchRows * kGroups; }
+
+// Power-of-two scale 2^-E bringing max |x| = amax into [1, 2), and 2^E.
+__device__ __forceinline__ void tile_scale(float amax, float& scale, float& unscale) {
+    scale = unscale = 1.f;
+    if (!(amax > 0.f) || !(amax <= 3.0e38f)) return;      // zero or non-finite: no scaling
+    int e = (int)((__float_as_uint(amax) >> 23) & 0xffu) - 127;
+    e = e < -126 ? -126 : (e > 126 ? 126 : e);
+    scale = __uint_as_float((uint32_t)(127 - e) << 23);
+    unscale = __uint_as_float((uint32_t)(127 + e) << 23);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __grid_constant__ TParams p) {
     extern __shared__ __align__(128) float smem[];
-    float* __restrict__ lut = smem;
-    float* __restrict__ cbs = lut + kLutFloats;
+    uint32_t* __restrict__ lut = reinterpret_cast<uint32_t*>(smem);
+    float* __restrict__ cbs = smem + kLutWords;
     uint32_t* ring = reinterpret_cast<uint32_t*>(cbs + kCbFloats);
     float* xs = reinterpret_cast<float*>(ring + kRing * kBatchRows * kGroups);
     uint64_t* bars = reinterpret_cast<uint64_t*>(xs + kTileCols);
+    float* staged = smem;                                // operand partials, before the table is built
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t bar0 = smem_u32(bars);
+    // per-stage table address bits of this lane (see lut_offset)
+    const uint32_t lb0 = (uint32_t)lane << 2, lb1 = lb0 | 2u, lb2 = lb0 | 128u, lb3 = lb0 | 130u;
 
     __shared__ int slot_done[kRing];                     // warps finished with a ring slot
+    __shared__ float xmax[kTileCols / 32];               // per-warp max |x| of the tile
     if (tid < kRing) slot_done[tid] = 0;
     pdl_launch_dependents();
     if (tid == 0) {
@@ -242,127 +319,146 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
     __syncthreads();
     uint32_t phase_bits = 0;                             // bit s: parity of ring slot s's next phase
 
-    for (int u = blockIdx.x; u < p.n_units; u += gridDim.x) {
+    const int u_first = p.cta_first[blockIdx.x], u_last = p.cta_first[blockIdx.x + 1];
+    int cb_job = -1;                                     // job whose codebook is in shared memory
+    for (int u = u_first; u < u_last; ++u) {
         const uint32_t jt = p.unit_jt[u];
         const int ji = (int)(jt >> 24);
         const TJob& J = p.jobs[ji];
-        const CUtensorMap* map = &p.maps[ji];
         const int tile = (int)(jt & 0xffffffu);
         const int r0 = p.unit_r0[u], r1 = p.unit_r1[u];
         const int G = J.G;
         const int gt = min(kGroups, G - tile * kGroups);
         const int nb = (r1 - r0 + kBatchRows - 1) / kBatchRows;
-        const bool tma = J.use_tma != 0;
-        if (u != (int)blockIdx.x) __syncthreads();      // the previous unit is done with shared memory
+        const uint32_t* lines = J.codes + (int64_t)tile * J.rows * kLineWords;   // this tile's code lines
+        if (u != u_first) __syncthreads();              // the previous unit is done with shared memory
 
-        // 1. code words of the first batches start streaming in
-        if (tma) {
-            if (tid == 0) {
-                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-                for (int b = 0; b < kRing && b < nb; ++b)
-                    tma_load_rows(smem_u32(ring + b * kBatchRows * kGroups), map, tile * kGroups,
-                                  r0 + b * kBatchRows, bar0 + 8 * b);
+        // 1. code words of the first four batches start streaming in
+        if (tid == 0) {
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            for (int b = 0; b < kRing && b < nb; ++b) {
+                const int rb = r0 + b * kBatchRows;
+                load_batch(smem_u32(ring_slot(ring, b)), lines, rb, min(r1 - rb, kBatchRows), bar0 + 8 * b);
             }
-        } else {
-            for (int b = 0; b < kRing && b < nb; ++b)
-                stage_batch_words(J, tile, gt, r0 + b * kBatchRows, min(r1, r0 + (b + 1) * kBatchRows),
-                                  ring + b * kBatchRows * kGroups);
         }
 
-        // 2. codebook (fp32) and the tile's operand slice
-        if (J.cb_kind == RVQ_F32) {
-            const float4* cb4 = reinterpret_cast<const float4*>(J.cb);
-            for (int i = tid; i < kCbFloats / 4; i += kThreads) cp_async16(cbs + 4 * i, cb4 + i);
-            cp_async_commit();
-        } else {
-            for (int i = tid; i < kCbFloats; i += kThreads) cbs[i] = load_as_f32(J.cb, i, J.cb_kind);
+        // 2. codebook (fp32) and the tile's operand slice; partial-sum operands
+        //    are staged in the table's space, then summed in tile order
+        if (ji != cb_job) {
+            cb_job = ji;
+            if (J.cb_kind == RVQ_F32) {
+                const float4* cb4 = reinterpret_cast<const float4*>(J.cb);
+                for (int i = tid; i < kCbFloats / 4; i += kThreads) cp_async16(cbs + 4 * i, cb4 + i);
+                cp_async_commit();
+            } else {
+                for (int i = tid; i < kCbFloats; i += kThreads) cbs[i] = load_as_f32(J.cb, i, J.cb_kind);
+            }
         }
-        if (u == (int)blockIdx.x) pdl_wait();            // x comes from the previous kernel
+        if (u == u_first) pdl_wait();                    // x comes from the previous kernel
+        const bool has_gate = J.gate.ptr != nullptr;
+        const bool stage_x = J.x.kind == RVQ_F32 && J.x.ntiles > 1 &&
+                             J.x.ntiles + (has_gate ? J.gate.ntiles : 0) <= kMaxStagedTiles;
+        const bool stage_g = has_gate && stage_x && J.gate.kind == RVQ_F32 && J.gate.ntiles > 1;
+        if (stage_x) stage_partials(J.x, tile, J.cols, staged);
+        if (stage_g) stage_partials(J.gate, tile, J.cols, staged + J.x.ntiles * kTileCols);
+        if (stage_x) __syncthreads();
         if (tid < kTileCols) {
             const int64_t col = (int64_t)tile * kTileCols + tid;
             float xv = 0.f;
             if (col < J.cols) {
-                xv = operand(J.x, col);
-                if (J.gate.ptr != nullptr) {
-                    const float g = operand(J.gate, col);
+                xv = stage_x ? staged_value(staged, J.x.ntiles, tid) : operand(J.x, col);
+                if (has_gate) {
+                    const float g = stage_g ? staged_value(staged + J.x.ntiles * kTileCols, J.gate.ntiles, tid)
+                                            : operand(J.gate, col);
                     xv = bf16r(bf16r(g / (1.0f + expf(-g))) * xv);
                 }
             }
             xs[tid] = xv;
+            float m = fabsf(xv);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) xmax[warp] = m;
         }
-        cp_async_wait<0>();          // the codebook (and, without TMA, the first code batches)
+        cp_async_wait<0>();          // the codebook
         __syncthreads();
 
         // 3. the tile's table (shared-memory bound: the codebook rows are broadcast
-        //    loads, the table 128 KB of conflict-free stores)
-        build_lut_ffma(lut, cbs, xs);
+        //    loads, the table 64 KB of conflict-free stores), from 2^-E x
+        float amax = xmax[0];
+#pragma unroll
+        for (int w = 1; w < kTileCols / 32; ++w) amax = fmaxf(amax, xmax[w]);
+        float xscale, xunscale;
+        tile_scale(amax, xscale, xunscale);
+        build_lut_f16(lut, cbs, xs, xscale);
         __syncthreads();
 
-        // 4. rows, batch by batch; batch b + 2 streams in while b + 1 is processed.
-        //    With TMA every warp waits on the slot's barrier itself, and the last
-        //    warp to finish a slot issues its refill: no CTA-wide barrier per batch.
-        const float* lg = lut + lane;
+        // 4. rows, batch by batch, three batches streaming in while one is processed.
+        //    Every warp waits on the slot's barrier itself, and the last warp to
+        //    finish a slot issues its refill: no CTA-wide barrier per batch.
+        //    Lanes past the matrix edge read zero code words and table columns
+        //    built from x = 0 (exact zeros); rows past the batch (stale words) only
+        //    reach outputs that are not stored.
         const uint32_t g_global = (uint32_t)tile * kGroups + lane;
         float* part = J.part + (int64_t)tile * J.rows;
+        // this lane's output row scale, fetched two batches ahead of its use
+        // (lanes 4i..4i+3 share the row i of each 8-row group; one row group
+        // per warp and batch)
+        const int orow_in = warp * 8 + ((lane >> 2) & 7);
+        const bool scale_lane = J.row_scales && (lane & 3) == 0;
+        auto row_scale = [&](int b) -> float {
+            const int r = r0 + b * kBatchRows + orow_in;
+            return (scale_lane && b < nb && r < r1)
+                       ? load_as_f32(J.scales, fastdiv((uint32_t)r, J.rpsdiv), J.scale_kind) : 1.f;
+        };
+        float sc_next = row_scale(0), sc_next2 = row_scale(1);
         for (int b = 0; b < nb; ++b) {
+            const float oscale_b = sc_next;
+            sc_next = sc_next2;
+            sc_next2 = row_scale(b + 2);
             const int slot = b % kRing;
-            if (tma) {
-                mbar_wait(bar0 + 8 * slot, (phase_bits >> slot) & 1u);
-                phase_bits ^= 1u << slot;
-            } else {
-                if (b + 1 < nb) cp_async_wait<1>();
-                else cp_async_wait<0>();
-                __syncthreads();
-            }
+            mbar_wait(bar0 + 8 * slot, (phase_bits >> slot) & 1u);
+            phase_bits ^= 1u << slot;
             const int rb0 = r0 + b * kBatchRows;
             const int nrows = min(r1, rb0 + kBatchRows) - rb0;
-            const uint32_t* cs = ring + slot * kBatchRows * kGroups + lane;
-            for (int rb = warp * 8; rb < nrows; rb += kWarps * 8) {
-                // this lane's output row (lanes 4i..4i+3 share row i): its scale is
-                // fetched before the lookups so the load overlaps them
+            const uint32_t* cs = ring_slot(ring, slot) + lane;
+            static_assert(kWarps * 8 == kBatchRows, "one 8-row group per warp and batch");
+            {
+                const int rb = warp * 8;
                 const int orow = rb + ((lane >> 2) & 7);
-                float oscale = 1.f;
-                if (J.row_scales && (lane & 3) == 0 && orow < nrows)
-                    oscale = load_as_f32(J.scales, fastdiv((uint32_t)(rb0 + orow), J.rpsdiv), J.scale_kind);
+                const float oscale = oscale_b;
                 float v[8];
+                if (J.row_scales) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t w = cs[(rb + i) * kGroups];
-                    float s = lg[(w & 0xffu) << 5];
-                    s += lg[kCodes * kGroups + (((w >> 8) & 0xffu) << 5)];
-                    s += lg[2 * kCodes * kGroups + (((w >> 16) & 0xffu) << 5)];
-                    s += lg[3 * kCodes * kGroups + ((w >> 24) << 5)];
-                    // rows past the unit (stale or next-unit words) and groups past
-                    // the matrix edge (zero-filled or stale) contribute nothing
-                    const bool valid = rb + i < nrows && lane < gt;
-                    if (!J.row_scales)
-                        s *= valid ? load_as_f32(J.scales,
-                                                 fastdiv((uint32_t)(rb0 + rb + i) * (uint32_t)G + g_global, J.gvdiv),
-                                                 J.scale_kind)
-                                   : 0.f;
-                    v[i] = valid ? s : 0.f;
+                    for (int i = 0; i < 8; ++i) v[i] = lookup4(lut, cs[(rb + i) * kGroups], lb0, lb1, lb2, lb3);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float s = lookup4(lut, cs[(rb + i) * kGroups], lb0, lb1, lb2, lb3);
+                        // per-vector scales: only rows and groups inside the matrix have one
+                        const bool valid = rb + i < nrows && lane < gt;
+                        v[i] = valid ? s * load_as_f32(J.scales,
+                                                       fastdiv((uint32_t)(rb0 + rb + i) * (uint32_t)G + g_global,
+                                                               J.gvdiv),
+                                                       J.scale_kind)
+                                     : 0.f;
+                    }
                 }
                 const float tot = reduce8(v);
-                if ((lane & 3) == 0 && orow < nrows) part[rb0 + orow] = tot * oscale;
+                if ((lane & 3) == 0 && orow < nrows) part[rb0 + orow] = (tot * xunscale) * oscale;
             }
             if (b + kRing < nb) {
                 const int nb0 = r0 + (b + kRing) * kBatchRows;
-                uint32_t* buf = ring + slot * kBatchRows * kGroups;
-                if (tma) {
-                    __syncwarp();
-                    if (lane == 0) {
+                uint32_t* buf = ring_slot(ring, slot);
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence_block();
+                    const int done = atomicAdd(&slot_done[slot], 1);
+                    if (done == kWarps - 1) {               // every warp has left this slot
+                        slot_done[slot] = 0;
                         __threadfence_block();
-                        const int done = atomicAdd(&slot_done[slot], 1);
-                        if (done == kWarps - 1) {               // every warp has left this slot
-                            slot_done[slot] = 0;
-                            __threadfence_block();
-                            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-                            tma_load_rows(smem_u32(buf), map, tile * kGroups, nb0, bar0 + 8 * slot);
-                        }
+                        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                        load_batch(smem_u32(buf), lines, nb0, min(r1 - nb0, kBatchRows), bar0 + 8 * slot);
                     }
-                } else {
-                    __syncthreads();                        // every warp is done with buf
-                    stage_batch_words(J, tile, gt, nb0, min(r1, nb0 + kBatchRows), buf);
                 }
             }
         }
@@ -378,7 +474,6 @@ struct DevInfo {
 };
 DevInfo g_dev[64];
 std::mutex g_mu;
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int dev_info(DevInfo** out) {
     int dev = 0;
@@ -397,14 +492,7 @@ int dev_info(DevInfo** out) {
             d.sms = prop.multiProcessorCount;
             e = cudaFuncSetAttribute(rvq_gemv_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kSmemBytes);
-            if (e == cudaSuccess && g_encode == nullptr) {
-                void* fn = nullptr;
-                cudaDriverEntryPointQueryResult q;
-                e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-                if (e == cudaSuccess && q == cudaDriverEntryPointSuccess)
-                    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-            }
-            d.ok = e == cudaSuccess && g_encode != nullptr;
+            d.ok = e == cudaSuccess;
         }
         if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
     }
@@ -428,7 +516,7 @@ int check_job(const rvq_gemv_tile_job& g) {
     if (g.rows < 1 || g.cols < 8 || g.cols % 8) return RVQ_ERR_UNSUPPORTED;
     if (g.rows * (g.cols / 8) != w.nvec || w.trimmed != w.nvec * 8 || w.tail_numel != 0)
         return RVQ_ERR_UNSUPPORTED;
-    if ((uintptr_t)w.indices & 3) return RVQ_ERR_INVALID;
+    if ((uintptr_t)w.indices & 15) return RVQ_ERR_INVALID;      // bulk copies start on 16 bytes
     if (w.nvec >= (1ll << 32) || g.rows >= (1ll << 31) || (g.cols + kTileCols - 1) / kTileCols >= (1 << 24))
         return RVQ_ERR_TOO_LARGE;
     if (w.codebook_kind != RVQ_F32 && w.codebook_kind != RVQ_F16 && w.codebook_kind != RVQ_BF16)
@@ -439,69 +527,140 @@ int check_job(const rvq_gemv_tile_job& g) {
     return RVQ_OK;
 }
 
-// Units: every (job, tile) gets CTAs in proportion to its work (rows x groups),
-// at least one, the wave's remainder going to the largest fractional shares;
-// each CTA takes an even share of its tile's rows.
+// Units.  Two plans are costed, a unit costing its rows plus kSwitchRows, and
+// the one whose most loaded CTA costs less is taken:
+//  * one unit per CTA: tile t gets c_t CTAs with equal row ranges, the c_t
+//    chosen (binary search on the cost bound) to minimise the largest unit;
+//  * runs: the (job, tile, row) work in job and tile order is cut into
+//    contiguous runs of equal cost, one run per CTA (a run that crosses a tile
+//    boundary builds two tables).
+// Row ranges are cut at multiples of 8 rows.
+
 int plan(const rvq_gemv_tile_job* jobs, int n, int sms, TParams& p) {
-    struct T { int job, tile; double share; int ctas; int64_t rows; };
-    static thread_local T ts[kMaxUnits];
-    int nt = 0;
-    double total = 0;
+    int ntiles = 0;
+    int64_t rows_total = 0;
     for (int j = 0; j < n; ++j) {
-        const int G = (int)(jobs[j].cols / 8);
-        const int ntiles = (G + kGroups - 1) / kGroups;
-        for (int t = 0; t < ntiles; ++t) {
-            if (nt >= kMaxUnits) return RVQ_ERR_TOO_LARGE;
-            const int gt = G - t * kGroups < kGroups ? G - t * kGroups : kGroups;
-            ts[nt] = {j, t, (double)jobs[j].rows * gt, 1, jobs[j].rows};
-            total += ts[nt].share;
-            ++nt;
+        const int64_t nt = (jobs[j].cols / 8 + kGroups - 1) / kGroups;
+        ntiles += (int)nt;
+        rows_total += nt * jobs[j].rows;
+    }
+    if (ntiles > kMaxUnits) return RVQ_ERR_TOO_LARGE;
+    const int ctas = sms < kMaxCtas ? sms : kMaxCtas;
+
+    // plan A: one unit per CTA
+    auto ctas_for = [&](int64_t bound_rows, int j) -> int64_t {   // CTAs per tile of job j
+        const int64_t R = jobs[j].rows;
+        int64_t c = (R + bound_rows - 1) / bound_rows;
+        const int64_t cmax = (R + 7) / 8;
+        return c < 1 ? 1 : (c > cmax ? cmax : c);
+    };
+    auto total_ctas = [&](int64_t bound_rows) -> int64_t {
+        int64_t t = 0;
+        for (int j = 0; j < n; ++j) t += ctas_for(bound_rows, j) * ((jobs[j].cols / 8 + kGroups - 1) / kGroups);
+        return t;
+    };
+    int64_t lo = 8, hi = 8;
+    for (int j = 0; j < n; ++j) hi = hi > jobs[j].rows ? hi : jobs[j].rows;
+    hi = (hi + 7) & ~7ll;
+    if (total_ctas(hi) > ctas) {
+        lo = hi = -1;                                       // more tiles than CTAs: plan A impossible
+    } else {
+        while (lo < hi) {                                   // smallest bound whose CTA count fits
+            const int64_t mid = ((lo + hi) / 2 + 7) & ~7ll;
+            if (mid >= hi) break;
+            if (total_ctas(mid) <= ctas) hi = mid; else lo = mid + 8;
         }
     }
-    int used = 0;
-    const int budget = sms > nt ? sms : nt;
-    for (int i = 0; i < nt; ++i) {
-        const double want = ts[i].share / total * budget;
-        int c = (int)want;
-        if (c < 1) c = 1;
-        if (c > ts[i].rows) c = (int)ts[i].rows;
-        ts[i].ctas = c;
-        ts[i].share = want - c;                  // remainder (negative when raised to 1)
-        used += c;
-    }
-    while (used < budget) {                      // largest remainders first
-        int best = -1;
-        for (int i = 0; i < nt; ++i)
-            if (ts[i].ctas < ts[i].rows && (best < 0 || ts[i].share > ts[best].share)) best = i;
-        if (best < 0) break;
-        ts[best].ctas += 1;
-        ts[best].share -= 1.0;
-        ++used;
-    }
-    int u = 0;
-    for (int i = 0; i < nt; ++i) {
-        for (int c = 0; c < ts[i].ctas; ++c) {
-            if (u >= kMaxUnits) return RVQ_ERR_TOO_LARGE;
-            p.unit_jt[u] = ((uint32_t)ts[i].job << 24) | (uint32_t)ts[i].tile;
-            p.unit_r0[u] = (int32_t)(ts[i].rows * c / ts[i].ctas);
-            p.unit_r1[u] = (int32_t)(ts[i].rows * (c + 1) / ts[i].ctas);
-            ++u;
+    double cost_a = 1e30;
+    int64_t bound = hi;
+    if (bound > 0) {
+        cost_a = 0;
+        for (int j = 0; j < n; ++j) {
+            const int64_t R = jobs[j].rows, c = ctas_for(bound, j);
+            const int64_t longest = ((R + c - 1) / c + 7) & ~7ll;
+            cost_a = cost_a > kSwitchRows + longest ? cost_a : (double)(kSwitchRows + longest);
         }
     }
+
+    // plan B: contiguous runs of equal cost
+    const double target = (double)(rows_total + (int64_t)kSwitchRows * (ntiles + ctas)) / ctas;
+    const double cost_b = target + kSwitchRows;             // the run that ends mid-tile pays one more table
+
+    int u = 0, c = 0;
+    p.cta_first[0] = 0;
+    if (cost_a <= cost_b) {
+        for (int j = 0; j < n; ++j) {
+            const int nt = (int)((jobs[j].cols / 8 + kGroups - 1) / kGroups);
+            const int64_t R = jobs[j].rows, cj = ctas_for(bound, j);
+            for (int t = 0; t < nt; ++t) {
+                for (int64_t k = 0; k < cj; ++k) {
+                    const int64_t a = (R * k / cj) & ~7ll, b = k + 1 == cj ? R : (R * (k + 1) / cj) & ~7ll;
+                    if (b <= a) continue;
+                    if (u >= kMaxUnits || c >= kMaxCtas) return RVQ_ERR_TOO_LARGE;
+                    p.unit_jt[u] = ((uint32_t)j << 24) | (uint32_t)t;
+                    p.unit_r0[u] = (int32_t)a;
+                    p.unit_r1[u] = (int32_t)b;
+                    ++u;
+                    p.cta_first[++c] = u;
+                }
+            }
+        }
+        p.n_ctas = c;
+        p.n_units = u;
+        return RVQ_OK;
+    }
+    double cost = 0;
+    for (int j = 0; j < n; ++j) {
+        const int nt = (int)((jobs[j].cols / 8 + kGroups - 1) / kGroups);
+        const int R = (int)jobs[j].rows;
+        for (int t = 0; t < nt; ++t) {
+            int r = 0;
+            while (r < R) {
+                const double room = target - cost - kSwitchRows;      // rows this run can still take
+                if (cost > 0 && room < 64 && c + 1 < ctas) {           // close this run, open the next
+                    p.cta_first[++c] = u;
+                    cost = 0;
+                    continue;
+                }
+                int take = R - r;
+                if (c + 1 < ctas && room < take) {
+                    take = (int)room;
+                    take = take < 64 ? 64 : (take + 7) & ~7;
+                    if (take > R - r) take = R - r;
+                }
+                if (u >= kMaxUnits) return RVQ_ERR_TOO_LARGE;
+                p.unit_jt[u] = ((uint32_t)j << 24) | (uint32_t)t;
+                p.unit_r0[u] = r;
+                p.unit_r1[u] = r + take;
+                ++u;
+                cost += kSwitchRows + take;
+                r += take;
+            }
+        }
+    }
+    p.cta_first[c + 1] = u;
+    p.n_ctas = c + 1;
     p.n_units = u;
     return RVQ_OK;
 }
 
-// [rows][G] uint32 words, box 32 x 256; reads past either edge fill zeros.
-int encode_map(CUtensorMap* m, const void* codes, int64_t rows, int64_t G) {
-    const cuuint64_t dims[2] = {(cuuint64_t)G, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)G * 4};
-    const cuuint32_t box[2] = {(cuuint32_t)kGroups, (cuuint32_t)kBatchRows};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(codes), dims, strides, box,
-                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? RVQ_OK : RVQ_ERR_INVALID;
+// Tile-major code lines: out[t][r][w] = the code word of vector (r, 32 t + w),
+// zero past the last group.  One thread per output word.
+__global__ void tile_codes_kernel(const uint8_t* __restrict__ planes, int64_t stage_stride, int64_t rows,
+                                  int64_t G, int64_t ntiles, uint32_t* __restrict__ out) {
+    const int64_t total = ntiles * rows * kLineWords;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t w = i % kLineWords, tr = i / kLineWords;
+        const int64_t r = tr % rows, t = tr / rows;
+        const int64_t g = t * kLineWords + w;
+        uint32_t word = 0;
+        if (g < G) {
+            const int64_t v = r * G + g;
+            word = (uint32_t)planes[v] | ((uint32_t)planes[stage_stride + v] << 8) |
+                   ((uint32_t)planes[2 * stage_stride + v] << 16) | ((uint32_t)planes[3 * stage_stride + v] << 24);
+        }
+        out[i] = word;
+    }
 }
 
 }  // namespace tiles
@@ -513,6 +672,30 @@ using namespace rvq::tiles;
 extern "C" {
 
 int64_t rvq_gemv_tiles_count(int64_t cols) { return cols < 1 ? 0 : (cols + kTileCols - 1) / kTileCols; }
+
+int64_t rvq_tile_codes_bytes(int64_t rows, int64_t cols) {
+    if (rows < 1 || cols < 8 || cols % 8) return 0;
+    return rvq_gemv_tiles_count(cols) * rows * kLineWords * 4;
+}
+
+int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64_t cols, void* out, void* stream) {
+    if (planes == nullptr || out == nullptr || rows < 1 || cols < 8 || cols % 8) return RVQ_ERR_INVALID;
+    const int64_t G = cols / 8;
+    if (stage_stride < rows * G || ((uintptr_t)out & 15)) return RVQ_ERR_INVALID;
+    const int64_t ntiles = rvq_gemv_tiles_count(cols);
+    const int64_t total = ntiles * rows * kLineWords;
+    const int64_t blocks64 = (total + 255) / 256;
+    const int blocks = (int)(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
+    tile_codes_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const uint8_t*>(planes),
+                                                                stage_stride, rows, G, ntiles,
+                                                                reinterpret_cast<uint32_t*>(out));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        last_cuda_error_slot() = (int)e;
+        return RVQ_ERR_CUDA;
+    }
+    return RVQ_OK;
+}
 
 int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream) {
     if (jobs == nullptr || n_jobs < 1 || n_jobs > kMaxJobs) return RVQ_ERR_INVALID;
@@ -543,15 +726,10 @@ int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream) {
         J.rpsdiv = make_fastdiv(J.row_scales ? gv / (uint32_t)J.G : 1u);
         J.cb_kind = g.weight.codebook_kind;
         J.scale_kind = g.weight.scale_kind;
-        J.use_tma = (J.G % 4 == 0) && (((uintptr_t)g.weight.indices & 15) == 0);
-        if (J.use_tma) {
-            rc = encode_map(&p.maps[i], g.weight.indices, g.rows, J.G);
-            if (rc != RVQ_OK) return rc;
-        }
     }
     rc = plan(jobs, n_jobs, d->sms, p);
     if (rc != RVQ_OK) return rc;
-    const int grid = p.n_units < d->sms ? p.n_units : d->sms;
+    const int grid = p.n_ctas;
     cudaError_t e = launch_pdl(rvq_gemv_tiles_kernel, dim3(grid), dim3(kThreads), kSmemBytes, (cudaStream_t)stream, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {

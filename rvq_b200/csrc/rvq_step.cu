@@ -9,6 +9,7 @@
 // to bf16), so the GEMV that produced them needs no reduction pass of its own.
 
 #include <cooperative_groups.h>
+#include <string.h>
 #include <type_traits>
 
 #include "rvq_common.cuh"
@@ -56,6 +57,43 @@ __device__ __forceinline__ float vec_value(const rvq_vec& v, int64_t i) {
     return load_as_f32(v.ptr, i, v.kind);
 }
 
+__device__ int g_tp_timeout;                 // sticky: a landing-buffer wait gave up
+
+// Operand read through L2 (a landing buffer that peers write over NVLink:
+// no stale L1 lines).  fp32 rows summed in row order, then rounded to bf16.
+__device__ __forceinline__ float vec_value_l2(const rvq_vec& v, int64_t i) {
+    const float* p = reinterpret_cast<const float*>(v.ptr) + i;
+    float s = __ldcg(p);
+    for (int t = 1; t < v.ntiles; ++t) s += __ldcg(p + (int64_t)t * v.n);
+    return bf16r(s);
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait until *arrivals has reached `target` (wrap-around safe).  Gives up
+// after about one second (or 2^24 polls), sets the sticky timeout flag and
+// returns false; the caller then goes on with whatever the buffer holds.
+__device__ __forceinline__ bool wait_arrivals(const uint32_t* arrivals, uint32_t target) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        if ((int32_t)(ld_acquire_sys(arrivals) - target) >= 0) return true;
+        if (i > 64) __nanosleep(128);
+        if ((i & 63) == 0 && globaltimer_ns() - t0 > 1000000000ull) break;
+    }
+    atomicExch(&g_tp_timeout, 1);
+    return false;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -88,6 +126,13 @@ step_norm_kernel(rvq_norm_args a) {
     pdl_launch_dependents();
     for (int64_t i = lo + tid; i < hi; i += kNormThreads) wbuf[i - lo] = bf16_at(a.weight, i);
     pdl_wait();
+    const bool landing = a.arrivals != nullptr && a.token == nullptr && a.add.ptr != nullptr;
+    uint32_t target = 0;
+    if (landing) {                              // every rank's push has arrived
+        target = __ldcg(a.consumed) + a.arrivals_per_use;
+        if (tid == 0) wait_arrivals(a.arrivals, target);
+        __syncthreads();
+    }
     float ss = 0.f;
     if (a.token != nullptr) {
         const int64_t tok = *a.token;
@@ -100,7 +145,7 @@ step_norm_kernel(rvq_norm_args a) {
     } else {
         for (int64_t i = lo + tid; i < hi; i += kNormThreads) {
             float hv = bf16_at(a.h, i);
-            if (a.add.ptr != nullptr) hv = bf16r(hv + vec_value(a.add, i));
+            if (a.add.ptr != nullptr) hv = bf16r(hv + (landing ? vec_value_l2(a.add, i) : vec_value(a.add, i)));
             hbuf[i - lo] = hv;
             ss = fmaf(hv, hv, ss);
         }
@@ -123,6 +168,7 @@ step_norm_kernel(rvq_norm_args a) {
         put_bf16(a.x, i, wbuf[i - lo] * bf16r(hv * inv));
     }
     cluster.sync();       // no CTA leaves while another may still read its cta_ss
+    if (landing && rank == 0 && tid == 0) *a.consumed = target;
 }
 
 // ---------------------------------------------------------------------------
@@ -502,6 +548,7 @@ extern "C" int rvq_step_norm(const rvq_norm_args* a, void* stream) {
     if (a->hidden < 1 || a->hidden > (int64_t)kNormCtas * kNormMaxSlice) return RVQ_ERR_UNSUPPORTED;
     if (a->token != nullptr && (a->embed == nullptr || a->vocab < 1)) return RVQ_ERR_INVALID;
     if (a->token == nullptr && a->add.ptr != nullptr && !vec_ok(a->add, a->hidden)) return RVQ_ERR_INVALID;
+    if (a->arrivals != nullptr && (a->consumed == nullptr || a->add.kind != RVQ_F32)) return RVQ_ERR_INVALID;
     const cudaError_t e = launch_pdl(step_norm_kernel, dim3(kNormCtas), dim3(kNormThreads), 0,
                                      (cudaStream_t)stream, *a);
     if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
@@ -538,4 +585,156 @@ extern "C" int rvq_step_silu_mul(const rvq_vec* gate, const rvq_vec* up, void* o
                                      *gate, *up, out);
     if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
     return e == cudaSuccess ? launch_status() : RVQ_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel push (see include/rvq_b200.h)
+// ---------------------------------------------------------------------------
+namespace rvq {
+namespace {
+
+constexpr int kPushThreads = 256;
+constexpr int kPushPerThread = 4;
+
+struct TpPush {
+    rvq_vec src;
+    float* dst[RVQ_MAX_TP];
+    uint32_t* arrivals[RVQ_MAX_TP];
+    int64_t n;
+    int32_t rank, tp;
+};
+
+// fp32 value of the projection output (tiles summed in order, not rounded)
+__device__ __forceinline__ float vec_value_f32(const rvq_vec& v, int64_t i) {
+    if (v.kind == RVQ_F32) {
+        const float* p = reinterpret_cast<const float*>(v.ptr) + i;
+        float s = __ldg(p);
+        int t = 1;
+        for (; t + 8 <= v.ntiles; t += 8) {
+            float c[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) c[k] = __ldg(p + (int64_t)(t + k) * v.n);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s += c[k];
+        }
+        for (; t < v.ntiles; ++t) s += __ldg(p + (int64_t)t * v.n);
+        return s;
+    }
+    return load_as_f32(v.ptr, i, v.kind);
+}
+
+__global__ void __launch_bounds__(kPushThreads) tp_push_kernel(TpPush a) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t base = (int64_t)blockIdx.x * kPushThreads * kPushPerThread;
+    float v[kPushPerThread];
+#pragma unroll
+    for (int k = 0; k < kPushPerThread; ++k) {
+        const int64_t i = base + k * kPushThreads + threadIdx.x;
+        v[k] = i < a.n ? vec_value_f32(a.src, i) : 0.f;
+    }
+    for (int r = 0; r < a.tp; ++r) {
+        float* d = a.dst[r] + (int64_t)a.rank * a.n;
+#pragma unroll
+        for (int k = 0; k < kPushPerThread; ++k) {
+            const int64_t i = base + k * kPushThreads + threadIdx.x;
+            if (i < a.n) d[i] = v[k];
+        }
+    }
+    __threadfence_system();                 // this thread's peer stores before the arrivals
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int r = 0; r < a.tp; ++r) {
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;\n" ::"l"(a.arrivals[r]) : "memory");
+        }
+    }
+}
+
+}  // namespace
+}  // namespace rvq
+
+extern "C" uint32_t rvq_tp_push_ctas(int64_t n) {
+    return n < 1 ? 0u : (uint32_t)((n + kPushThreads * kPushPerThread - 1) / (kPushThreads * kPushPerThread));
+}
+
+extern "C" int rvq_tp_push(const rvq_tp_push_args* a, void* stream) {
+    if (a == nullptr || a->tp < 1 || a->tp > RVQ_MAX_TP || a->rank < 0 || a->rank >= a->tp || a->n < 1)
+        return RVQ_ERR_INVALID;
+    if (!vec_ok(a->src, a->n)) return RVQ_ERR_INVALID;
+    TpPush p;
+    memset(&p, 0, sizeof(p));
+    p.src = a->src;
+    p.n = a->n;
+    p.rank = a->rank;
+    p.tp = a->tp;
+    for (int r = 0; r < a->tp; ++r) {
+        if (a->dst[r] == nullptr || a->arrivals[r] == nullptr) return RVQ_ERR_INVALID;
+        p.dst[r] = a->dst[r];
+        p.arrivals[r] = a->arrivals[r];
+    }
+    const cudaError_t e = launch_pdl(tp_push_kernel, dim3(rvq_tp_push_ctas(a->n)), dim3(kPushThreads), 0,
+                                     (cudaStream_t)stream, p);
+    if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
+    return e == cudaSuccess ? launch_status() : RVQ_ERR_CUDA;
+}
+
+extern "C" int rvq_p2p_alloc(size_t bytes, void** out) {
+    if (out == nullptr || bytes == 0) return RVQ_ERR_INVALID;
+    cudaError_t e = cudaMalloc(out, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*out, 0, bytes);
+    if (e != cudaSuccess) {
+        last_cuda_error_slot() = (int)e;
+        return RVQ_ERR_CUDA;
+    }
+    return RVQ_OK;
+}
+
+extern "C" int rvq_p2p_free(void* ptr) {
+    const cudaError_t e = cudaFree(ptr);
+    if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
+    return e == cudaSuccess ? RVQ_OK : RVQ_ERR_CUDA;
+}
+
+extern "C" int rvq_ipc_export(void* ptr, void* handle64) {
+    if (ptr == nullptr || handle64 == nullptr) return RVQ_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+    if (e != cudaSuccess) {
+        last_cuda_error_slot() = (int)e;
+        return RVQ_ERR_CUDA;
+    }
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    memcpy(handle64, &h, sizeof(h));
+    return RVQ_OK;
+}
+
+extern "C" int rvq_ipc_import(const void* handle64, void** out) {
+    if (handle64 == nullptr || out == nullptr) return RVQ_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        last_cuda_error_slot() = (int)e;
+        return RVQ_ERR_CUDA;
+    }
+    return RVQ_OK;
+}
+
+extern "C" int rvq_ipc_close(void* ptr) {
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
+    return e == cudaSuccess ? RVQ_OK : RVQ_ERR_CUDA;
+}
+
+extern "C" int rvq_take_tp_timeout(void) {
+    int v = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, rvq::g_tp_timeout, sizeof(int));
+    const int zero = 0;
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(rvq::g_tp_timeout, &zero, sizeof(int));
+    if (e != cudaSuccess) {
+        last_cuda_error_slot() = (int)e;
+        return -RVQ_ERR_CUDA;
+    }
+    return v;
 }

@@ -39,7 +39,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .engine import LayerDecodePlan, decode_to_tensor
-from .gemv import GemvPlan, gemv_supported, interleave_codes
+from .gemv import GemvPlan, gemv_supported, interleave_codes, tile_codes
 from .slots import SlotArena, SlotSpec
 
 PROJ = ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
@@ -91,11 +91,15 @@ class Qwen3Decoder:
     ``_attention``), True the standard causal one.  ``tp_group``: a NCCL
     process group to run tensor-parallel over (one rank per GPU); the
     artifact is the full model, or this rank's shard when
-    ``artifact_is_shard`` (rvq_b200/shard.py layout)."""
+    ``artifact_is_shard`` (rvq_b200/shard.py layout).  ``tp_reduce``: how the
+    native step sums the row-parallel outputs over the ranks: "push" (peer
+    stores over NVLink into landing buffers, rvq_b200/tp.py) or "nccl"
+    (``dist.all_reduce`` captured in the graph); prefill always uses NCCL."""
 
     def __init__(self, config, artifact, device, mode: str = "fused", max_len: int = 512,
                  runtime_dtype: torch.dtype = torch.bfloat16, causal: bool = False,
-                 step_impl: str = "native", tp_group=None, artifact_is_shard: bool = False):
+                 step_impl: str = "native", tp_group=None, artifact_is_shard: bool = False,
+                 tp_reduce: str = "push"):
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
         if step_impl not in ("native", "torch"):
@@ -111,6 +115,10 @@ class Qwen3Decoder:
         # followed by an all-reduce of their outputs (rvq_b200/shard.py)
         self.tp_group = tp_group
         self.tp = dist.get_world_size(tp_group) if tp_group is not None else 1
+        if tp_reduce not in ("push", "nccl"):
+            raise ValueError("tp_reduce is 'push' or 'nccl'")
+        self.push = self.tp > 1 and tp_reduce == "push" and step_impl == "native"
+        self.exchange = None
         if self.tp > 1:
             from .shard import shard_artifact, sharded_dims
             rank = dist.get_rank(tp_group)
@@ -180,10 +188,14 @@ class Qwen3Decoder:
             for n in PROJ:
                 if not gemv_supported(E[n]):
                     raise NotImplementedError(f"fused mode needs rvq_gemv-compatible entries ({n})")
-                E[n]["codes_il"] = interleave_codes(E[n]["indices"])
             cb = lambda n: self.codebooks[E[n]["codebook_id"]]
-            if self.step_impl == "native":
-                continue                        # rvq_gemv_tiles plans: _build_step_ops
+            if self.step_impl == "native":      # rvq_gemv_tiles plans: _build_step_ops
+                for n in PROJ:
+                    rows, cols = (int(v) for v in E[n]["shape"])
+                    E[n]["codes_tiled"] = tile_codes(E[n]["indices"], rows, cols)
+                continue
+            for n in PROJ:
+                E[n]["codes_il"] = interleave_codes(E[n]["indices"])
             L["gemv_qkv"] = GemvPlan([(E[PROJ[0]], cb(PROJ[0]), self.x_attn, self.q),
                                       (E[PROJ[1]], cb(PROJ[1]), self.x_attn, self.k),
                                       (E[PROJ[2]], cb(PROJ[2]), self.x_attn, self.v)])
@@ -337,7 +349,7 @@ class Qwen3Decoder:
             self.gate_part, self.up_part = part(d.intermediate, d.hidden), part(d.intermediate, d.hidden)
             self.down_part = part(d.hidden, d.intermediate)
             q, k, v, o, down = self.q_part, self.k_part, self.v_part, self.o_part, self.down_part
-            if self.tp > 1:
+            if self.tp > 1 and not self.push:
                 # row-parallel outputs: tiles summed locally, then one fp32 vector all-reduced
                 self.o_red = torch.zeros(d.hidden, dtype=torch.float32, device=dev)
                 self.down_red = torch.zeros(d.hidden, dtype=torch.float32, device=dev)
@@ -345,19 +357,28 @@ class Qwen3Decoder:
         else:
             q, k, v, o, down = self.q, self.k, self.v, self.o, self.down
         tiles = lambda t: t.shape[0] if t.dim() == 2 else 1
+        land_o = land_d = None
+        if self.push:
+            # row-parallel outputs pushed to every rank's landing buffer; the norms wait and add
+            from .tp import PeerExchange, TpPushOp
+            self.exchange = PeerExchange(self.tp_group, d.hidden, dev)
+            self.push_o = TpPushOp(self.exchange, "o", o, tiles(o))
+            self.push_down = TpPushOp(self.exchange, "down", down, tiles(down))
+            land_o, land_d = self.exchange.landing("o"), self.exchange.landing("down")
         for l, L in enumerate(self.layers):
             first = l == 0
             ops = {
                 "norm1": NormOp(self.h, L["input_layernorm.weight"], self.x_attn, d.eps,
-                                add=None if first else down, add_tiles=tiles(down),
-                                token=self._tok if first else None, embed=self.embed if first else None),
+                                add=None if first or land_d else down, add_tiles=tiles(down),
+                                token=self._tok if first else None, embed=self.embed if first else None,
+                                landing=None if first else land_d),
                 "attn": AttentionOp(q, k, v, L["self_attn.q_norm.weight"],
                                     L["self_attn.k_norm.weight"], self.cos, self.sin, self._pos,
                                     self.k_cache[l], self.v_cache[l], self.attn_out, n_heads=d.n_heads,
                                     n_kv=d.n_kv, head_dim=d.head_dim, eps=d.eps, scaling=self.scaling,
                                     valid_bias=0.0 if self.causal else 1.0, q_tiles=tiles(q), kv_tiles=tiles(k)),
-                "norm2": NormOp(self.h, L["post_attention_layernorm.weight"], self.x_mlp, d.eps, add=o,
-                                add_tiles=tiles(o)),
+                "norm2": NormOp(self.h, L["post_attention_layernorm.weight"], self.x_mlp, d.eps,
+                                add=None if land_o else o, add_tiles=tiles(o), landing=land_o),
             }
             if fused:
                 E = L["entries"]
@@ -373,7 +394,8 @@ class Qwen3Decoder:
             else:
                 ops["silu"] = SiluMulOp(self.gate, self.up, self.act)
             self.step_ops.append(ops)
-        self.final_op = NormOp(self.h, self.final_norm, self.x_final, d.eps, add=down, add_tiles=tiles(down))
+        self.final_op = NormOp(self.h, self.final_norm, self.x_final, d.eps, add=None if land_d else down,
+                               add_tiles=tiles(down), landing=land_d)
 
     @staticmethod
     def _mv(w: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> None:
@@ -393,24 +415,30 @@ class Qwen3Decoder:
             ops["attn"].launch()
             if fused:
                 ops["o"].launch()
-                if self.tp > 1:
-                    torch.sum(self.o_part, 0, out=self.o_red)
-                    self._allreduce(self.o_red)
             else:
                 self._mv(w[PROJ[3]], self.attn_out, self.o)
+            if self.push:
+                self.push_o.launch()
+            elif fused and self.tp > 1:
+                torch.sum(self.o_part, 0, out=self.o_red)
+                self._allreduce(self.o_red)
+            elif not fused:
                 self._allreduce(self.o)
             ops["norm2"].launch()
             if fused:
                 ops["gu"].launch()
                 ops["down"].launch()
-                if self.tp > 1:
-                    torch.sum(self.down_part, 0, out=self.down_red)
-                    self._allreduce(self.down_red)
             else:
                 self._mv(w[PROJ[4]], self.x_mlp, self.gate)
                 self._mv(w[PROJ[5]], self.x_mlp, self.up)
                 ops["silu"].launch()
                 self._mv(w[PROJ[6]], self.act, self.down)
+            if self.push:
+                self.push_down.launch()
+            elif fused and self.tp > 1:
+                torch.sum(self.down_part, 0, out=self.down_red)
+                self._allreduce(self.down_red)
+            elif not fused:
                 self._allreduce(self.down)
         self.final_op.launch()
         self._mv(self.lm_head, self.x_final, self.logits_buf)
@@ -453,6 +481,19 @@ class Qwen3Decoder:
         self._pos.fill_(pos)
         self.graph.replay()
         return self._logits
+
+    def close(self) -> None:
+        """Release the captured graph and, collectively over the tensor-parallel
+        group, the peer landing buffers.  Every rank calls it at the same point."""
+        self.graph = None
+        if self.exchange is not None:
+            torch.cuda.synchronize(self.device)
+            from .tp import take_timeout
+            timed_out = take_timeout()
+            self.exchange.close()
+            self.exchange = None
+            if timed_out:
+                raise RuntimeError("a tensor-parallel landing-buffer wait timed out")
 
     def generate(self, prompt: torch.Tensor, new_tokens: int, return_logits: bool = False):
         """Greedy: prompt ids [T] (device) -> ``new_tokens`` ids (device [new_tokens])."""

@@ -174,6 +174,11 @@ def _tiles_lib():
         lib.rvq_gemv_tiles.argtypes = [ctypes.POINTER(RvqGemvTileJob), ctypes.c_int, ctypes.c_void_p]
         lib.rvq_gemv_tiles_count.restype = ctypes.c_int64
         lib.rvq_gemv_tiles_count.argtypes = [ctypes.c_int64]
+        lib.rvq_tile_codes_bytes.restype = ctypes.c_int64
+        lib.rvq_tile_codes_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+        lib.rvq_tile_codes.restype = ctypes.c_int
+        lib.rvq_tile_codes.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_void_p, ctypes.c_void_p]
         _tiles_bound = True
     return lib
 
@@ -183,11 +188,32 @@ def tiles_count(cols: int) -> int:
     return int(_tiles_lib().rvq_gemv_tiles_count(cols))
 
 
+def tile_codes(indices: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """The [4, nvec] uint8 code planes of a rows x cols entry in the
+    tile-major layout ``rvq_gemv_tiles`` streams: ``[tiles, rows, 32]`` 32-bit
+    words (stage k in byte k, zero past the last group), returned as a flat
+    uint8 tensor.  Runs on the device."""
+    if indices.dtype != torch.uint8 or indices.dim() != 2 or int(indices.shape[0]) != 4:
+        raise NotImplementedError("tiling takes [4, nvec] uint8 code planes")
+    indices = indices.contiguous()
+    if int(indices.shape[1]) != rows * (cols // 8) or cols % 8:
+        raise ValueError("code planes do not match the weight's shape")
+    nbytes = int(_tiles_lib().rvq_tile_codes_bytes(rows, cols))
+    out = torch.empty(nbytes, dtype=torch.uint8, device=indices.device)
+    with torch.cuda.device(indices.device):
+        rc = _tiles_lib().rvq_tile_codes(ctypes.c_void_p(indices.data_ptr()), int(indices.shape[1]), rows, cols,
+                                         ctypes.c_void_p(out.data_ptr()),
+                                         ctypes.c_void_p(torch.cuda.current_stream(indices.device).cuda_stream))
+    if rc:
+        _native.check(rc, "rvq_tile_codes")
+    return out
+
+
 class GemvTilesPlan:
     """One ``rvq_gemv_tiles`` launch over up to 4 products.
 
     ``products``: ``(entry, codebook, x, partials)`` or ``(entry, codebook, x,
-    partials, gate)`` tuples.  ``entry["codes_il"]`` (from ``interleave_codes``)
+    partials, gate)`` tuples.  ``entry["codes_tiled"]`` (from ``tile_codes``)
     is required.  ``x`` / ``gate`` are bf16 vectors or fp32 partials
     ``[ntiles, cols]``; ``partials`` is fp32 ``[tiles_count(cols), rows]``.
     With ``gate`` the operand is ``bf16(bf16(silu(gate)) * x)``.
@@ -201,8 +227,8 @@ class GemvTilesPlan:
         for prod in products:
             entry, codebook, x, part = prod[:4]
             gate = prod[4] if len(prod) > 4 else None
-            if not gemv_supported(entry) or entry.get("codes_il") is None:
-                raise NotImplementedError("rvq_gemv_tiles needs a K=4 uint8 entry with codes_il")
+            if not gemv_supported(entry) or entry.get("codes_tiled") is None:
+                raise NotImplementedError("rvq_gemv_tiles needs a K=4 uint8 entry with codes_tiled")
             rows, cols = int(entry["shape"][0]), int(entry["shape"][1])
             nt = tiles_count(cols)
             if part.dtype != torch.float32 or tuple(part.shape) != (nt, rows) or not part.is_contiguous():
@@ -212,7 +238,7 @@ class GemvTilesPlan:
             if not codebook.is_contiguous() or codebook.data_ptr() % 16:
                 codebook = codebook.contiguous().clone()
             scales = entry["scales"].contiguous()
-            codes = entry["codes_il"]
+            codes = entry["codes_tiled"]
             xv = _step.vec(x, x.shape[0] if (x.dtype == torch.float32 and x.dim() == 2) else 1)
             gv = _step.vec(gate, gate.shape[0] if (gate is not None and gate.dtype == torch.float32
                                                     and gate.dim() == 2) else 1)

@@ -24,7 +24,9 @@ class RvqVec(ctypes.Structure):
 class RvqNormArgs(ctypes.Structure):
     _fields_ = [("h", ctypes.c_void_p), ("add", RvqVec), ("token", ctypes.c_void_p),
                 ("embed", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("x", ctypes.c_void_p),
-                ("hidden", ctypes.c_int64), ("eps", ctypes.c_float), ("vocab", ctypes.c_int32)]
+                ("hidden", ctypes.c_int64), ("eps", ctypes.c_float), ("vocab", ctypes.c_int32),
+                ("arrivals", ctypes.c_void_p), ("consumed", ctypes.c_void_p),
+                ("arrivals_per_use", ctypes.c_uint32), ("reserved", ctypes.c_int32)]
 
 
 class RvqAttnArgs(ctypes.Structure):
@@ -82,9 +84,11 @@ def _stream() -> ctypes.c_void_p:
 
 
 class NormOp:
-    """``h <- h + add`` (or ``embed[token]``), ``x <- rmsnorm(h) * weight``."""
+    """``h <- h + add`` (or ``embed[token]``), ``x <- rmsnorm(h) * weight``.
+    ``landing``: a tensor-parallel landing buffer (``PeerExchange.landing``)
+    to wait for and add instead of ``add``."""
 
-    def __init__(self, h, weight, x, eps, add=None, add_tiles=1, token=None, embed=None):
+    def __init__(self, h, weight, x, eps, add=None, add_tiles=1, token=None, embed=None, landing=None):
         hidden = h.numel()
         if weight.numel() != hidden or x.numel() != hidden:
             raise ValueError("h, weight and x must have the same length")
@@ -97,6 +101,12 @@ class NormOp:
                                 None if embed is None else _bf16(embed, "embed"),
                                 _bf16(weight, "weight"), _bf16(x, "x"), hidden, float(eps),
                                 0 if embed is None else int(embed.shape[0]))
+        if landing is not None:
+            if add is not None or token is not None:
+                raise ValueError("landing replaces add and excludes token")
+            self.args.add = RvqVec(landing["add"], hidden, landing["tp"], _native.RVQ_F32)
+            self.args.arrivals, self.args.consumed = landing["arrivals"], landing["consumed"]
+            self.args.arrivals_per_use = landing["per_use"]
 
     def launch(self) -> None:
         rc = _lib().rvq_step_norm(ctypes.byref(self.args), _stream())

@@ -51,11 +51,15 @@ def test_struct_layout_matches_header(lib):
 def test_step_struct_layouts():
     from rvq_b200 import step
     assert ctypes.sizeof(step.RvqVec) == 24
-    assert ctypes.sizeof(step.RvqNormArgs) == 8 + 24 + 4 * 8 + 8 + 4 + 4
+    assert ctypes.sizeof(step.RvqNormArgs) == 8 + 24 + 4 * 8 + 8 + 4 + 4 + 8 + 8 + 4 + 4
     assert ctypes.sizeof(step.RvqAttnArgs) == 3 * 24 + 8 * 8 + 4 * 4 + 4 * 4
     from rvq_b200 import gemv
     assert ctypes.sizeof(gemv.RvqGemvTileJob) == ctypes.sizeof(_native.RvqEntry) + 2 * 24 + 3 * 8
     assert gemv.tiles_count(2560) == 10 and gemv.tiles_count(9728) == 38 and gemv.tiles_count(520) == 3
+    lib = gemv._tiles_lib()
+    assert lib.rvq_tile_codes_bytes(9728, 2560) == 10 * 9728 * 128
+    assert lib.rvq_tile_codes_bytes(5, 520) == 3 * 5 * 128
+    assert lib.rvq_tile_codes_bytes(5, 12) == 0
 
 
 def test_step_calls_reject_bad_arguments(lib):
@@ -79,6 +83,26 @@ def test_step_calls_reject_bad_arguments(lib):
     g = step.RvqVec(8, 100, 1, _native.RVQ_BF16)
     u = step.RvqVec(8, 99, 1, _native.RVQ_BF16)
     assert lib.rvq_step_silu_mul(ctypes.byref(g), ctypes.byref(u), 8, None) == _native.RVQ_ERR_INVALID
+
+
+def test_tp_push_struct_and_host_checks(lib):
+    """Peer-exchange entry points: struct layout, CTA count, argument checks."""
+    from rvq_b200 import step, tp
+    tp._lib()
+    assert ctypes.sizeof(tp.RvqTpPushArgs) == 24 + 2 * 8 * tp.RVQ_MAX_TP + 8 + 4 + 4
+    assert tp.push_ctas(5120) == 5 and tp.push_ctas(1024) == 1 and tp.push_ctas(1025) == 2
+    a = tp.RvqTpPushArgs()
+    a.src = step.RvqVec(8, 64, 1, _native.RVQ_BF16)
+    a.n, a.rank, a.tp = 64, 0, 2
+    a.dst[0], a.arrivals[0] = 8, 8                                  # rank 1's pointers missing
+    assert lib.rvq_tp_push(ctypes.byref(a), None) == _native.RVQ_ERR_INVALID
+    a.tp = tp.RVQ_MAX_TP + 1
+    assert lib.rvq_tp_push(ctypes.byref(a), None) == _native.RVQ_ERR_INVALID
+    a.tp, a.rank = 2, 2
+    assert lib.rvq_tp_push(ctypes.byref(a), None) == _native.RVQ_ERR_INVALID
+    n = step.RvqNormArgs(8, step.RvqVec(8, 64, 2, _native.RVQ_F32), None, None, 8, 8, 64, 1e-6, 0)
+    n.arrivals = 8                                                   # no consumed counter
+    assert lib.rvq_step_norm(ctypes.byref(n), None) == _native.RVQ_ERR_INVALID
 
 
 def test_status_strings(lib):

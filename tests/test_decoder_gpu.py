@@ -142,7 +142,10 @@ def test_fused_steps_track_slot_steps(cuda_device):
 @pytest.mark.parametrize("mode", ["dense", "fused"])
 def test_native_step_tracks_torch_step(mode, cuda_device):
     """The rvq_step kernels against the decoder's PyTorch step on the same
-    tokens: logits within summation-order noise, same greedy ids."""
+    tokens: logits within summation-order noise (dense), or within the fp16
+    table rounding of rvq_gemv_tiles against rvq_gemv's fp32 tables (fused,
+    about 2^-12 relative per GEMV, amplified through the bf16 roundings of
+    4 layers); same greedy ids."""
     art = synthetic.make_model_artifact(MID, 4, 4096, seed=31)
     cfg = synthetic.qwen3_config(MID, 4, 4096)
     prompt = torch.randint(0, 4096, (20,), generator=torch.Generator().manual_seed(4)).to(cuda_device)
@@ -151,5 +154,6 @@ def test_native_step_tracks_torch_step(mode, cuda_device):
     tor = teacher_forced(Qwen3Decoder(cfg, art, cuda_device, mode=mode, max_len=64, step_impl="torch"),
                          prompt, ids)
     assert torch.equal(nat[0], tor[0])            # the prompt runs the same PyTorch ops
+    tol = 1e-2 if mode == "dense" else 2e-2
     for i, (a, b) in enumerate(zip(nat[1:], tor[1:])):
-        assert rel(a, b) < 1e-2, (i, rel(a, b))
+        assert rel(a, b) < tol, (i, rel(a, b))

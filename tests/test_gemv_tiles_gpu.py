@@ -1,8 +1,11 @@
 """GPU: rvq_gemv_tiles (per-tile partial sums) against the oracle's reconstruction.
 
 Each tile's partial sum is compared with the fp64 product of the oracle's
-fp32 weight restricted to that tile's 256 columns; the table-based sum is
-exact up to fp32 rounding (rel. error <= 2e-5 over the whole output).
+fp32 weight restricted to that tile's 256 columns.  The tables hold fp16
+entries of codeword . (2^-E x) (one rounding, relative error <= 2^-11 per
+entry, random in sign), so the sums agree to ~1.5e-4 relative; the bound
+here is TOL = 1e-3, still 4x below the 2^-9 relative rounding of a bf16 weight
+that the reference's reconstruct-then-matmul incurs.
 """
 
 import numpy as np
@@ -12,9 +15,11 @@ import torch.nn.functional as F
 
 from oracle.rvq_oracle import OUT_F32, RVQEntryNP, decode_rvq
 from rvq_b200 import synthetic
-from rvq_b200.gemv import GemvTilesPlan, interleave_codes, tiles_count
+from rvq_b200.gemv import GemvTilesPlan, tile_codes, tiles_count
 
 pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
 
 
 def oracle_w(entry, cb):
@@ -28,7 +33,8 @@ def oracle_w(entry, cb):
 
 def dev_entry(entry, device):
     e = {k: (v.to(device) if torch.is_tensor(v) else v) for k, v in entry.items()}
-    e["codes_il"] = interleave_codes(e["indices"])
+    rows, cols = (int(v) for v in e["shape"])
+    e["codes_tiled"] = tile_codes(e["indices"], rows, cols)
     return e
 
 
@@ -63,8 +69,8 @@ def test_tiles_match_reconstruction(rows, cols, group, cb_dtype, cuda_device):
     w = oracle_w(entry, cb)
     xd = x.double().numpy()
     tp = tile_products(w, xd)
-    assert rel_err(part.cpu().numpy(), tp) <= 2e-5
-    assert rel_err(part.sum(0).cpu().numpy(), w @ xd) <= 2e-5
+    assert rel_err(part.cpu().numpy(), tp) <= TOL
+    assert rel_err(part.sum(0).cpu().numpy(), w @ xd) <= TOL
 
 
 def test_multi_job_launch_and_determinism(cuda_device):
@@ -87,7 +93,7 @@ def test_multi_job_launch_and_determinism(cuda_device):
     torch.cuda.synchronize()
     for e, cb, p, p0 in zip(entries, cbs, parts, first):
         assert torch.equal(p, p0)
-        assert rel_err(p.cpu().numpy(), tile_products(oracle_w(e, cb), x.double().numpy())) <= 2e-5
+        assert rel_err(p.cpu().numpy(), tile_products(oracle_w(e, cb), x.double().numpy())) <= TOL
 
 
 def test_partial_operand_and_fused_silu(cuda_device):
@@ -112,12 +118,30 @@ def test_partial_operand_and_fused_silu(cuda_device):
     GemvTilesPlan([(dev_entry(entry, cuda_device), cb.to(cuda_device, torch.float32), up_p, part, gate_p)]).launch()
     torch.cuda.synchronize()
     w = oracle_w(entry, cb)
-    assert rel_err(part.sum(0).cpu().numpy(), w @ act) <= 2e-5
+    assert rel_err(part.sum(0).cpu().numpy(), w @ act) <= TOL
     # the same with the plain operand (no gate): x = up partials
     part2 = torch.zeros_like(part)
     GemvTilesPlan([(dev_entry(entry, cuda_device), cb.to(cuda_device, torch.float32), up_p, part2)]).launch()
     torch.cuda.synchronize()
-    assert rel_err(part2.sum(0).cpu().numpy(), w @ tile_sum(up_p).double().cpu().numpy()) <= 2e-5
+    assert rel_err(part2.sum(0).cpu().numpy(), w @ tile_sum(up_p).double().cpu().numpy()) <= TOL
+
+
+def test_tile_codes_layout(cuda_device):
+    """rvq_tile_codes against a host restatement of the layout: word (t, r, w)
+    = the stage codes of vector (r, 32 t + w), stage k in byte k, zero past
+    the last group of a row."""
+    g = torch.Generator().manual_seed(14)
+    for rows, cols in [(5, 264), (40, 2560), (3, 8)]:
+        entry = synthetic.make_rvq_entry(rows, cols, g)
+        planes = entry["indices"].numpy().astype(np.uint32)
+        G, nt = cols // 8, tiles_count(cols)
+        words = planes[0] | (planes[1] << 8) | (planes[2] << 16) | (planes[3] << 24)
+        want = np.zeros((nt, rows, 32), np.uint32)
+        for t in range(nt):
+            gs = min(32, G - 32 * t)
+            want[t, :, :gs] = words.reshape(rows, G)[:, 32 * t:32 * t + gs]
+        got = tile_codes(entry["indices"].to(cuda_device), rows, cols).cpu().numpy().view(np.uint32)
+        assert np.array_equal(got.reshape(nt, rows, 32), want)
 
 
 def test_rejects_bad_jobs(cuda_device):

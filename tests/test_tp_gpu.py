@@ -1,10 +1,12 @@
 """GPU (2 devices): the tensor-parallel decoder against the single-GPU one.
 
 Both run the same full model: the TP ranks shard it (rvq_b200/shard.py) and
-all-reduce the row-parallel outputs with NCCL inside the captured step.  The
-sums are re-associated across ranks, so logits agree within a tolerance and
-greedy ids agree wherever the single-GPU margin is above that noise; both
-ranks always produce the same ids.  Skipped with fewer than 2 devices.
+sum the row-parallel outputs inside the captured step, either by peer stores
+into landing buffers (``tp_reduce="push"``, rvq_b200/tp.py) or by an NCCL
+all-reduce.  The sums are re-associated across ranks, so logits agree within
+a tolerance and greedy ids agree wherever the single-GPU margin is above that
+noise; both ranks always produce the same ids.  The 2-rank tests are skipped
+with fewer than 2 devices; the bounded landing wait is tested on one.
 """
 
 import datetime
@@ -23,7 +25,7 @@ pytestmark = pytest.mark.gpu
 SHAPE = synthetic.BlockShape(hidden=512, intermediate=1536, n_heads=8, n_kv_heads=2, head_dim=64)
 
 
-def _worker(rank, world, port, mode, out):
+def _worker(rank, world, port, mode, reduce, out):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dev = torch.device(f"cuda:{rank}")
     torch.cuda.set_device(dev)
@@ -32,9 +34,10 @@ def _worker(rank, world, port, mode, out):
     art = synthetic.make_model_artifact(SHAPE, 3, 2048, seed=41)
     cfg = synthetic.qwen3_config(SHAPE, 3, 2048)
     prompt = torch.randint(0, 2048, (16,), generator=torch.Generator().manual_seed(9)).to(dev)
-    dec = Qwen3Decoder(cfg, art, dev, mode=mode, max_len=48, tp_group=dist.group.WORLD)
+    dec = Qwen3Decoder(cfg, art, dev, mode=mode, max_len=48, tp_group=dist.group.WORLD, tp_reduce=reduce)
     ids, logits = dec.generate(prompt, 10, return_logits=True)
     out[rank] = (ids.cpu(), [l.cpu() for l in logits])
+    dec.close()                                   # raises if a landing wait timed out
     del dec
     torch.cuda.synchronize()
     dist.barrier()
@@ -42,12 +45,13 @@ def _worker(rank, world, port, mode, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["fused", "dense"])
-def test_two_rank_decoder_matches_single_gpu(mode):
+@pytest.mark.parametrize("mode,reduce", [("fused", "push"), ("dense", "push"), ("fused", "nccl"),
+                                         ("dense", "nccl")])
+def test_two_rank_decoder_matches_single_gpu(mode, reduce):
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    port = 29600 + os.getpid() % 300 + (1 if mode == "dense" else 0)
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, out)) for r in range(2)]
+    port = 29600 + os.getpid() % 300 + 2 * (mode == "dense") + (reduce == "nccl")
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, reduce, out)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -71,3 +75,30 @@ def test_two_rank_decoder_matches_single_gpu(mode):
             top = torch.topk(ref_logits[i], 2).values
             assert float(top[0] - top[1]) < 4 * worst, i
             break
+
+
+def test_landing_wait_gives_up_and_flags():
+    """A norm that waits on a counter nothing advances returns after about a
+    second with the timeout flag set; the context stays usable."""
+    import time
+    from rvq_b200 import step, tp
+    dev = torch.device("cuda:0")
+    hidden = 256
+    blk = tp.DeviceBlock(256 + hidden * 4)
+    try:
+        h = torch.zeros(hidden, dtype=torch.bfloat16, device=dev)
+        w = torch.ones(hidden, dtype=torch.bfloat16, device=dev)
+        x = torch.empty(hidden, dtype=torch.bfloat16, device=dev)
+        landing = {"add": blk.ptr + 256, "arrivals": blk.ptr, "consumed": blk.ptr + 4, "per_use": 1, "tp": 1}
+        op = step.NormOp(h, w, x, 1e-6, landing=landing)
+        assert not tp.take_timeout()
+        t0 = time.time()
+        op.launch()
+        torch.cuda.synchronize()
+        assert 0.5 < time.time() - t0 < 30
+        assert tp.take_timeout()
+        assert not tp.take_timeout()                       # sticky until read, then clear
+        assert torch.isfinite(x.float()).all()
+        assert float((torch.ones(4, device=dev) * 2).sum()) == 8.0
+    finally:
+        blk.free()
