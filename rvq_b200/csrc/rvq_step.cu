@@ -57,6 +57,43 @@ __device__ __forceinline__ float vec_value(const rvq_vec& v, int64_t i) {
     return load_as_f32(v.ptr, i, v.kind);
 }
 
+// vec_value with up to 32 partial loads in flight per thread (the tile sum is
+// still taken in tile order): for consumers with few threads per element.
+__device__ __forceinline__ float vec_value_deep(const rvq_vec& v, int64_t i) {
+    if (v.kind != RVQ_F32 || v.ntiles <= 8) return vec_value(v, i);
+    const float* p = reinterpret_cast<const float*>(v.ptr) + i;
+    const int64_t n = v.n;
+    const int nt = v.ntiles;
+    if (nt <= 32) {                                  // one round: 32 loads (clamped to the last tile)
+        float c[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) c[k] = __ldg(p + (int64_t)min(k, nt - 1) * n);
+        float s = c[0];
+#pragma unroll
+        for (int k = 1; k < 32; ++k)
+            if (k < nt) s += c[k];
+        return bf16r(s);
+    }
+    float s = __ldg(p);
+    int t = 1;
+    for (; t + 32 <= nt; t += 32) {                  // whole chunks: 32 loads, then the adds in order
+        float c[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) c[k] = __ldg(p + (int64_t)(t + k) * n);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) s += c[k];
+    }
+    for (; t + 8 <= nt; t += 8) {
+        float c[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) c[k] = __ldg(p + (int64_t)(t + k) * n);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += c[k];
+    }
+    for (; t < nt; ++t) s += __ldg(p + (int64_t)t * n);
+    return bf16r(s);
+}
+
 __device__ int g_tp_timeout;                 // sticky: a landing-buffer wait gave up
 
 // Operand read through L2 (a landing buffer that peers write over NVLink:
@@ -106,7 +143,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // memory in rank order (deterministic).
 // ---------------------------------------------------------------------------
 constexpr int kNormCtas = 8;
-constexpr int kNormThreads = 512;
+constexpr int kNormThreads = 1024;
 constexpr int kNormMaxSlice = 2048;     // hidden <= 16384
 
 __global__ void __cluster_dims__(kNormCtas, 1, 1) __launch_bounds__(kNormThreads)
@@ -145,7 +182,7 @@ step_norm_kernel(rvq_norm_args a) {
     } else {
         for (int64_t i = lo + tid; i < hi; i += kNormThreads) {
             float hv = bf16_at(a.h, i);
-            if (a.add.ptr != nullptr) hv = bf16r(hv + (landing ? vec_value_l2(a.add, i) : vec_value(a.add, i)));
+            if (a.add.ptr != nullptr) hv = bf16r(hv + (landing ? vec_value_l2(a.add, i) : vec_value_deep(a.add, i)));
             hbuf[i - lo] = hv;
             ss = fmaf(hv, hv, ss);
         }
@@ -300,22 +337,21 @@ step_attn_kernel(rvq_attn_args a) {
         wsm[i] = bf16_at(src, (which >= 2 ? pos * HD : 0) + d);
     }
     pdl_wait();                                      // q, k, v come from the previous kernel
-    for (int base = 0; base < (rep + 2) * HD; base += 6 * kAttnThreads) {
-        float val[6];
-#pragma unroll
-        for (int m = 0; m < 6; ++m) {
-            const int i = base + tid + m * kAttnThreads;
-            const int r = i / HD, d = i - r * HD;
-            val[m] = 0.f;
-            if (r < rep) val[m] = vec_value(a.q, ((int64_t)kv * rep + r) * HD + d);
-            else if (r == rep) val[m] = vec_value(a.k, (int64_t)kv * HD + d);
-            else if (r == rep + 1) val[m] = vec_value(a.v, (int64_t)kv * HD + d);
-        }
-#pragma unroll
-        for (int m = 0; m < 6; ++m) {
-            const int i = base + tid + m * kAttnThreads;
-            if (i < (rep + 2) * HD) raw[i] = val[m];
-        }
+    // the operands' tile sums are split over the cluster (CTA `rank` sums
+    // elements [rank * och, (rank + 1) * och), all tile loads of an element in
+    // flight), then every CTA gathers the other ranges over DSMEM
+    const int nel = (rep + 2) * HD;
+    const int och = (nel + kAttnCtas - 1) / kAttnCtas;
+    for (int i = rank * och + tid; i < min(nel, (rank + 1) * och); i += kAttnThreads) {
+        const int r = i / HD, d = i - r * HD;
+        raw[i] = r < rep ? vec_value_deep(a.q, ((int64_t)kv * rep + r) * HD + d)
+               : r == rep ? vec_value_deep(a.k, (int64_t)kv * HD + d)
+                          : vec_value_deep(a.v, (int64_t)kv * HD + d);
+    }
+    cluster.sync();
+    for (int i = tid; i < nel; i += kAttnThreads) {
+        const int c = i / och;
+        if (c != rank) raw[i] = cluster.map_shared_rank(raw, c)[i];
     }
     __syncthreads();
 
