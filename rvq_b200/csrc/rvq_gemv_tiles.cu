@@ -211,33 +211,6 @@ __device__ __forceinline__ void load_batch(uint32_t dst, const uint32_t* lines, 
     bulk_load(dst, lines + (int64_t)r * kLineWords, (uint32_t)n * kLineWords * 4, bar);
 }
 
-// Reduce 8 per-lane values (rows 0..7) over the warp: returns the total of row
-// (lane >> 2) & 7 (in every lane of that row's quad).  9 shuffles, fixed order.
-__device__ __forceinline__ float reduce8(const float (&v)[8]) {
-    const int lane = threadIdx.x & 31;
-    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-    float u[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float send = b4 ? v[i] : v[i + 4];
-        const float keep = b4 ? v[i + 4] : v[i];
-        u[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-    float w[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const float send = b3 ? u[i] : u[i + 2];
-        const float keep = b3 ? u[i + 2] : u[i];
-        w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-    const float send = b2 ? w[0] : w[1];
-    const float keep = b2 ? w[1] : w[0];
-    float z = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    z += __shfl_xor_sync(0xffffffffu, z, 2);
-    z += __shfl_xor_sync(0xffffffffu, z, 1);
-    return z;
-}
-
 // ---------------------------------------------------------------------------
 // The tile's table: word (c, pair, g) = fp16 pair (cb[2 pair][c] . x'_g,
 // cb[2 pair + 1][c] . x'_g), x'_g = 2^-E x[8g : 8g + 8].

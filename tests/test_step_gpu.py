@@ -86,9 +86,12 @@ def torch_attention(q, k, v, qn, kn, cos, sin, pos, kc, vc, nh, nkv, hd, eps, sc
 @pytest.mark.parametrize("nh,nkv,hd,pos,bias,partials", [
     (32, 8, 128, 0, 1.0, False), (32, 8, 128, 127, 1.0, False), (32, 8, 128, 300, 0.0, True),
     (64, 8, 128, 200, 1.0, True), (8, 2, 64, 50, 1.0, False), (16, 16, 256, 17, 0.0, False)])
-def test_attention_matches_torch(nh, nkv, hd, pos, bias, partials, cuda_device):
+@pytest.mark.parametrize("short_cache", [False, True])
+def test_attention_matches_torch(nh, nkv, hd, pos, bias, partials, short_cache, cuda_device):
+    """A 512-row cache and one of pos + 40 rows (the keys split over the
+    8-CTA cluster differ)."""
     g = torch.Generator().manual_seed(nh * 1000 + pos)
-    max_len = 512
+    max_len = pos + 40 if short_cache else 512
     dev = cuda_device
     bf = torch.bfloat16
     kc = (torch.randn(nkv, max_len, hd, generator=g)).to(dev, bf)
