@@ -256,6 +256,52 @@ __device__ __forceinline__ void build_lut_f16(uint32_t* __restrict__ lut, const 
     }
 }
 
+// The same table from an fp16 codebook ([4][256] rows of 8 halves, 16 KB) and
+// x' in fp16: one 16-byte broadcast load per codebook row instead of two, the
+// 8-term dot products by fma.rn.f32.f16 (exact products, fp32 accumulation in
+// element order, as the fp32 build).
+__device__ __forceinline__ float dot8_h(const uint4& c, const uint32_t (&xh)[4]) {
+    float acc;
+    asm("{\n .reg .b16 c0, c1, c2, c3, c4, c5, c6, c7, x0, x1, x2, x3, x4, x5, x6, x7;\n"
+        " mov.b32 {c0, c1}, %1;\n mov.b32 {c2, c3}, %2;\n mov.b32 {c4, c5}, %3;\n mov.b32 {c6, c7}, %4;\n"
+        " mov.b32 {x0, x1}, %5;\n mov.b32 {x2, x3}, %6;\n mov.b32 {x4, x5}, %7;\n mov.b32 {x6, x7}, %8;\n"
+        " fma.rn.f32.f16 %0, c0, x0, 0f00000000;\n fma.rn.f32.f16 %0, c1, x1, %0;\n"
+        " fma.rn.f32.f16 %0, c2, x2, %0;\n fma.rn.f32.f16 %0, c3, x3, %0;\n"
+        " fma.rn.f32.f16 %0, c4, x4, %0;\n fma.rn.f32.f16 %0, c5, x5, %0;\n"
+        " fma.rn.f32.f16 %0, c6, x6, %0;\n fma.rn.f32.f16 %0, c7, x7, %0;\n}\n"
+        : "=f"(acc)
+        : "r"(c.x), "r"(c.y), "r"(c.z), "r"(c.w), "r"(xh[0]), "r"(xh[1]), "r"(xh[2]), "r"(xh[3]));
+    return acc;
+}
+
+__device__ __forceinline__ void build_lut_h(uint32_t* __restrict__ lut, const uint4* __restrict__ cbh,
+                                            const float* __restrict__ xs, float xscale) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t xh[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 h = __floats2half2_rn(xs[lane * 8 + 2 * i] * xscale, xs[lane * 8 + 2 * i + 1] * xscale);
+        xh[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+#pragma unroll 1
+    for (int p0 = warp; p0 < kCodes * 2; p0 += kWarps * 2) {
+        uint4 c[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {            // j = 2 * word + stage within the pair
+            const int p = p0 + (j >> 1) * kWarps, code = p >> 1, k = ((p & 1) << 1) + (j & 1);
+            c[j] = cbh[k * kCodes + code];
+        }
+        float acc[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = dot8_h(c[j], xh);
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            const __half2 h = __floats2half2_rn(acc[2 * w], acc[2 * w + 1]);    // low half: even stage
+            lut[(p0 + w * kWarps) * kGroups + lane] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+    }
+}
+
 __device__ __forceinline__ uint32_t* ring_slot(uint32_t* ring, int slot) { return ring + slot * kBatchRows * kGroups; }
 
 // Power-of-two scale 2^-E bringing max |x| = amax into [1, 2), and 2^E.
@@ -294,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
 
     const int u_first = p.cta_first[blockIdx.x], u_last = p.cta_first[blockIdx.x + 1];
     int cb_job = -1;                                     // job whose codebook is in shared memory
+    bool cb_half = false;                                // ... staged as fp16 (else fp32)
     for (int u = u_first; u < u_last; ++u) {
         const uint32_t jt = p.unit_jt[u];
         const int ji = (int)(jt >> 24);
@@ -318,12 +365,31 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
         // 2. codebook (fp32) and the tile's operand slice; partial-sum operands
         //    are staged in the table's space, then summed in tile order
         if (ji != cb_job) {
+            // fp16 when every codebook value is an fp16 number (the artifact's
+            // codebooks are fp16), else fp32
             cb_job = ji;
-            if (J.cb_kind == RVQ_F32) {
-                const float4* cb4 = reinterpret_cast<const float4*>(J.cb);
-                for (int i = tid; i < kCbFloats / 4; i += kThreads) cp_async16(cbs + 4 * i, cb4 + i);
+            uint4* cbh = reinterpret_cast<uint4*>(cbs);
+            int inexact = 0;
+            if (J.cb_kind == RVQ_F16) {
+                const uint4* src = reinterpret_cast<const uint4*>(J.cb);
+                for (int i = tid; i < kPairs; i += kThreads) cp_async16(cbh + i, src + i);
                 cp_async_commit();
             } else {
+                for (int i = tid; i < kPairs; i += kThreads) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float f0 = load_as_f32(J.cb, (int64_t)i * 8 + 2 * t, J.cb_kind);
+                        const float f1 = load_as_f32(J.cb, (int64_t)i * 8 + 2 * t + 1, J.cb_kind);
+                        const __half2 h = __floats2half2_rn(f0, f1);
+                        inexact |= (__low2float(h) != f0) | (__high2float(h) != f1);
+                        w[t] = *reinterpret_cast<const uint32_t*>(&h);
+                    }
+                    cbh[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            cb_half = !__syncthreads_or(inexact);
+            if (!cb_half) {
                 for (int i = tid; i < kCbFloats; i += kThreads) cbs[i] = load_as_f32(J.cb, i, J.cb_kind);
             }
         }
@@ -362,7 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
         for (int w = 1; w < kTileCols / 32; ++w) amax = fmaxf(amax, xmax[w]);
         float xscale, xunscale;
         tile_scale(amax, xscale, xunscale);
-        build_lut_f16(lut, cbs, xs, xscale);
+        if (cb_half) build_lut_h(lut, reinterpret_cast<const uint4*>(cbs), xs, xscale);
+        else build_lut_f16(lut, cbs, xs, xscale);
         __syncthreads();
 
         // 4. rows, batch by batch, three batches streaming in while one is processed.

@@ -382,7 +382,7 @@ class Qwen3Decoder:
             }
             if fused:
                 E = L["entries"]
-                cb = lambda n: self.codebooks[E[n]["codebook_id"]]
+                cb = lambda n: self._cb_tiles(E[n]["codebook_id"])
                 ops["qkv"] = GemvTilesPlan([(E[PROJ[0]], cb(PROJ[0]), self.x_attn, self.q_part),
                                             (E[PROJ[1]], cb(PROJ[1]), self.x_attn, self.k_part),
                                             (E[PROJ[2]], cb(PROJ[2]), self.x_attn, self.v_part)])
@@ -396,6 +396,17 @@ class Qwen3Decoder:
             self.step_ops.append(ops)
         self.final_op = NormOp(self.h, self.final_norm, self.x_final, d.eps, add=None if land_d else down,
                                add_tiles=tiles(down), landing=land_d)
+
+    def _cb_tiles(self, cid: str) -> torch.Tensor:
+        """The codebook handed to rvq_gemv_tiles: fp16 when every value is an
+        fp16 number (the artifact stores fp16 codebooks; the kernel then loads
+        it without converting), else the fp32 copy."""
+        cache = self.__dict__.setdefault("_cb16", {})
+        if cid not in cache:
+            cb = self.codebooks[cid]
+            h = cb.to(torch.float16)
+            cache[cid] = h if torch.equal(h.to(cb.dtype), cb) else cb
+        return cache[cid]
 
     @staticmethod
     def _mv(w: torch.Tensor, x: torch.Tensor, y: torch.Tensor) -> None:

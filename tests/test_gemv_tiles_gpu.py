@@ -56,10 +56,15 @@ def tile_products(w, x):
     (333, 520, None, torch.float32),       # ragged last tile (1 group), odd rows
     (8, 8, 8, torch.float32),              # one vector per row
     (3000, 1000, 40, torch.float32),       # G = 125: rows not 16-byte aligned, 5 vectors per scale
+    (2048, 2560, None, "f32_not_f16"),     # fp32 codebook that fp16 cannot hold: fp32 staging
 ])
 def test_tiles_match_reconstruction(rows, cols, group, cb_dtype, cuda_device):
     g = torch.Generator().manual_seed(rows + 3 * cols)
     cb = synthetic.make_codebook(4, 256, 8, g)
+    if cb_dtype == "f32_not_f16":
+        cb = cb.float() * (1 + 1e-6 * torch.randn(cb.shape, generator=g))
+        assert not torch.equal(cb.half().float(), cb)
+        cb_dtype = torch.float32
     entry = synthetic.make_rvq_entry(rows, cols, g, group_size=group)
     x = torch.randn(cols, generator=g).to(torch.bfloat16)
     part = torch.full((tiles_count(cols), rows), float("nan"), device=cuda_device)
