@@ -349,9 +349,18 @@ step_attn_kernel(rvq_attn_args a) {
                           : vec_value_deep(a.v, (int64_t)kv * HD + d);
     }
     cluster.sync();
-    for (int i = tid; i < nel; i += kAttnThreads) {
-        const int c = i / och;
-        if (c != rank) raw[i] = cluster.map_shared_rank(raw, c)[i];
+    for (int base = 0; base < nel; base += 6 * kAttnThreads) {   // 6 DSMEM loads in flight, then the stores
+        float val[6];
+#pragma unroll
+        for (int m = 0; m < 6; ++m) {
+            const int i = min(base + tid + m * kAttnThreads, nel - 1);
+            val[m] = cluster.map_shared_rank(raw, i / och)[i];
+        }
+#pragma unroll
+        for (int m = 0; m < 6; ++m) {
+            const int i = base + tid + m * kAttnThreads;
+            if (i < nel && i / och != rank) raw[i] = val[m];
+        }
     }
     __syncthreads();
 
@@ -379,10 +388,14 @@ step_attn_kernel(rvq_attn_args a) {
     }
     __syncthreads();
 
-    // 3. scores: warp per key, lanes over head_dim; rows of kKeyChunk keys loaded first
-    float mx[kMaxRep];
+    // 3. scores: warp per key, lanes over head_dim; rows of kKeyChunk keys loaded
+    //    first; the rep heads' lane partials are reduced 8 heads at a time by one
+    //    reduce-scatter (lane quad q ends up with head 8 g + q)
+    constexpr int kGroupsMax = kMaxRep / 8;
+    const int hq = (lane >> 2) & 7;                   // this lane quad's head within a group of 8
+    float mx[kGroupsMax];
 #pragma unroll
-    for (int r = 0; r < kMaxRep; ++r) mx[r] = -INFINITY;
+    for (int g = 0; g < kGroupsMax; ++g) mx[g] = -INFINITY;
     for (int jb = j0 + warp; jb < j1; jb += kAttnWarps * kKeyChunk) {
         float kd[kKeyChunk][E];
 #pragma unroll
@@ -403,23 +416,33 @@ step_attn_kernel(rvq_attn_args a) {
             const int j = jb + c * kAttnWarps;
             if (j >= j1) break;                               // warp-uniform
 #pragma unroll
-            for (int r = 0; r < kMaxRep; ++r) {
-                if (r < rep) {
-                    float t = 0.f;
+            for (int g = 0; g < kGroupsMax; ++g) {
+                if (8 * g < rep) {
+                    float pr[8];
 #pragma unroll
-                    for (int e = 0; e < E; ++e) t = fmaf(qs[r * HD + d0 + e], kd[c][e], t);
-                    t = warp_sum(t);
-                    const float sv = bf16r(bf16r(bf16r(t) * a.scaling) + a.valid_bias);
-                    if (lane == 0) sc[r * kpc_max + (j - j0)] = sv;
-                    mx[r] = fmaxf(mx[r], sv);
+                    for (int r = 0; r < 8; ++r) {
+                        float t = 0.f;
+                        if (8 * g + r < rep) {
+#pragma unroll
+                            for (int e = 0; e < E; ++e) t = fmaf(qs[(8 * g + r) * HD + d0 + e], kd[c][e], t);
+                        }
+                        pr[r] = t;
+                    }
+                    const float t = reduce8(pr);
+                    const int r = 8 * g + hq;
+                    if (r < rep) {
+                        const float sv = bf16r(bf16r(bf16r(t) * a.scaling) + a.valid_bias);
+                        if ((lane & 3) == 0) sc[r * kpc_max + (j - j0)] = sv;
+                        mx[g] = fmaxf(mx[g], sv);
+                    }
                 }
             }
         }
     }
-    if (lane == 0) {
+    if ((lane & 3) == 0) {
 #pragma unroll
-        for (int r = 0; r < kMaxRep; ++r)
-            if (r < rep) red[r][warp] = mx[r];
+        for (int g = 0; g < kGroupsMax; ++g)
+            if (8 * g + hq < rep) red[8 * g + hq][warp] = mx[g];
     }
     __syncthreads();
     if (tid < rep) {
@@ -441,10 +464,13 @@ step_attn_kernel(rvq_attn_args a) {
             if (r < rep) sm[r] += expf(sc[r * kpc_max + (j - j0)] - mloc[r]);
     }
 #pragma unroll
-    for (int r = 0; r < kMaxRep; ++r) {
-        if (r < rep) {
-            const float t = warp_sum(sm[r]);
-            if (lane == 0) red[r][warp] = t;
+    for (int g = 0; g < kGroupsMax; ++g) {
+        if (8 * g < rep) {
+            float pr[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) pr[r] = sm[8 * g + r];
+            const float t = reduce8(pr);
+            if ((lane & 3) == 0 && 8 * g + hq < rep) red[8 * g + hq][warp] = t;
         }
     }
     __syncthreads();
@@ -455,14 +481,19 @@ step_attn_kernel(rvq_attn_args a) {
     }
     cluster.sync();
     if (tid < rep) {
-        float m = -INFINITY;
-        for (int c = 0; c < kAttnCtas; ++c) m = fmaxf(m, cluster.map_shared_rank(mloc, c)[tid]);
-        float t = 0.f;
+        float mcs[kAttnCtas], scs[kAttnCtas];                 // every CTA's max and sum, one round trip
+#pragma unroll
         for (int c = 0; c < kAttnCtas; ++c) {
-            const float mc = cluster.map_shared_rank(mloc, c)[tid];
-            const float sc_ = cluster.map_shared_rank(sloc, c)[tid];
-            if (sc_ > 0.f) t += sc_ * expf(mc - m);
+            mcs[c] = cluster.map_shared_rank(mloc, c)[tid];
+            scs[c] = cluster.map_shared_rank(sloc, c)[tid];
         }
+        float m = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kAttnCtas; ++c) m = fmaxf(m, mcs[c]);
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < kAttnCtas; ++c)
+            if (scs[c] > 0.f) t += scs[c] * expf(mcs[c] - m);
         gmax[tid] = m;
         gsum[tid] = t;
     }
