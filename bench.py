@@ -348,9 +348,11 @@ def batch1_leg(world, device):
     """Batch-1 greedy generation, ms/token (the metric's second half).  N=1:
     the 36-layer 2560/9728 model (fused RVQ GEMV and the dense bf16 model)
     and the 64-layer 5120/25600 model; N>1: the 64-layer model tensor-parallel
-    over the N GPUs (NCCL all-reduce after the row-parallel projections)."""
+    over the N GPUs (row-parallel outputs summed by peer stores over NVLink into
+    every rank's landing buffer, rvq_b200/tp.py)."""
     from rvq_b200 import bench_tp, synthetic
     out = {"prompt_tokens": 128, "new_tokens": 128, "timing": "device time per token, max over ranks",
+           "tp_reduce": "push (peer stores into landing buffers)" if world > 1 else None,
            "data": "synthetic random-init weights generated on the GPU, seeded"}
     try:
         group = torch.distributed.group.WORLD if world > 1 else None
