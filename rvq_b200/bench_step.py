@@ -13,7 +13,9 @@ position 130; prints us per layer for each, the final norm + head, and the
 whole step (CUDA events).  ``one-step``: prefill 16 ids and one eager decode
 step (the launches an ncu capture selects from).  ``generate``: greedy
 generation replaying the captured step.  The config-1 block is 2560 / 9728 /
-32q / 8kv / 128, the config-4 block 5120 / 25600 / 64q / 8kv / 128.
+32q / 8kv / 128, the config-4 block 5120 / 25600 / 64q / 8kv / 128.  With
+``--tp N`` the kernels are timed on one rank's share of a TP=N model (heads,
+kv heads and intermediate divided by N; no reduction).
 """
 
 from __future__ import annotations
@@ -32,15 +34,23 @@ BLOCKS = {
 }
 
 
-def build(block: str, layers: int, vocab: int, max_len: int, device) -> Qwen3Decoder:
-    shape = BLOCKS[block]
+def rank_shape(block: str, tp: int) -> synthetic.BlockShape:
+    """One tensor-parallel rank's share of the block: heads, kv heads and the
+    intermediate size divided by tp (the shapes each GPU runs at TP = tp)."""
+    b = BLOCKS[block]
+    return synthetic.BlockShape(hidden=b.hidden, intermediate=b.intermediate // tp, n_heads=b.n_heads // tp,
+                                n_kv_heads=b.n_kv_heads // tp, head_dim=b.head_dim)
+
+
+def build(block: str, layers: int, vocab: int, max_len: int, device, tp: int = 1) -> Qwen3Decoder:
+    shape = rank_shape(block, tp)
     cfg = synthetic.qwen3_config(shape, layers, vocab)
     art = synthetic.make_tp_shard_artifact(shape, layers, vocab, 0, 1, seed=0, device=device)
     return Qwen3Decoder(cfg, art, device, mode="fused", max_len=max_len)
 
 
-def time_kernels(block: str, layers: int, device) -> dict:
-    dec = build(block, layers, 151936, 256, device)
+def time_kernels(block: str, layers: int, device, tp: int = 1) -> dict:
+    dec = build(block, layers, 151936, 256, device, tp)
     prompt = torch.randint(0, 151936, (128,), generator=torch.Generator().manual_seed(1)).to(device)
     dec.generate(prompt, 4)
     dec._pos.fill_(130)
@@ -78,7 +88,7 @@ def time_kernels(block: str, layers: int, device) -> dict:
         lambda: (dec.final_op.launch(), dec._mv(dec.lm_head, dec.x_final, dec.logits_buf))), 2)
     res["step_per_layer_incl_head"] = round(graph_us(dec._step_native) / layers, 2)
     dec.close()
-    return {"block": block, "layers": layers, "us_per_layer": res,
+    return {"block": block, "tp_rank_share": tp, "layers": layers, "us_per_layer": res,
             "timing": "each kernel replayed alone from a CUDA graph over all layers, CUDA events"}
 
 
@@ -107,11 +117,12 @@ def main(argv=None):
     ap.add_argument("--block", choices=tuple(BLOCKS), default="config1")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--new", type=int, default=24)
+    ap.add_argument("--tp", type=int, default=1, help="time one rank's share of a TP=tp model (kernels only)")
     a = ap.parse_args(argv)
     device = torch.device("cuda:0")
     torch.cuda.set_device(device)
     if a.what == "kernels":
-        print(json.dumps(time_kernels(a.block, a.layers, device)))
+        print(json.dumps(time_kernels(a.block, a.layers, device, a.tp)))
     elif a.what == "one-step":
         one_step(a.block, a.layers, device)
         print("ok")

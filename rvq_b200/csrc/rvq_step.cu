@@ -660,8 +660,8 @@ extern "C" int rvq_step_silu_mul(const rvq_vec* gate, const rvq_vec* up, void* o
 namespace rvq {
 namespace {
 
-constexpr int kPushThreads = 256;
-constexpr int kPushPerThread = 4;
+constexpr int kPushThreads = 128;
+constexpr int kPushPerThread = 1;     // one element per thread: its tile loads all in flight
 
 struct TpPush {
     rvq_vec src;
@@ -671,23 +671,47 @@ struct TpPush {
     int32_t rank, tp;
 };
 
-// fp32 value of the projection output (tiles summed in order, not rounded)
+// A read-only load issued where it is written (the chunk's loads leave before any add).
+__device__ __forceinline__ float ldg_now(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];\n" : "=f"(v) : "l"(p));
+    return v;
+}
+
+// fp32 value of the projection output (tiles summed in order, not rounded),
+// 32 tile loads in flight at a time
 __device__ __forceinline__ float vec_value_f32(const rvq_vec& v, int64_t i) {
-    if (v.kind == RVQ_F32) {
-        const float* p = reinterpret_cast<const float*>(v.ptr) + i;
-        float s = __ldg(p);
-        int t = 1;
-        for (; t + 8 <= v.ntiles; t += 8) {
-            float c[8];
+    if (v.kind != RVQ_F32) return load_as_f32(v.ptr, i, v.kind);
+    const float* p = reinterpret_cast<const float*>(v.ptr) + i;
+    const int64_t n = v.n;
+    const int nt = v.ntiles;
+    float s = __ldg(p);
+    int t = 1;
+    for (; t + 32 <= nt; t += 32) {
+        float c[32];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) c[k] = __ldg(p + (int64_t)(t + k) * v.n);
+        for (int k = 0; k < 32; ++k) c[k] = ldg_now(p + (int64_t)(t + k) * n);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) s += c[k];
-        }
-        for (; t < v.ntiles; ++t) s += __ldg(p + (int64_t)t * v.n);
-        return s;
+        for (int k = 0; k < 32; k += 8)             // every load issued before the first add
+            asm volatile("" : "+f"(c[k]), "+f"(c[k + 1]), "+f"(c[k + 2]), "+f"(c[k + 3]), "+f"(c[k + 4]),
+                         "+f"(c[k + 5]), "+f"(c[k + 6]), "+f"(c[k + 7]));
+#pragma unroll
+        for (int k = 0; k < 32; ++k) s += c[k];
     }
-    return load_as_f32(v.ptr, i, v.kind);
+    if (t < nt) {                                   // the rest: clamped loads, adds in order
+        float c[31];
+#pragma unroll
+        for (int k = 0; k < 31; ++k) c[k] = ldg_now(p + (int64_t)min(t + k, nt - 1) * n);
+#pragma unroll
+        for (int k = 0; k < 24; k += 8)
+            asm volatile("" : "+f"(c[k]), "+f"(c[k + 1]), "+f"(c[k + 2]), "+f"(c[k + 3]), "+f"(c[k + 4]),
+                         "+f"(c[k + 5]), "+f"(c[k + 6]), "+f"(c[k + 7]));
+        asm volatile("" : "+f"(c[24]), "+f"(c[25]), "+f"(c[26]), "+f"(c[27]), "+f"(c[28]), "+f"(c[29]), "+f"(c[30]));
+#pragma unroll
+        for (int k = 0; k < 31; ++k)
+            if (t + k < nt) s += c[k];
+    }
+    return s;
 }
 
 __global__ void __launch_bounds__(kPushThreads) tp_push_kernel(TpPush a) {

@@ -90,7 +90,7 @@ def test_tp_push_struct_and_host_checks(lib):
     from rvq_b200 import step, tp
     tp._lib()
     assert ctypes.sizeof(tp.RvqTpPushArgs) == 24 + 2 * 8 * tp.RVQ_MAX_TP + 8 + 4 + 4
-    assert tp.push_ctas(5120) == 5 and tp.push_ctas(1024) == 1 and tp.push_ctas(1025) == 2
+    assert tp.push_ctas(5120) == 40 and tp.push_ctas(128) == 1 and tp.push_ctas(129) == 2
     a = tp.RvqTpPushArgs()
     a.src = step.RvqVec(8, 64, 1, _native.RVQ_BF16)
     a.n, a.rank, a.tp = 64, 0, 2
