@@ -44,6 +44,8 @@ WORKLOAD = ("config1 ping-pong slot fill: Qwen-style block hidden 2560 / interme
             "32q 8kv head 128, 7 RVQ projections (K=4, 256 codes, d=8, per-row fp16 scales) "
             "+ 4 bf16 norms -> bf16 slot")
 N_LAYERS_ROTATED = 8
+# slot writes + code reads + scale reads of the 7 projections, plus the 4 bf16 norm copies
+BYTES_PER_STEP = 252396544
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -207,16 +209,70 @@ def time_cpu_port(sample, seconds: float, min_reps: int = 1):
     return algo * reps / el / 1e9, threads, reps, el, algo
 
 
+def torch_block_sample(seed: int = 0):
+    """The RVQ entries of one config-1 block as CPU torch tensors, with their
+    codebooks and bf16 outputs, for the PyTorch restatement of the reference's
+    ``_decode_rvq_into``."""
+    from rvq_b200 import synthetic
+    art = synthetic.make_block_artifact(seed=seed)
+    items = []
+    for key, e in art["entries"].items():
+        if e["method"] != "rvq_groupwise":
+            continue
+        cb = art["shared_codebooks"][e["codebook_id"]].float()
+        out = torch.empty(tuple(e["shape"]), dtype=torch.bfloat16)
+        items.append((e, cb, out))
+    return items
+
+
+def time_torch_port(seconds: float, min_reps: int = 1):
+    """The reference's PyTorch CPU reconstruction (oracle.torch_port restates
+    infer_compressed_layerwise_single_slot.py:123-149) over whole config-1
+    blocks, with every host thread; returns (GB/s, threads, blocks, s)."""
+    from oracle.torch_port import decode_rvq_into
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    items = torch_block_sample()
+    algo = sum(e["indices"].numel() + e["scales"].numel() * 2 + out.numel() * 2 for e, _, out in items)
+    for e, cb, out in items:                 # warm-up (page-in, allocator)
+        decode_rvq_into(e, cb, out)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for e, cb, out in items:
+            decode_rvq_into(e, cb, out)
+        reps += 1
+        el = time.perf_counter() - t0
+        if reps >= min_reps and el >= seconds:
+            break
+    return algo * reps / el / 1e9, threads, reps, el
+
+
+def cpu_baselines(seconds: float):
+    """Both CPU figures on this host: the C/OpenMP port (the stronger one,
+    reported as ``value``) and the PyTorch restatement of the reference's own
+    function (``torch_port``), each over whole config-1 blocks."""
+    sample = cpu_block_sample(1.0)
+    v, threads, reps, el, algo = time_cpu_port(sample, seconds)
+    tv, tthreads, treps, tel = time_torch_port(seconds)
+    return {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full config-1 block decode(s) ({algo} algorithmic bytes each), "
+                      f"C/OpenMP port of the reference reconstruction, bf16 out, {el:.1f} s",
+            "torch_port": {"value": round(tv, 4), "unit": "GB/s", "cores": tthreads,
+                           "sample": f"{treps} full config-1 block decode(s), PyTorch restatement of the "
+                                     f"reference's _decode_rvq_into (same ops, torch.set_num_threads"
+                                     f"({tthreads})), bf16 out, {tel:.1f} s"}}
+
+
 def run_reference_arm(args, world, rank):
+    """The reference's CPU reconstruction of the same workload as the GPU arm:
+    every step decodes one whole config-1 block (7 projections) into bf16 on
+    the host's cores with the C/OpenMP port; rank 0 only."""
     if rank != 0:
         return
-    # per step: 1/16 of every projection's rows of one block (contiguous)
-    frac = 1.0 / 16.0
-    sample = cpu_block_sample(frac)
-    import numpy as np
-
+    sample = cpu_block_sample(1.0)
     from oracle.c_oracle import decode_rvq_bits_c, max_threads
     from oracle.rvq_oracle import OUT_BF16
+    import numpy as np
     threads = max_threads()
     bufs = [np.empty(e.numel, np.uint16) for e, _ in sample]
     algo = sum(a for _, a in sample)
@@ -232,16 +288,20 @@ def run_reference_arm(args, world, rank):
         step()
     el = time.perf_counter() - t0
     gbs = algo * args.steps / el / 1e9
-    desc = (f"1/16 of the rows of each of the 7 projections of one config-1 block per step "
-            f"({algo} algorithmic bytes), C/OpenMP port of the reference reconstruction, bf16 out")
+    desc = (f"one whole config-1 block per step ({algo} algorithmic bytes: 7 projections, bf16 out), "
+            f"C/OpenMP port of the reference reconstruction on {threads} host threads")
+    tv, tthreads, treps, tel = time_torch_port(min(args.cpu_seconds, 10.0))
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": desc},
+        "config": gpu_config(world),
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": desc},
+                         "kind": "port", "sample": desc,
+                         "torch_port": {"value": round(tv, 4), "unit": "GB/s", "cores": tthreads,
+                                        "sample": f"{treps} whole block(s) in {tel:.1f} s, PyTorch "
+                                                  f"restatement of the reference's _decode_rvq_into"}},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -251,6 +311,15 @@ def run_reference_arm(args, world, rank):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+
+def gpu_config(world: int) -> dict:
+    """The workload description both arms print."""
+    return {"workload": WORKLOAD, "bytes_per_step_per_gpu": BYTES_PER_STEP,
+            "weights_per_step_per_gpu": 100925440, "layers_rotated": N_LAYERS_ROTATED,
+            "slots": 2, "l2": "inputs larger than L2: >250 MB touched per step, 8 distinct layers rotated",
+            "timed_region": "K steps replayed from one CUDA graph on the launching stream",
+            "parallelism": f"independent per-GPU decode x{world}"}
+
 
 def build_layers(device, n_layers):
     """n_layers distinct copies of one seeded block resident on the device,
@@ -275,7 +344,9 @@ def build_layers(device, n_layers):
 
 def time_device(plans, steps, warmup, stream, world):
     """W eager warm-up steps, then exactly K steps replayed from one CUDA graph
-    (the same launches, without host launch gaps between them)."""
+    (the same launches, without host launch gaps between them).  The graph is
+    replayed once untimed first, so its upload and first-launch costs stay
+    outside the timed region."""
     for s in range(warmup):
         plans[s % len(plans)].launch(stream.cuda_stream)
     torch.cuda.synchronize()
@@ -283,6 +354,9 @@ def time_device(plans, steps, warmup, stream, world):
     with torch.cuda.graph(graph, stream=stream):
         for s in range(steps):
             plans[s % len(plans)].launch(stream.cuda_stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -381,6 +455,8 @@ def run_ours(args, world, rank, local):
         raise RuntimeError("rvq_b200 CUDA library has no usable sm_100 device")
     art, rel, cbs, slots, layers, plans = build_layers(device, N_LAYERS_ROTATED)
     bytes_per_step = plans[0].algorithmic_bytes
+    if bytes_per_step != BYTES_PER_STEP:
+        raise RuntimeError(f"block bytes {bytes_per_step} differ from the workload's {BYTES_PER_STEP}")
     launches_per_step = plans[0].launches
     stream = torch.cuda.Stream(device)
 
@@ -416,11 +492,7 @@ def run_ours(args, world, rank, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sample = cpu_block_sample(1.0)
-        v, threads, reps, el, algo = time_cpu_port(sample, args.cpu_seconds)
-        cpu = {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{reps} full config-1 block decode(s) ({algo} algorithmic bytes each), "
-                         f"C/OpenMP port of the reference reconstruction, bf16 out, {el:.1f} s"}
+        cpu = cpu_baselines(args.cpu_seconds)
 
     batch1 = None
     if not args.no_batch1:
@@ -436,12 +508,7 @@ def run_ours(args, world, rank, local):
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_max / args.steps, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "bytes_per_step_per_gpu": bytes_per_step,
-                   "weights_per_step_per_gpu": 100925440, "layers_rotated": N_LAYERS_ROTATED,
-                   "slots": 2, "l2": "inputs larger than L2: >250 MB touched per step, "
-                                     "8 distinct layers rotated",
-                   "timed_region": "K steps replayed from one CUDA graph on the launching stream",
-                   "parallelism": f"independent per-GPU decode x{world}"},
+        "config": gpu_config(world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": profile_traffic("rvq_layer_kernel"),

@@ -25,7 +25,7 @@ import torch
 
 from . import synthetic
 from .decoder import Qwen3Decoder
-from .layerwise import (build_layer_plan, build_meta_model, generate_greedy_ids,
+from .layerwise import (plan_from_module_tree, build_meta_model, generate_greedy_ids,
                         materialize_always_hot, upload_artifact)
 
 
@@ -109,7 +109,7 @@ def run(layers=36, prompt_len=128, new=128, vocab=151936, reps=3, modes=("dense"
     if reference:
         model = build_meta_model(cfg)
         cbs, entries = upload_artifact(art, device)
-        plan = build_layer_plan(model, entries)
+        plan = plan_from_module_tree(model, entries)
         embed, lm_head = materialize_always_hot(model, plan, cbs, device, torch.bfloat16)
         torch.cuda.synchronize()
         t = time.time()

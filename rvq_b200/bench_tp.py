@@ -75,6 +75,15 @@ def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=
         pos += 1
     e.record()
     torch.cuda.synchronize()
+    # a bounded device wait that gave up on any rank invalidates every rank's numbers
+    try:
+        dec.check_waits()
+        waits_ok = 1.0
+    except RuntimeError:
+        waits_ok = 0.0
+    if _max_over_ranks(1.0 - waits_ok, device) > 0:
+        dec.close()
+        raise RuntimeError("a bounded device wait timed out during the timed generation")
     ms_tok = _max_over_ranks(s.elapsed_time(e) / (new - 1), device)
     ttft_ms = _max_over_ranks(sorted(ttft)[1], device)
     ids = torch.cat(toks)

@@ -188,6 +188,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait: false (and the sticky flag set) if the phase never completed;
 // then one more bounded wait, so that a late copy lands before the CTA moves on.
+// After a false return the caller issues no further copies and waits for none:
+// the launch's results are undefined apart from the flag, and a copy that never
+// completed may still be in flight when the CTA exits.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     for (long long i = 0; i < kWaitLimit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
@@ -329,7 +332,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
 
     __shared__ int slot_done[kRing];                     // warps finished with a ring slot
     __shared__ float xmax[kTileCols / 32];               // per-warp max |x| of the tile
+    // set when a ring wait gave up twice: from then on the CTA issues no copies and
+    // waits for none (its partial sums are invalid; the sticky flag tells the host)
+    __shared__ volatile int aborted;
     if (tid < kRing) slot_done[tid] = 0;
+    if (tid == 0) aborted = 0;
     pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < kRing; ++s) mbar_init(bar0 + 8 * s);
@@ -354,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
         if (u != u_first) __syncthreads();              // the previous unit is done with shared memory
 
         // 1. code words of the first four batches start streaming in
-        if (tid == 0) {
+        if (tid == 0 && !aborted) {
             asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
             for (int b = 0; b < kRing && b < nb; ++b) {
                 const int rb = r0 + b * kBatchRows;
@@ -456,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
             sc_next = sc_next2;
             sc_next2 = row_scale(b + 2);
             const int slot = b % kRing;
-            mbar_wait(bar0 + 8 * slot, (phase_bits >> slot) & 1u);
+            if (!aborted && !mbar_wait(bar0 + 8 * slot, (phase_bits >> slot) & 1u)) aborted = 1;
             phase_bits ^= 1u << slot;
             const int rb0 = r0 + b * kBatchRows;
             const int nrows = min(r1, rb0 + kBatchRows) - rb0;
@@ -497,7 +504,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
                         slot_done[slot] = 0;
                         __threadfence_block();
                         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-                        load_batch(smem_u32(buf), lines, nb0, min(r1 - nb0, kBatchRows), bar0 + 8 * slot);
+                        if (!aborted)
+                            load_batch(smem_u32(buf), lines, nb0, min(r1 - nb0, kBatchRows), bar0 + 8 * slot);
                     }
                 }
             }

@@ -493,6 +493,26 @@ class Qwen3Decoder:
         self.graph.replay()
         return self._logits
 
+    def check_waits(self) -> None:
+        """Raise if a bounded device wait of this decoder's kernels gave up
+        since the last check: a tensor-parallel landing-buffer wait (the norm
+        then summed whatever the buffer held) or a fused GEMV's wait for its
+        code copies.  Either makes the logits of that step invalid.
+        Synchronises the device."""
+        torch.cuda.synchronize(self.device)
+        failed = []
+        with torch.cuda.device(self.device):
+            if self.push:
+                from .tp import take_timeout
+                if take_timeout():
+                    failed.append("a tensor-parallel landing-buffer wait")
+            if self.mode == "fused" and self.step_impl == "native":
+                from .gemv import take_wait_timeout
+                if take_wait_timeout():
+                    failed.append("a fused GEMV code-copy wait")
+        if failed:
+            raise RuntimeError(" and ".join(failed) + " timed out; the generated tokens are invalid")
+
     def close(self) -> None:
         """Release the captured graph and, collectively over the tensor-parallel
         group, the peer landing buffers.  Every rank calls it at the same point."""
@@ -524,4 +544,5 @@ class Qwen3Decoder:
             pos += 1
             tok = logits.argmax().view(1)
         ids = torch.cat(toks)
+        self.check_waits()
         return (ids, all_logits) if return_logits else ids

@@ -179,8 +179,20 @@ def _tiles_lib():
         lib.rvq_tile_codes.restype = ctypes.c_int
         lib.rvq_tile_codes.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_void_p, ctypes.c_void_p]
+        lib.rvq_take_wait_timeout.restype = ctypes.c_int
+        lib.rvq_take_wait_timeout.argtypes = []
         _tiles_bound = True
     return lib
+
+
+def take_wait_timeout() -> bool:
+    """True if an ``rvq_gemv_tiles`` wait for its bulk code copies gave up
+    since the last call (the result of that launch is then invalid).  Reads
+    and clears the library's sticky flag; synchronises the current device."""
+    v = _tiles_lib().rvq_take_wait_timeout()
+    if v < 0:
+        _native.check(-v, "rvq_take_wait_timeout")
+    return bool(v)
 
 
 def tiles_count(cols: int) -> int:

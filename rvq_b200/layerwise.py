@@ -12,16 +12,16 @@ The model math is untouched: each HF decoder layer runs through
 (lines 279-294), including the reference's choice of attention mask
 (lines 223-238).
 
-Helpers restate the reference's host set-up for synthetic artifacts:
-``build_layer_plan`` (lines 88-158), parameters-on-meta model construction
-(lines 69-73, the role accelerate's ``init_empty_weights`` plays there) and
-the artifact upload (lines 423-433).
+The set-up helpers below serve tests and benchmarks on synthetic artifacts
+(the deployment keeps its own host set-up): a parameters-on-meta model (the
+role accelerate's ``init_empty_weights`` plays in the reference), a layer
+plan from the model's module tree, the artifact upload (lines 423-433) and
+the always-resident tensors (lines 439-461).
 """
 
 from __future__ import annotations
 
 import contextlib
-import re
 from typing import Dict, List, Optional
 
 import torch
@@ -76,68 +76,41 @@ def build_meta_model(config):
     return model.eval()
 
 
-def find_base_model(model):
-    """Reference: infer_compressed_layerwise_triton.py:76-85."""
-    if hasattr(model, "get_model"):
-        try:
-            return model.get_model()
-        except Exception:
-            pass
-    for attr in ("model", "language_model", "transformer"):
-        if hasattr(model, attr):
-            return getattr(model, attr)
-    raise RuntimeError("Could not locate the base decoder model.")
+def plan_from_module_tree(model, entries: Dict[str, Dict[str, object]]):
+    """The layer plan ``_layerwise_logits`` reads, for an artifact whose keys
+    are the model's own parameter names (what this package's synthetic
+    artifacts write).  In a deployment the engine's own plan builder hands the
+    plan in; the drop-in forward only reads these keys of it: ``base_model``,
+    ``entries``, ``layer_keys`` (per decoder layer, sorted), ``embed_key``,
+    ``lm_head_key`` and ``norm_keys``.
 
+    Built by walking the decoder's module tree: every parameter of decoder
+    layer i, named by its path from the top-level model, that the artifact
+    holds.  Artifacts written under another naming prefix need the
+    deployment's plan builder, not this helper."""
+    decoder = model.get_decoder()
+    path = {id(m): name for name, m in model.named_modules()}
 
-def _prefix_for_suffix(keys, suffix: str) -> str:
-    for key in keys:
-        if key.endswith(suffix):
-            return key[: -len(suffix)]
-    return ""
+    def full(module, pname: str) -> str:
+        base = path[id(module)]
+        return f"{base}.{pname}" if base else pname
 
-
-def build_layer_plan(model, entry_map: Dict[str, Dict[str, object]]):
-    """Group artifact entries by decoder layer (reference:
-    infer_compressed_layerwise_triton.py:95-158, prefix remap included)."""
-    model_state_keys = list(model.state_dict().keys())
-    anchors = ("embed_tokens.weight", "lm_head.weight", "layers.0.input_layernorm.weight")
-    model_prefix = artifact_prefix = ""
-    for anchor in anchors:
-        model_prefix = _prefix_for_suffix(model_state_keys, anchor)
-        artifact_prefix = _prefix_for_suffix(entry_map.keys(), anchor)
-        if model_prefix or artifact_prefix:
-            break
-    if model_prefix != artifact_prefix:
-        remapped = {}
-        for key, value in entry_map.items():
-            if artifact_prefix and key.startswith(artifact_prefix):
-                remapped[model_prefix + key[len(artifact_prefix):]] = value
-            else:
-                remapped[key] = value
-        entry_map = remapped
-    key_set = set(model_state_keys)
-    usable = {k: v for k, v in entry_map.items() if k in key_set}
-    base_prefix = _prefix_for_suffix(model_state_keys, "embed_tokens.weight")
-    embed_key = f"{base_prefix}embed_tokens.weight"
-    embed_key = embed_key if embed_key in usable else None
-    lm_prefix = _prefix_for_suffix(model_state_keys, "lm_head.weight")
-    lm_head_key = f"{lm_prefix}lm_head.weight"
-    lm_head_key = lm_head_key if lm_head_key in usable else None
-    layer_re = re.compile(rf"^{re.escape(base_prefix)}layers\.(\d+)\.")
-    groups: Dict[int, List[str]] = {}
-    for key in usable:
-        m = layer_re.match(key)
-        if m:
-            groups.setdefault(int(m.group(1)), []).append(key)
-    norm_keys = [k for k in usable if k.startswith(f"{base_prefix}norm.")]
+    layer_keys = []
+    for layer in decoder.layers:
+        keys = [full(layer, pname) for pname, _ in layer.named_parameters()]
+        layer_keys.append(sorted(k for k in keys if k in entries))
+    embed_key = full(decoder.embed_tokens, "weight")
+    head = model.get_output_embeddings()
+    lm_head_key = full(head, "weight") if head is not None else None
+    norm_keys = sorted(full(decoder.norm, pname) for pname, _ in decoder.norm.named_parameters())
+    held = lambda k: k if k is not None and k in entries else None
     return {
-        "base_prefix": base_prefix,
-        "entries": usable,
-        "base_model": find_base_model(model),
-        "embed_key": embed_key,
-        "lm_head_key": lm_head_key,
-        "layer_keys": [sorted(groups[i]) for i in sorted(groups)],
-        "norm_keys": sorted(norm_keys),
+        "base_model": decoder,
+        "entries": entries,
+        "layer_keys": layer_keys,
+        "embed_key": held(embed_key),
+        "lm_head_key": held(lm_head_key),
+        "norm_keys": [k for k in norm_keys if k in entries],
     }
 
 
@@ -169,17 +142,10 @@ def materialize_always_hot(model, plan, gpu_codebooks, device, runtime_dtype):
     return embed, lm_head
 
 
-def make_dynamic_cache(base_model):
-    """Reference: infer_compressed_layerwise_triton.py:191-199."""
+def new_kv_cache(base_model):
+    """An empty HF key/value cache for the decoder layers."""
     from transformers.cache_utils import DynamicCache
-    cache = DynamicCache(config=base_model.config)
-    num_layers = len(getattr(base_model, "layers", []))
-    if not hasattr(cache, "conv_states"):
-        cache.conv_states = [None] * num_layers
-    if not hasattr(cache, "recurrent_states"):
-        cache.recurrent_states = [None] * num_layers
-    cache.has_previous_state = False
-    return cache
+    return DynamicCache(config=base_model.config)
 
 
 def slots_for(plan, gpu_codebooks, device, runtime_dtype) -> PingPongSlots:
@@ -268,7 +234,7 @@ def generate_greedy_ids(model, plan, gpu_codebooks, embed_weight, lm_head_weight
     forward = forward or _layerwise_logits
     generated = input_ids
     attention = torch.ones_like(input_ids)
-    cache = make_dynamic_cache(plan["base_model"])
+    cache = new_kv_cache(plan["base_model"])
     with torch.inference_mode():
         cache_position = torch.arange(generated.shape[1], device=device)
         logits, cache = forward(model, plan, gpu_codebooks, embed_weight, lm_head_weight, generated,

@@ -2,9 +2,9 @@
 memory (include/rvq_b200.h: ``rvq_tp_push``, ``rvq_p2p_alloc``,
 ``rvq_ipc_export`` / ``rvq_ipc_import``).
 
-Each rank owns one device block holding its arrival counter, the count of
-arrivals it has consumed, and one landing buffer [tp][hidden] fp32 per
-reduction point (``o`` after attention, ``down`` after the MLP).  After a
+Each rank owns one device block holding, per reduction point (``o`` after
+attention, ``down`` after the MLP), an arrival counter, the count of arrivals
+it has consumed, and one landing buffer [tp][hidden] fp32.  After a
 row-parallel projection the rank launches one push kernel that sums its own
 output and stores it into slot [rank] of every rank's landing buffer, then
 bumps every rank's counter.  The next RMSNorm (``NormOp`` with ``landing``)
@@ -17,8 +17,9 @@ rank B writes its slot of rank A's ``o`` buffer for layer l+1 only after B's
 norm after ``down`` of layer l has seen A's ``down`` push of layer l, and A
 launches that push after it has finished reading its ``o`` buffer for layer
 l.  The same argument holds for ``down`` with the roles of the two points
-exchanged, and one counter per rank is enough because a rank's later pushes
-always follow all its earlier ones (stream order).
+exchanged.  Each point has its own counter, so arrivals for one point can
+never satisfy a wait at the other: a peer's late ``o`` push of layer l is
+never counted toward this rank's ``down`` wait of layer l.
 
 Setup is collective: every rank of the group constructs ``PeerExchange`` at
 the same point, and ``close()`` is collective too.
@@ -36,7 +37,7 @@ from . import _native
 from .step import RvqVec
 
 RVQ_MAX_TP = 8
-_HEADER = 256                  # arrivals (u32) and consumed (u32), padded to 256 B
+_HEADER = 256                  # per point: arrivals (u32) and consumed (u32), padded to 256 B
 
 
 class RvqTpPushArgs(ctypes.Structure):
@@ -143,15 +144,20 @@ class PeerExchange:
 
     # local pointers read by the consuming norm kernel
     def landing(self, point: str) -> Dict[str, int]:
-        return {"add": self.block.ptr + self.offsets[point], "arrivals": self.block.ptr,
-                "consumed": self.block.ptr + 4, "per_use": self.arrivals_per_use, "tp": self.tp}
+        c = self.counters(point)
+        return {"add": self.block.ptr + self.offsets[point], "arrivals": self.block.ptr + c,
+                "consumed": self.block.ptr + c + 4, "per_use": self.arrivals_per_use, "tp": self.tp}
+
+    def counters(self, point: str) -> int:
+        """Byte offset of the point's (arrivals, consumed) pair in a block."""
+        return 8 * self.POINTS.index(point)
 
     def push_args(self, point: str, src: RvqVec) -> RvqTpPushArgs:
         a = RvqTpPushArgs()
         a.src = src
         for r in range(self.tp):
             a.dst[r] = self.bases[r] + self.offsets[point]
-            a.arrivals[r] = self.bases[r]
+            a.arrivals[r] = self.bases[r] + self.counters(point)
         a.n, a.rank, a.tp = self.hidden, self.rank, self.tp
         return a
 

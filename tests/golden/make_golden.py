@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Generate the golden RVQ vectors in this directory from the reference itself.
 
-Run in a container that holds the reference checkout (default path
-/root/reference, override with RVQ_REFERENCE_DIR):
+Run where a checkout of the reference is available, giving its path:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference checkout>
+    (or RVQ_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py)
 
 What it records
 * ``<case>.npz``: an entry (indices, codebook, scales, tail, metadata) and
@@ -37,7 +37,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("RVQ_REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("RVQ_REFERENCE_DIR") or (sys.argv[1] if len(sys.argv) > 1 else "")
+if not REF or not os.path.isdir(REF):
+    sys.exit(f"usage: {os.path.basename(__file__)} <reference checkout> (or set RVQ_REFERENCE_DIR)")
 sys.path.insert(0, REF)
 sys.path.insert(0, REPO)
 

@@ -7,10 +7,10 @@ then greedy-decodes a few tokens with the token loop of its
 ``generate_greedy`` (lines 323-386, on token ids instead of text).  Writes
 ``engine_tiny.npz``: prompt, generated ids and every step's logits.
 
-Run in a container that holds the reference (default /root/reference,
-override with RVQ_REFERENCE_DIR):
+Run where a checkout of the reference is available, giving its path:
 
-    python tests/golden/make_golden_engine.py
+    python tests/golden/make_golden_engine.py <reference checkout>
+    (or RVQ_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden_engine.py)
 
 The reference engine needs ``accelerate`` (absent here) and CUDA streams;
 this script provides, for the CPU run only:
@@ -35,7 +35,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("RVQ_REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("RVQ_REFERENCE_DIR") or (sys.argv[1] if len(sys.argv) > 1 else "")
+if not REF or not os.path.isdir(REF):
+    sys.exit(f"usage: {os.path.basename(__file__)} <reference checkout> (or set RVQ_REFERENCE_DIR)")
 sys.path.insert(0, REF)
 sys.path.insert(0, REPO)
 

@@ -15,7 +15,7 @@ import torch
 
 from rvq_b200 import synthetic
 from rvq_b200.decoder import Qwen3Decoder
-from rvq_b200.layerwise import (build_layer_plan, build_meta_model, generate_greedy_ids,
+from rvq_b200.layerwise import (plan_from_module_tree, build_meta_model, generate_greedy_ids,
                                 materialize_always_hot, upload_artifact)
 
 pytestmark = pytest.mark.gpu
@@ -27,7 +27,7 @@ QW = synthetic.BlockShape()          # the 2560 / 9728 / 32q / 8kv / 128 block
 def engine_run(art, cfg, prompt, new_tokens, device):
     model = build_meta_model(cfg)
     cbs, entries = upload_artifact(art, device)
-    plan = build_layer_plan(model, entries)
+    plan = plan_from_module_tree(model, entries)
     embed, lm_head = materialize_always_hot(model, plan, cbs, device, torch.bfloat16)
     ids, logits = generate_greedy_ids(model, plan, cbs, embed, lm_head, prompt.view(1, -1), new_tokens,
                                       device, torch.bfloat16)

@@ -6,7 +6,7 @@ import torch
 
 from oracle.engine_ref import OracleEngine, oracle_weight
 from rvq_b200 import synthetic
-from rvq_b200.layerwise import (_layerwise_logits, build_layer_plan, build_meta_model,
+from rvq_b200.layerwise import (_layerwise_logits, plan_from_module_tree, build_meta_model,
                                 generate_greedy_ids, materialize_always_hot, slots_for,
                                 upload_artifact)
 
@@ -21,7 +21,7 @@ def build_engine(shape, n_layers, vocab, seed, device, dtype=torch.bfloat16):
     cfg = synthetic.qwen3_config(shape, n_layers, vocab)
     model = build_meta_model(cfg)
     gpu_codebooks, gpu_entries = upload_artifact(art, device)
-    plan = build_layer_plan(model, gpu_entries)
+    plan = plan_from_module_tree(model, gpu_entries)
     embed, lm_head = materialize_always_hot(model, plan, gpu_codebooks, device, dtype)
     return art, cfg, model, plan, gpu_codebooks, embed, lm_head
 
@@ -70,7 +70,7 @@ def test_slow_consumer_sees_its_own_layer(cuda_device):
     cfg = synthetic.qwen3_config(shape, n_layers, 256)
     model = build_meta_model(cfg)
     cbs, entries = upload_artifact(art, cuda_device)
-    plan = build_layer_plan(model, entries)
+    plan = plan_from_module_tree(model, entries)
     slots = slots_for(plan, cbs, cuda_device, torch.bfloat16)
     x = torch.randn(64, shape.hidden, generator=torch.Generator().manual_seed(2)).to(cuda_device, torch.bfloat16)
     main = torch.cuda.current_stream()

@@ -98,3 +98,19 @@ def test_stage_order_is_sequential_from_positive_zero():
         for k in range(K):
             acc = acc + gathered[k]
         assert torch.equal(gathered.sum(0), acc), K
+
+
+@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("kind", KINDS)
+def test_torch_port_matches_reference(name, kind):
+    """The PyTorch restatement timed as the reference's own CPU baseline gives
+    the reference's bits on every golden case."""
+    import torch
+    from oracle.torch_port import decode_rvq_into
+    case = load_case(name)
+    dt = {OUT_F16: torch.float16, OUT_BF16: torch.bfloat16, OUT_F32: torch.float32}[kind]
+    out = torch.zeros(int(np.prod(case.meta["shape"])), dtype=dt)
+    decode_rvq_into(case.entry_torch(), case.codebook_torch(dtype=torch.float32), out)
+    bits = out.view(torch.int32 if kind == OUT_F32 else torch.int16).numpy()
+    bits = bits.view(np.uint32 if kind == OUT_F32 else np.uint16)
+    assert bits_equal(bits, case.expected[kind], kind), name
