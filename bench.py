@@ -418,25 +418,31 @@ def time_e2e(rel, cbs_host, device, steps, warmup, stream):
     return start.elapsed_time(end), h2d, d2h, launches * steps
 
 
-def batch1_leg(world, device):
+def batch1_leg(world, device, peak):
     """Batch-1 greedy generation, ms/token (the metric's second half).  N=1:
-    the 36-layer 2560/9728 model (fused RVQ GEMV and the dense bf16 model)
-    and the 64-layer 5120/25600 model; N>1: the 64-layer model tensor-parallel
-    over the N GPUs (row-parallel outputs summed by peer stores over NVLink into
-    every rank's landing buffer, rvq_b200/tp.py)."""
-    from rvq_b200 import bench_tp, synthetic
+    the 36-layer 2560/9728 model in every weight mode (dense bf16, slot
+    decode + cuBLAS, fused table GEMV, fused exact-weight GEMV), each mode's
+    ids checked against the drop-in engine (HF decoder layers on decoded
+    slots, bit-identical to the oracle engine pinned to the reference
+    engine's output), and the 64-layer 5120/25600 model; N>1: the 64-layer
+    model tensor-parallel over the N GPUs (row-parallel outputs summed by peer
+    stores over NVLink into every rank's landing buffer, rvq_b200/tp.py)."""
+    from rvq_b200 import bench_generate, bench_tp
     out = {"prompt_tokens": 128, "new_tokens": 128, "timing": "device time per token, max over ranks",
            "tp_reduce": "push (peer stores into landing buffers)" if world > 1 else None,
            "data": "synthetic random-init weights generated on the GPU, seeded"}
     try:
         group = torch.distributed.group.WORLD if world > 1 else None
         if world == 1:
-            c2 = synthetic.BlockShape()
-            out["config2_36_layers"] = {
-                "fused": bench_tp.measure(c2, 36, 151936, "fused", device),
-                "dense_bf16": bench_tp.measure(c2, 36, 151936, "dense", device)}
-        out[f"config4_64_layers_tp{world}"] = {"fused": bench_tp.measure(bench_tp.SHAPE, 64, 151936, "fused",
-                                                                        device, group)}
+            out["config2_36_layers"] = bench_generate.run(36, 128, 128, 151936, reps=2, device=device,
+                                                          hbm_gbs=peak)
+        c4 = {}
+        for mode in ("fused", "fused_exact"):
+            c4[mode] = bench_tp.measure(bench_tp.SHAPE, 64, 151936, mode, device, group)
+            c4[mode]["per_gpu_weight_GB/s"] = round(bench_tp.bytes_per_token(bench_tp.SHAPE, 64, 151936, world)
+                                                    / (c4[mode]["ms_per_token"] * 1e6), 1)
+            c4[mode]["roofline_frac"] = round(c4[mode]["per_gpu_weight_GB/s"] / peak, 4)
+        out[f"config4_64_layers_tp{world}"] = c4
     except Exception as exc:                     # reported in the line; the decode figures above stand
         out["error"] = f"{type(exc).__name__}: {exc}"[:300]
     return out
@@ -496,7 +502,7 @@ def run_ours(args, world, rank, local):
 
     batch1 = None
     if not args.no_batch1:
-        batch1 = batch1_leg(world, device)
+        batch1 = batch1_leg(world, device, peak)
 
     if world > 1:
         torch.distributed.barrier()

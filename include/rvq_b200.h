@@ -317,6 +317,17 @@ int64_t rvq_gemv_tiles_count(int64_t cols);
 /* Up to 4 jobs in one launch (e.g. q, k and v).  No workspace, no allocation. */
 int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream);
 
+/* rvq_gemv_tiles with exact bf16 weights: every weight is rebuilt
+ * bit-identically to rvq_decode's bf16 output (fp32 sum of the stage codewords
+ * in stage order, times the fp32 scale, rounded to nearest even) and
+ * multiplied by the bf16 operand in fp32, so the products are exactly those
+ * that F.linear forms on the decoded slot (infer_compressed_layerwise_triton.py:
+ * 290-292, cuBLAS on bf16 weights) and only the fp32 summation order differs.
+ * Same jobs, partials layout and consumers as rvq_gemv_tiles; operands must be
+ * bf16 vectors or fp32 partials (fp16 operands: RVQ_ERR_UNSUPPORTED).  Reference
+ * counterpart: the slot decode + F.linear pair it replaces. */
+int rvq_gemv_tiles_exact(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream);
+
 /* Repack uint8 code planes [4][stage_stride] of a rows x cols weight into the
  * tile-major layout rvq_gemv_tiles reads: [tiles][rows][32] 32-bit words, word
  * (t, r, w) = the 4 stage codes (stage k in byte k) of vector (r, 32 t + w),

@@ -40,6 +40,17 @@ def _max_over_ranks(v: float, device) -> float:
     return float(t.item())
 
 
+def bytes_per_token(shape, layers, vocab, tp):
+    """HBM bytes one rank reads per token in the fused modes: its shard of every
+    layer's codes (4 B per 8 weights) and row scales, and the replicated bf16
+    head (tied embedding)."""
+    local = synthetic.BlockShape(hidden=shape.hidden, intermediate=shape.intermediate // tp,
+                                 n_heads=shape.n_heads // tp, n_kv_heads=shape.n_kv_heads // tp,
+                                 head_dim=shape.head_dim)
+    per_layer = sum(o * i // 2 + o * 2 for _, o, i in local.projections())
+    return layers * per_layer + vocab * shape.hidden * 2
+
+
 def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=128, seed=0, tp_reduce="push"):
     """TTFT and ms/token (device time, max over the group's ranks) of greedy
     generation for the rank's shard of a random model of ``shape``."""

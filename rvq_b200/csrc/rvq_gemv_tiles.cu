@@ -514,6 +514,210 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
 }
 
 // ---------------------------------------------------------------------------
+// Exact-weight variant (rvq_gemv_tiles_exact).  Every weight is rebuilt
+// bit-identically to rvq_decode -- fp32 sum of the stage codewords in stage
+// order starting from +0, times the fp32 scale, rounded to nearest even bf16
+// -- and multiplied by the bf16 operand in fp32 (exact products, an fma chain
+// over the vector's 8 columns), so the products are those F.linear forms on
+// the decoded bf16 slot and only the fp32 summation order differs.  No tables:
+// lane g of a warp owns group g of the tile, and a warp takes 8 rows per
+// batch, reduced over the lanes with reduce8.
+//
+// The codebook sits in shared memory as fp16 with 8 copies per entry: entry
+// (k, c), copy p at byte (k / 2) << 16 | c << 8 | (k % 2) << 7 | p << 4, so
+// one prmt of the code word gives a lane's address, and the 8 lanes of every
+// quarter-warp phase (p = lane & 7) read 8 different bank quads.  A codebook
+// that fp16 cannot hold exactly is read from global memory in fp32 instead.
+// Code words are loaded straight from the tile-major lines, one batch ahead.
+// ---------------------------------------------------------------------------
+namespace exact {
+constexpr int kThreads = 1024;
+constexpr int kWarps = kThreads / 32;
+constexpr int kBatchRows = kWarps * 8;                       // 8 rows per warp and batch
+constexpr int kCopies = 8;
+constexpr int kCbBytes = kStages * kCodes * 16 * kCopies;    // 128 KB
+constexpr int kMaxStagedTiles = 64;                          // operand partial tiles staged (64 KB)
+constexpr size_t kSmemBytes = (size_t)kCbBytes + (size_t)(kMaxStagedTiles + 1) * kTileCols * 4;
+constexpr int kSwitchRows = 256;                             // starting a unit ~ 256 rows
+}  // namespace exact
+
+// fp16 codebook rows into the 8-copy layout; false if some value is not an
+// exact fp16 number (then the rows are read from global memory instead).
+__device__ __forceinline__ bool stage_cb_exact(const TJob& J, char* cbs) {
+    const int lane = threadIdx.x & 31;
+    int inexact = 0;
+    for (int e = threadIdx.x; e < kPairs; e += exact::kThreads) {
+        uint4 q;
+        if (J.cb_kind == RVQ_F16) {
+            q = __ldg(reinterpret_cast<const uint4*>(J.cb) + e);
+        } else {
+            uint32_t w[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float f0 = load_as_f32(J.cb, (int64_t)e * 8 + 2 * t, J.cb_kind);
+                const float f1 = load_as_f32(J.cb, (int64_t)e * 8 + 2 * t + 1, J.cb_kind);
+                const __half2 h = __floats2half2_rn(f0, f1);
+                inexact |= (__float_as_uint(__low2float(h)) != __float_as_uint(f0)) |
+                           (__float_as_uint(__high2float(h)) != __float_as_uint(f1)) | isnan(f0) | isnan(f1);
+                w[t] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            q = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        char* base = cbs + ((e >> 9) << 16) + ((e & 255) << 8) + (((e >> 8) & 1) << 7);
+#pragma unroll
+        for (int i = 0; i < exact::kCopies; ++i) {
+            const int cp = (i + lane) & (exact::kCopies - 1);
+            *reinterpret_cast<uint4*>(base + cp * 16) = q;
+        }
+    }
+    return !__syncthreads_or(inexact);
+}
+
+// bf16 weights of one vector: RNE(fp32(scale) * (((0 + cb0) + cb1) + cb2) + cb3)
+template <bool SMEM>
+__device__ __forceinline__ uint4 exact_weights(const char* cbs, const TJob& J, uint32_t w, const uint32_t (&lb)[4],
+                                               float s) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (SMEM) {
+#pragma unroll
+        for (int k = 0; k < kStages; ++k) {
+            const uint4 q = *reinterpret_cast<const uint4*>(cbs + __byte_perm(w, lb[k], 0x7604 | (k << 4)));
+            add_f16x2_f32(acc[0], acc[1], q.x);
+            add_f16x2_f32(acc[2], acc[3], q.y);
+            add_f16x2_f32(acc[4], acc[5], q.z);
+            add_f16x2_f32(acc[6], acc[7], q.w);
+        }
+    } else {
+        for (int k = 0; k < kStages; ++k) {
+            const int64_t row = (int64_t)(k * kCodes + ((w >> (8 * k)) & 0xffu)) * 8;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) acc[t] = __fadd_rn(acc[t], load_as_f32(J.cb, row + t, J.cb_kind));
+        }
+    }
+    uint4 r;
+    r.x = pack2(__fmul_rn(acc[0], s), __fmul_rn(acc[1], s), RVQ_BF16);
+    r.y = pack2(__fmul_rn(acc[2], s), __fmul_rn(acc[3], s), RVQ_BF16);
+    r.z = pack2(__fmul_rn(acc[4], s), __fmul_rn(acc[5], s), RVQ_BF16);
+    r.w = pack2(__fmul_rn(acc[6], s), __fmul_rn(acc[7], s), RVQ_BF16);
+    return r;
+}
+
+// sum over t of w[t] * x[t] in fp32, t = 0..7 in order (bf16 x bf16 products are exact)
+__device__ __forceinline__ float dot8_bf16(const uint4& w, const uint32_t (&xh)[4]) {
+    float acc;
+    asm("{\n .reg .b16 w0, w1, w2, w3, w4, w5, w6, w7, x0, x1, x2, x3, x4, x5, x6, x7;\n"
+        " mov.b32 {w0, w1}, %1;\n mov.b32 {w2, w3}, %2;\n mov.b32 {w4, w5}, %3;\n mov.b32 {w6, w7}, %4;\n"
+        " mov.b32 {x0, x1}, %5;\n mov.b32 {x2, x3}, %6;\n mov.b32 {x4, x5}, %7;\n mov.b32 {x6, x7}, %8;\n"
+        " fma.rn.f32.bf16 %0, w0, x0, 0f00000000;\n fma.rn.f32.bf16 %0, w1, x1, %0;\n"
+        " fma.rn.f32.bf16 %0, w2, x2, %0;\n fma.rn.f32.bf16 %0, w3, x3, %0;\n"
+        " fma.rn.f32.bf16 %0, w4, x4, %0;\n fma.rn.f32.bf16 %0, w5, x5, %0;\n"
+        " fma.rn.f32.bf16 %0, w6, x6, %0;\n fma.rn.f32.bf16 %0, w7, x7, %0;\n}\n"
+        : "=f"(acc)
+        : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(xh[0]), "r"(xh[1]), "r"(xh[2]), "r"(xh[3]));
+    return acc;
+}
+
+template <bool SMEM>
+__device__ __forceinline__ void exact_rows(const TJob& J, const char* cbs, int tile, int r0, int r1, int gt,
+                                           const uint32_t (&xh)[4], const uint32_t (&lb)[4]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t* lines = J.codes + (int64_t)tile * J.rows * kLineWords;
+    float* part = J.part + (int64_t)tile * J.rows;
+    const uint32_t g_global = (uint32_t)tile * kGroups + lane;
+    const int nb = (r1 - r0 + exact::kBatchRows - 1) / exact::kBatchRows;
+    const int orow = warp * 8 + ((lane >> 2) & 7);
+    // this warp's 8 code words of batch b (zero past the unit's rows)
+    auto fetch = [&](int b, uint32_t (&w)[8]) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int r = r0 + b * exact::kBatchRows + warp * 8 + i;
+            w[i] = (b < nb && r < r1) ? __ldg(lines + (int64_t)r * kLineWords + lane) : 0u;
+        }
+    };
+    uint32_t wn[8];
+    fetch(0, wn);
+    for (int b = 0; b < nb; ++b) {
+        uint32_t wc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wc[i] = wn[i];
+        fetch(b + 1, wn);
+        const int rb = r0 + b * exact::kBatchRows + warp * 8;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int r = rb + i;
+            float s = 0.f;
+            if (r < r1) {
+                if (J.row_scales) s = load_as_f32(J.scales, fastdiv((uint32_t)r, J.rpsdiv), J.scale_kind);
+                else if (lane < gt)
+                    s = load_as_f32(J.scales, fastdiv((uint32_t)r * (uint32_t)J.G + g_global, J.gvdiv),
+                                    J.scale_kind);
+            }
+            v[i] = dot8_bf16(exact_weights<SMEM>(cbs, J, wc[i], lb, s), xh);
+        }
+        const float tot = reduce8(v);
+        const int r = r0 + b * exact::kBatchRows + orow;
+        if ((lane & 3) == 0 && r < r1) part[r] = tot;
+    }
+}
+
+__global__ void __launch_bounds__(exact::kThreads, 1) rvq_gemv_exact_kernel(const __grid_constant__ TParams p) {
+    extern __shared__ __align__(128) float smem[];
+    char* cbs = reinterpret_cast<char*>(smem);
+    float* staged = smem + exact::kCbBytes / 4;                  // operand partials [tiles][256]
+    float* xs = staged + exact::kMaxStagedTiles * kTileCols;     // the tile's operand slice
+    const int tid = threadIdx.x, lane = tid & 31;
+    uint32_t lb[4];
+#pragma unroll
+    for (int k = 0; k < kStages; ++k)
+        lb[k] = ((uint32_t)(k & 1) << 7) | ((uint32_t)(lane & 7) << 4) | ((uint32_t)(k >> 1) << 16);
+    pdl_launch_dependents();
+    const int u_first = p.cta_first[blockIdx.x], u_last = p.cta_first[blockIdx.x + 1];
+    int cb_job = -1;
+    bool cb_smem = false;
+    for (int u = u_first; u < u_last; ++u) {
+        const uint32_t jt = p.unit_jt[u];
+        const int ji = (int)(jt >> 24);
+        const TJob& J = p.jobs[ji];
+        const int tile = (int)(jt & 0xffffffu);
+        const int r0 = p.unit_r0[u], r1 = p.unit_r1[u];
+        const int gt = min(kGroups, J.G - tile * kGroups);
+        if (u != u_first) __syncthreads();                       // the previous unit is done with shared memory
+        if (ji != cb_job) {
+            cb_job = ji;
+            cb_smem = stage_cb_exact(J, cbs);
+        }
+        if (u == u_first) pdl_wait();                            // the operand comes from the previous kernel
+        const bool has_gate = J.gate.ptr != nullptr;
+        const bool stage_x = J.x.kind == RVQ_F32 && J.x.ntiles > 1 &&
+                             J.x.ntiles + (has_gate ? J.gate.ntiles : 0) <= exact::kMaxStagedTiles;
+        const bool stage_g = has_gate && stage_x && J.gate.kind == RVQ_F32 && J.gate.ntiles > 1;
+        if (stage_x) stage_partials(J.x, tile, J.cols, staged);
+        if (stage_g) stage_partials(J.gate, tile, J.cols, staged + J.x.ntiles * kTileCols);
+        if (stage_x) __syncthreads();
+        if (tid < kTileCols) {
+            const int64_t col = (int64_t)tile * kTileCols + tid;
+            float xv = 0.f;
+            if (col < J.cols) {
+                xv = stage_x ? staged_value(staged, J.x.ntiles, tid) : operand(J.x, col);
+                if (has_gate) {
+                    const float g = stage_g ? staged_value(staged + J.x.ntiles * kTileCols, J.gate.ntiles, tid)
+                                            : operand(J.gate, col);
+                    xv = bf16r(bf16r(g / (1.0f + expf(-g))) * xv);
+                }
+            }
+            xs[tid] = xv;                                        // a bf16 value (operand kinds are bf16 or partials)
+        }
+        __syncthreads();
+        uint32_t xh[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xh[i] = pack2(xs[lane * 8 + 2 * i], xs[lane * 8 + 2 * i + 1], RVQ_BF16);
+        if (cb_smem) exact_rows<true>(J, cbs, tile, r0, r1, gt, xh, lb);
+        else exact_rows<false>(J, cbs, tile, r0, r1, gt, xh, lb);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------
 struct DevInfo {
@@ -536,10 +740,14 @@ int dev_info(DevInfo** out) {
         d.ready = true;
         cudaDeviceProp prop;
         e = cudaGetDeviceProperties(&prop, dev);
-        if (e == cudaSuccess && prop.major == 10 && prop.sharedMemPerBlockOptin >= kSmemBytes) {
+        if (e == cudaSuccess && prop.major == 10 && prop.sharedMemPerBlockOptin >= kSmemBytes &&
+            prop.sharedMemPerBlockOptin >= exact::kSmemBytes) {
             d.sms = prop.multiProcessorCount;
             e = cudaFuncSetAttribute(rvq_gemv_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kSmemBytes);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(rvq_gemv_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)exact::kSmemBytes);
             d.ok = e == cudaSuccess;
         }
         if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
@@ -584,7 +792,7 @@ int check_job(const rvq_gemv_tile_job& g) {
 //    boundary builds two tables).
 // Row ranges are cut at multiples of 8 rows.
 
-int plan(const rvq_gemv_tile_job* jobs, int n, int sms, TParams& p) {
+int plan(const rvq_gemv_tile_job* jobs, int n, int sms, TParams& p, int switch_rows = kSwitchRows) {
     int ntiles = 0;
     int64_t rows_total = 0;
     for (int j = 0; j < n; ++j) {
@@ -626,13 +834,13 @@ int plan(const rvq_gemv_tile_job* jobs, int n, int sms, TParams& p) {
         for (int j = 0; j < n; ++j) {
             const int64_t R = jobs[j].rows, c = ctas_for(bound, j);
             const int64_t longest = ((R + c - 1) / c + 7) & ~7ll;
-            cost_a = cost_a > kSwitchRows + longest ? cost_a : (double)(kSwitchRows + longest);
+            cost_a = cost_a > switch_rows + longest ? cost_a : (double)(switch_rows + longest);
         }
     }
 
     // plan B: contiguous runs of equal cost
-    const double target = (double)(rows_total + (int64_t)kSwitchRows * (ntiles + ctas)) / ctas;
-    const double cost_b = target + kSwitchRows;             // the run that ends mid-tile pays one more table
+    const double target = (double)(rows_total + (int64_t)switch_rows * (ntiles + ctas)) / ctas;
+    const double cost_b = target + switch_rows;             // the run that ends mid-tile pays one more table
 
     int u = 0, c = 0;
     p.cta_first[0] = 0;
@@ -664,7 +872,7 @@ int plan(const rvq_gemv_tile_job* jobs, int n, int sms, TParams& p) {
         for (int t = 0; t < nt; ++t) {
             int r = 0;
             while (r < R) {
-                const double room = target - cost - kSwitchRows;      // rows this run can still take
+                const double room = target - cost - switch_rows;      // rows this run can still take
                 if (cost > 0 && room < 64 && c + 1 < ctas) {           // close this run, open the next
                     p.cta_first[++c] = u;
                     cost = 0;
@@ -681,7 +889,7 @@ int plan(const rvq_gemv_tile_job* jobs, int n, int sms, TParams& p) {
                 p.unit_r0[u] = r;
                 p.unit_r1[u] = r + take;
                 ++u;
-                cost += kSwitchRows + take;
+                cost += switch_rows + take;
                 r += take;
             }
         }
@@ -745,11 +953,14 @@ int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64
     return RVQ_OK;
 }
 
-int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream) {
+static int launch_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream, bool exact_weights) {
     if (jobs == nullptr || n_jobs < 1 || n_jobs > kMaxJobs) return RVQ_ERR_INVALID;
     for (int i = 0; i < n_jobs; ++i) {
         const int rc = check_job(jobs[i]);
         if (rc != RVQ_OK) return rc;
+        // exact weights are multiplied as bf16 x bf16: the operands must be bf16 values
+        if (exact_weights && (jobs[i].x.kind == RVQ_F16 || (jobs[i].gate.ptr && jobs[i].gate.kind == RVQ_F16)))
+            return RVQ_ERR_UNSUPPORTED;
     }
     DevInfo* d = nullptr;
     int rc = dev_info(&d);
@@ -775,16 +986,28 @@ int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream) {
         J.cb_kind = g.weight.codebook_kind;
         J.scale_kind = g.weight.scale_kind;
     }
-    rc = plan(jobs, n_jobs, d->sms, p);
+    rc = plan(jobs, n_jobs, d->sms, p, exact_weights ? exact::kSwitchRows : kSwitchRows);
     if (rc != RVQ_OK) return rc;
     const int grid = p.n_ctas;
-    cudaError_t e = launch_pdl(rvq_gemv_tiles_kernel, dim3(grid), dim3(kThreads), kSmemBytes, (cudaStream_t)stream, p);
+    cudaError_t e =
+        exact_weights
+            ? launch_pdl(rvq_gemv_exact_kernel, dim3(grid), dim3(exact::kThreads), exact::kSmemBytes,
+                         (cudaStream_t)stream, p)
+            : launch_pdl(rvq_gemv_tiles_kernel, dim3(grid), dim3(kThreads), kSmemBytes, (cudaStream_t)stream, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         last_cuda_error_slot() = (int)e;
         return RVQ_ERR_CUDA;
     }
     return RVQ_OK;
+}
+
+int rvq_gemv_tiles(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream) {
+    return launch_tiles(jobs, n_jobs, stream, false);
+}
+
+int rvq_gemv_tiles_exact(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream) {
+    return launch_tiles(jobs, n_jobs, stream, true);
 }
 
 int rvq_take_wait_timeout(void) {

@@ -13,8 +13,13 @@ share every other op:
 * ``slot``:  the reference's dataflow -- each layer's RVQ weights decoded into
   one of two slots (``rvq_decode_layer``, one launch per layer) on a side
   stream one layer ahead, cuBLAS on the slot;
-* ``fused``: decode steps never materialise a weight: ``rvq_gemv`` for every
-  projection (q/k/v in one launch, gate/up in one launch).
+* ``fused``: decode steps never materialise a weight: the lookup-table
+  GEMV for every projection (q/k/v in one launch, gate/up in one launch);
+* ``fused_exact``: the same launches with exact bf16 weights
+  (``rvq_gemv_tiles_exact``): each weight is rebuilt bit-identically to the
+  slot's bf16 value and multiplied in fp32, so the products are those of the
+  reference's ``F.linear`` on the slot and only the fp32 summation order
+  differs (the strict-parity mode for greedy token identity).
 
 Prefill (the prompt, T tokens at once) is a dense contraction; the RVQ modes
 run it through the slot pipeline, ``dense`` on its resident weights.
@@ -46,7 +51,7 @@ PROJ = ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.
         "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight")
 NORMS = ("input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_norm.weight",
          "self_attn.k_norm.weight")
-MODES = ("dense", "slot", "fused")
+MODES = ("dense", "slot", "fused", "fused_exact")
 
 
 @dataclass
@@ -106,8 +111,11 @@ class Qwen3Decoder:
             raise ValueError("step_impl is 'native' (rvq_step kernels) or 'torch'")
         if runtime_dtype != torch.bfloat16 and step_impl == "native":
             raise NotImplementedError("the native decode step computes in bf16")
+        if mode == "fused_exact" and step_impl != "native":
+            raise NotImplementedError("fused_exact runs on the native decode step")
         self.step_impl = step_impl
         self.mode = mode
+        self.fused = mode in ("fused", "fused_exact")
         self.device = dev = torch.device(device)
         self.dtype = dt = runtime_dtype
         self.dims = d = Dims.from_config(config)
@@ -181,7 +189,7 @@ class Qwen3Decoder:
         self.q, self.k, self.v = z(d.n_heads * d.head_dim), z(d.n_kv * d.head_dim), z(d.n_kv * d.head_dim)
         self.attn_out, self.o = z(d.n_heads * d.head_dim), z(d.hidden)
         self.gate, self.up, self.act, self.down = z(d.intermediate), z(d.intermediate), z(d.intermediate), z(d.hidden)
-        if self.mode != "fused":
+        if not self.fused:
             return
         for L in self.layers:
             E = L["entries"]
@@ -323,7 +331,7 @@ class Qwen3Decoder:
         (the prompt; and decode steps when ``step_impl == "torch"``)."""
         d = self.dims
         h = self.embed.index_select(0, ids)
-        gemv = self.mode == "fused" and pos is not None
+        gemv = self.fused and pos is not None
         for l, w in self._layer_weights(self.mode != "dense" and not gemv):
             h = self._layer(l, h, pos, w, gemv)
         h = rmsnorm(h[-1:], self.final_norm, d.eps)
@@ -338,7 +346,8 @@ class Qwen3Decoder:
         self.x_final = torch.zeros(d.hidden, dtype=dt, device=dev)
         self.logits_buf = torch.zeros(d.vocab, dtype=dt, device=dev)
         self.step_ops = []
-        fused = self.mode == "fused"
+        fused = self.fused
+        exact = self.mode == "fused_exact"
         if fused:
             # projection outputs stay as per-tile fp32 partials; consumers add the tiles
             from .gemv import GemvTilesPlan, tiles_count
@@ -385,12 +394,12 @@ class Qwen3Decoder:
                 cb = lambda n: self._cb_tiles(E[n]["codebook_id"])
                 ops["qkv"] = GemvTilesPlan([(E[PROJ[0]], cb(PROJ[0]), self.x_attn, self.q_part),
                                             (E[PROJ[1]], cb(PROJ[1]), self.x_attn, self.k_part),
-                                            (E[PROJ[2]], cb(PROJ[2]), self.x_attn, self.v_part)])
-                ops["o"] = GemvTilesPlan([(E[PROJ[3]], cb(PROJ[3]), self.attn_out, self.o_part)])
+                                            (E[PROJ[2]], cb(PROJ[2]), self.x_attn, self.v_part)], exact=exact)
+                ops["o"] = GemvTilesPlan([(E[PROJ[3]], cb(PROJ[3]), self.attn_out, self.o_part)], exact=exact)
                 ops["gu"] = GemvTilesPlan([(E[PROJ[4]], cb(PROJ[4]), self.x_mlp, self.gate_part),
-                                           (E[PROJ[5]], cb(PROJ[5]), self.x_mlp, self.up_part)])
+                                           (E[PROJ[5]], cb(PROJ[5]), self.x_mlp, self.up_part)], exact=exact)
                 ops["down"] = GemvTilesPlan([(E[PROJ[6]], cb(PROJ[6]), self.up_part, self.down_part,
-                                              self.gate_part)])      # silu(gate) * up fused in
+                                              self.gate_part)], exact=exact)      # silu(gate) * up fused in
             else:
                 ops["silu"] = SiluMulOp(self.gate, self.up, self.act)
             self.step_ops.append(ops)
@@ -413,7 +422,7 @@ class Qwen3Decoder:
         torch.mm(x.view(1, -1), w.t(), out=y.view(1, -1))         # = F.linear(x, w)
 
     def _step_native(self) -> torch.Tensor:
-        fused = self.mode == "fused"
+        fused = self.fused
         for l, w in self._layer_weights(self.mode == "slot"):
             ops = self.step_ops[l]
             ops["norm1"].launch()
@@ -506,7 +515,7 @@ class Qwen3Decoder:
                 from .tp import take_timeout
                 if take_timeout():
                     failed.append("a tensor-parallel landing-buffer wait")
-            if self.mode == "fused" and self.step_impl == "native":
+            if self.mode == "fused" and self.step_impl == "native":      # the table GEMV's bulk copies
                 from .gemv import take_wait_timeout
                 if take_wait_timeout():
                     failed.append("a fused GEMV code-copy wait")

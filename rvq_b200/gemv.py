@@ -170,8 +170,10 @@ def _tiles_lib():
     global _tiles_bound
     lib = _native.load()
     if not _tiles_bound:
-        lib.rvq_gemv_tiles.restype = ctypes.c_int
-        lib.rvq_gemv_tiles.argtypes = [ctypes.POINTER(RvqGemvTileJob), ctypes.c_int, ctypes.c_void_p]
+        for name in ("rvq_gemv_tiles", "rvq_gemv_tiles_exact"):
+            fn = getattr(lib, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [ctypes.POINTER(RvqGemvTileJob), ctypes.c_int, ctypes.c_void_p]
         lib.rvq_gemv_tiles_count.restype = ctypes.c_int64
         lib.rvq_gemv_tiles_count.argtypes = [ctypes.c_int64]
         lib.rvq_tile_codes_bytes.restype = ctypes.c_int64
@@ -229,9 +231,16 @@ class GemvTilesPlan:
     is required.  ``x`` / ``gate`` are bf16 vectors or fp32 partials
     ``[ntiles, cols]``; ``partials`` is fp32 ``[tiles_count(cols), rows]``.
     With ``gate`` the operand is ``bf16(bf16(silu(gate)) * x)``.
+
+    ``exact``: ``rvq_gemv_tiles_exact`` -- the weights are the bit-exact bf16
+    values of the decoded slot and the products those of ``F.linear`` on it
+    (only the fp32 summation order differs); otherwise the lookup-table GEMV,
+    whose weights are never rounded to bf16.
     """
 
-    def __init__(self, products):
+    def __init__(self, products, exact: bool = False):
+        self.exact = bool(exact)
+        self._entry = "rvq_gemv_tiles_exact" if self.exact else "rvq_gemv_tiles"
         if not 1 <= len(products) <= 4:
             raise ValueError("a GEMV launch takes 1 to 4 products")
         self._keep: list = []
@@ -268,6 +277,6 @@ class GemvTilesPlan:
     def launch(self, stream: Optional[int] = None) -> None:
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
-        rc = _tiles_lib().rvq_gemv_tiles(self.jobs, self.n, ctypes.c_void_p(stream))
+        rc = getattr(_tiles_lib(), self._entry)(self.jobs, self.n, ctypes.c_void_p(stream))
         if rc:
-            _native.check(rc, "rvq_gemv_tiles")
+            _native.check(rc, self._entry)

@@ -157,3 +157,23 @@ def test_native_step_tracks_torch_step(mode, cuda_device):
     tol = 1e-2 if mode == "dense" else 2e-2
     for i, (a, b) in enumerate(zip(nat[1:], tor[1:])):
         assert rel(a, b) < tol, (i, rel(a, b))
+
+
+def test_greedy_ids_identical_to_engine_strict(cuda_device):
+    """Strict parity on the 2560/9728/32q/8kv/128 block, 8 layers, 32 greedy
+    tokens: the ids of the dense, slot and exact-weight fused decoders equal
+    the drop-in engine's exactly (the engine runs the reference's HF layers on
+    decoded bf16 slots and is bit-identical to the oracle engine pinned to the
+    reference engine's own output).  No margin allowance: every step's top-1
+    must agree."""
+    vocab, layers, new = 32768, 8, 32
+    art = synthetic.make_tp_shard_artifact(QW, layers, vocab, 0, 1, seed=40, device=cuda_device)
+    cfg = synthetic.qwen3_config(QW, layers, vocab)
+    prompt = torch.randint(0, vocab, (32,), generator=torch.Generator().manual_seed(41)).to(cuda_device)
+    ref_ids, ref_logits = engine_run(art, cfg, prompt, new, cuda_device)
+    for mode in ("dense", "slot", "fused_exact"):
+        dec = Qwen3Decoder(cfg, art, cuda_device, mode=mode, max_len=96, artifact_is_shard=True)
+        ids = dec.generate(prompt, new)
+        first = next((i for i in range(new) if int(ids[i]) != int(ref_ids[i])), None)
+        assert first is None, (mode, first, margin(ref_logits[first]))
+        dec.close()

@@ -159,3 +159,98 @@ def test_rejects_bad_jobs(cuda_device):
     with pytest.raises(ValueError):
         GemvTilesPlan([(e, cb, torch.zeros(128, dtype=torch.bfloat16, device=cuda_device),
                         torch.zeros(1, 64, device=cuda_device))])                     # wrong operand length
+
+
+# ---------------------------------------------------------------------------
+# rvq_gemv_tiles_exact: bit-exact bf16 weights, fp32 products
+# ---------------------------------------------------------------------------
+
+# fp32 summation of at most 256 exact bf16 x bf16 products per tile
+TOL_EXACT = 2e-6
+
+
+def oracle_w_bf16(entry, cb):
+    """The decoded slot's bf16 weights (the reference's reconstruction, RNE), as fp64."""
+    from oracle.rvq_oracle import OUT_BF16, bf16_bits_to_f32, decode_rvq_bits
+    numel = int(np.prod(entry["shape"]))
+    e = RVQEntryNP(indices=entry["indices"].numpy(), codebook=cb.float().numpy(),
+                   scales=entry["scales"].float().numpy(), tail=entry["tail"].float().numpy(), d=8,
+                   group_size=int(entry["group_size"]), trimmed_numel=int(entry["trimmed_numel"]),
+                   numel=numel)
+    return bf16_bits_to_f32(decode_rvq_bits(e, OUT_BF16)).reshape(entry["shape"]).astype(np.float64)
+
+
+@pytest.mark.parametrize("rows,cols,group,cb_dtype", [
+    (9728, 2560, None, torch.float32),     # gate projection, per-row scales, fp32 codebook (fp16 values)
+    (2560, 9728, None, torch.float16),     # down projection, 38 tiles, fp16 codebook
+    (1024, 2560, 128, torch.float32),      # 16 vectors per scale
+    (333, 520, None, torch.float32),       # ragged last tile (1 group), odd rows
+    (8, 8, 8, torch.float32),              # one vector per row
+    (3000, 1000, 40, torch.float32),       # 5 vectors per scale, scales change inside a tile row
+    (2048, 2560, None, "f32_not_f16"),     # fp32 codebook that fp16 cannot hold: global fp32 path
+])
+def test_exact_tiles_match_bf16_weights(rows, cols, group, cb_dtype, cuda_device):
+    g = torch.Generator().manual_seed(rows + 5 * cols)
+    cb = synthetic.make_codebook(4, 256, 8, g)
+    if cb_dtype == "f32_not_f16":
+        cb = cb.float() * (1 + 1e-6 * torch.randn(cb.shape, generator=g))
+        assert not torch.equal(cb.half().float(), cb)
+        cb_dtype = torch.float32
+    entry = synthetic.make_rvq_entry(rows, cols, g, group_size=group)
+    x = torch.randn(cols, generator=g).to(torch.bfloat16)
+    part = torch.full((tiles_count(cols), rows), float("nan"), device=cuda_device)
+    GemvTilesPlan([(dev_entry(entry, cuda_device), cb.to(cuda_device, cb_dtype), x.to(cuda_device), part)],
+                  exact=True).launch()
+    torch.cuda.synchronize()
+    assert not torch.isnan(part).any()
+    w = oracle_w_bf16(entry, cb)
+    xd = x.double().numpy()
+    assert rel_err(part.cpu().numpy(), tile_products(w, xd)) <= TOL_EXACT
+    got = part.sum(0).cpu().double().numpy()
+    assert rel_err(got, w @ xd) <= TOL_EXACT
+    # F.linear on the decoded bf16 slot (cuBLAS): the same products, another summation order
+    slot = torch.from_numpy(w).to(torch.bfloat16).to(cuda_device)
+    lin = F.linear(x.to(cuda_device).float().view(1, -1), slot.float()).view(-1).double().cpu().numpy()
+    assert rel_err(got, lin) <= 1e-5
+
+
+def test_exact_partial_operand_fused_silu_and_determinism(cuda_device):
+    g = torch.Generator().manual_seed(22)
+    rows, cols, nt = 2560, 9728, 10
+    cb = synthetic.make_codebook(4, 256, 8, g)
+    entry = dev_entry(synthetic.make_rvq_entry(rows, cols, g), cuda_device)
+    gate_p = (torch.randn(nt, cols, generator=g) / 3).to(cuda_device)
+    up_p = (torch.randn(nt, cols, generator=g) / 3).to(cuda_device)
+
+    def tile_sum(p):
+        s = p[0].clone()
+        for t in range(1, nt):
+            s += p[t]
+        return s.to(torch.bfloat16)
+
+    act = (F.silu(tile_sum(gate_p)) * tile_sum(up_p)).double().cpu().numpy()
+    part = torch.zeros(tiles_count(cols), rows, device=cuda_device)
+    plan = GemvTilesPlan([(entry, cb.to(cuda_device, torch.float32), up_p, part, gate_p)], exact=True)
+    plan.launch()
+    torch.cuda.synchronize()
+    first = part.clone()
+    host_entry = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in entry.items()}
+    w = oracle_w_bf16(host_entry, cb)
+    assert rel_err(part.sum(0).cpu().numpy(), w @ act) <= TOL_EXACT
+    for _ in range(3):
+        plan.launch()
+    torch.cuda.synchronize()
+    assert torch.equal(part, first)
+    from rvq_b200.gemv import take_wait_timeout
+    assert not take_wait_timeout()
+
+
+def test_exact_rejects_fp16_operand(cuda_device):
+    from rvq_b200 import _native
+    g = torch.Generator().manual_seed(23)
+    cb = synthetic.make_codebook(4, 256, 8, g).to(cuda_device, torch.float32)
+    e = dev_entry(synthetic.make_rvq_entry(64, 256, g), cuda_device)
+    x = torch.zeros(256, dtype=torch.float16, device=cuda_device)
+    plan = GemvTilesPlan([(e, cb, x, torch.zeros(1, 64, device=cuda_device))], exact=True)
+    with pytest.raises(_native.RvqError):
+        plan.launch()
