@@ -83,6 +83,25 @@ typedef struct rvq_copy {
     int64_t nbytes;
 } rvq_copy;
 
+/* One int8_groupwise entry (compress_full_model.py:391-425, the artifact's
+ * other method): out[i] = cast(float(q[i]) * float(scale[i / group_size])) for
+ * i < trimmed, then the tail.  Replaces _decode_int8_into
+ * (infer_compressed_layerwise_single_slot.py:110-120), which the single-slot
+ * engine calls from _decode_entry_into (lines 155-157). */
+typedef struct rvq_int8_entry {
+    const void* q;            /* device int8, trimmed values (the artifact's q [groups][group_size]) */
+    const void* scales;       /* device, trimmed / group_size values of scale_kind */
+    const void* tail;         /* device, tail_numel values of tail_kind (may be NULL if 0) */
+    void* out;                /* device, >= trimmed + tail_numel elements of out_kind */
+    int64_t trimmed;          /* trimmed_numel, a multiple of group_size */
+    int64_t group_size;
+    int64_t tail_numel;
+    int32_t scale_kind;       /* RVQ_F16, RVQ_BF16 or RVQ_F32 */
+    int32_t tail_kind;        /* RVQ_F16, RVQ_BF16 or RVQ_F32 */
+    int32_t out_kind;         /* RVQ_F16, RVQ_BF16 or RVQ_F32 */
+    int32_t reserved;
+} rvq_int8_entry;
+
 /* Maximum entries + copies one rvq_decode_layer call takes. */
 #define RVQ_MAX_LAYER_JOBS 32
 
@@ -110,6 +129,17 @@ int rvq_decode(const rvq_entry* e, void* stream);
  * (infer_compressed_layerwise_single_slot.py:652-668). */
 int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* copies,
                      int n_copies, void* stream);
+
+/* RVQ_OK when rvq_decode_int8 would accept `e`, else its status (host-only). */
+int rvq_check_int8_entry(const rvq_int8_entry* e);
+
+/* Decode one int8_groupwise entry (one launch, no allocation, no sync). */
+int rvq_decode_int8(const rvq_int8_entry* e, void* stream);
+
+/* rvq_decode_layer for a layer that also holds int8_groupwise entries:
+ * n_entries + n_int8 + n_copies <= RVQ_MAX_LAYER_JOBS, one launch. */
+int rvq_decode_layer_mixed(const rvq_entry* entries, int n_entries, const rvq_int8_entry* int8s,
+                           int n_int8, const rvq_copy* copies, int n_copies, void* stream);
 
 /* One fused dequant-GEMV y = W x for a batch of one (no counterpart in the
  * reference, which reconstructs W into the slot and then calls F.linear:

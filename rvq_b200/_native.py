@@ -33,7 +33,8 @@ KIND_OF_DTYPE = {
 }
 
 EXPORTED_SYMBOLS = (
-    "rvq_available", "rvq_check_entry", "rvq_decode", "rvq_decode_layer",
+    "rvq_available", "rvq_check_entry", "rvq_decode", "rvq_decode_layer", "rvq_decode_int8",
+    "rvq_check_int8_entry", "rvq_decode_layer_mixed",
     "rvq_take_index_error", "rvq_last_cuda_error", "rvq_status_string", "rvq_version",
 )
 
@@ -69,6 +70,22 @@ class RvqCopy(ctypes.Structure):
     ]
 
 
+class RvqInt8Entry(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("scales", ctypes.c_void_p),
+        ("tail", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("trimmed", ctypes.c_int64),
+        ("group_size", ctypes.c_int64),
+        ("tail_numel", ctypes.c_int64),
+        ("scale_kind", ctypes.c_int32),
+        ("tail_kind", ctypes.c_int32),
+        ("out_kind", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 class RvqError(RuntimeError):
     def __init__(self, status: int, where: str, message: str):
         super().__init__(f"{where}: {message} (status {status})")
@@ -101,6 +118,13 @@ def load() -> ctypes.CDLL:
     lib.rvq_decode.argtypes = [ctypes.POINTER(RvqEntry), vp]
     lib.rvq_decode_layer.restype = i32
     lib.rvq_decode_layer.argtypes = [ctypes.POINTER(RvqEntry), i32, ctypes.POINTER(RvqCopy), i32, vp]
+    lib.rvq_check_int8_entry.restype = i32
+    lib.rvq_check_int8_entry.argtypes = [ctypes.POINTER(RvqInt8Entry)]
+    lib.rvq_decode_int8.restype = i32
+    lib.rvq_decode_int8.argtypes = [ctypes.POINTER(RvqInt8Entry), vp]
+    lib.rvq_decode_layer_mixed.restype = i32
+    lib.rvq_decode_layer_mixed.argtypes = [ctypes.POINTER(RvqEntry), i32, ctypes.POINTER(RvqInt8Entry), i32,
+                                           ctypes.POINTER(RvqCopy), i32, vp]
     lib.rvq_take_index_error.restype = i32
     lib.rvq_take_index_error.argtypes = []
     lib.rvq_last_cuda_error.restype = i32
@@ -168,6 +192,25 @@ def make_entry(indices: torch.Tensor, codebook: torch.Tensor, scales: torch.Tens
     e.d = int(d)
     e.index_kind = kind_of(indices)
     e.codebook_kind = kind_of(codebook)
+    e.scale_kind = kind_of(scales)
+    e.tail_kind = kind_of(tail) if tail_n else RVQ_BF16
+    e.out_kind = kind_of(out_flat)
+    return e
+
+
+def make_int8_entry(q: torch.Tensor, scales: torch.Tensor, tail: Optional[torch.Tensor],
+                    out_flat: torch.Tensor, *, group_size: int, trimmed: int) -> RvqInt8Entry:
+    """The C struct of an int8_groupwise entry from device tensors (q int8,
+    contiguous; the library validates sizes and kinds)."""
+    e = RvqInt8Entry()
+    e.q = q.data_ptr() if q.numel() else None
+    e.scales = scales.data_ptr() if scales.numel() else None
+    tail_n = int(tail.numel()) if tail is not None else 0
+    e.tail = tail.data_ptr() if tail_n else None
+    e.out = out_flat.data_ptr()
+    e.trimmed = int(trimmed)
+    e.group_size = int(group_size)
+    e.tail_numel = tail_n
     e.scale_kind = kind_of(scales)
     e.tail_kind = kind_of(tail) if tail_n else RVQ_BF16
     e.out_kind = kind_of(out_flat)

@@ -74,6 +74,23 @@ __device__ __forceinline__ void add_f16x2_f32(float& lo_acc, float& hi_acc, uint
         : "r"(w));
 }
 
+// a *= s, b *= s as one packed fp32x2 multiply (sm_100 mul.rn.f32x2: each
+// lane an IEEE round-to-nearest fp32 product, bit-identical to two __fmul_rn).
+__device__ __forceinline__ void mul2_f32(float& a, float& b, float s) {
+    asm("{\n .reg .b64 A, B, C;\n mov.b64 A, {%0, %1};\n mov.b64 B, {%2, %2};\n mul.rn.f32x2 C, A, B;\n"
+        " mov.b64 {%0, %1}, C;\n}\n"
+        : "+f"(a), "+f"(b)
+        : "f"(s));
+}
+
+// 32 bytes (two 16-byte vectors) with one 256-bit store that does not allocate
+// in L1 (write-once data).  dst must be 32-byte aligned.
+__device__ __forceinline__ void store_v8_na(void* dst, const uint4& a, const uint4& b) {
+    asm volatile("st.global.L1::no_allocate.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(dst), "r"(a.x),
+                 "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, int out_kind) {
     if (out_kind == RVQ_BF16) {
         __nv_bfloat162 v = __floats2bfloat162_rn(a, b);

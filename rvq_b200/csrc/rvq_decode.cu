@@ -15,17 +15,23 @@
 //   CTA streams one or two contiguous regions and loads at most a couple of
 //   codebooks.
 // * 1 CTA of 1024 threads per SM.  The CTA stages the job's codebook in
-//   shared memory as fp16 with 8 copies interleaved per entry: lane L reads
-//   copy (L & 7), so the 8 lanes of each quarter-warp phase of a 16-byte
-//   shared load always hit 8 different bank quads -- random codes never
-//   conflict.  K=4 x 256 codes x 16 B x 8 copies = 128 KB.
+//   shared memory as fp16 with 8 copies per entry: lane L reads copy (L & 7),
+//   so the 8 lanes of each quarter-warp phase of a 16-byte shared load always
+//   hit 8 different bank quads -- random codes never conflict.  K=4 x 256
+//   codes x 16 B x 8 copies = 128 KB.  Fast-path jobs place entry (k, c),
+//   copy p at byte (k / 2) << 16 | c << 8 | (k % 2) << 7 | p << 4; other jobs
+//   at ((k * ncodes + c) << copies_log2 | p) * 16.
 // * A codebook handed over as fp32 (what the engine uploads) is converted to
 //   fp16 while it is staged; the CTA checks that every value survives the
 //   round trip exactly and otherwise keeps fp32 entries instead, so the
 //   result never depends on that choice.
-// * Lane L of a warp owns vectors v0 + 32j + L (j = 0..3) of its tile: index
-//   loads are 32 consecutive bytes per plane, and each 128-bit store of the
-//   warp covers 512 contiguous output bytes.
+// * Fast path (K=4, 256 codes, u8 codes, 16-bit output): lane L of a warp owns
+//   vectors 4L .. 4L + 3 of its 128-vector tile, so its 32-bit index word of a
+//   plane holds exactly its 4 codes (one coalesced 128-byte load per plane and
+//   warp); a code byte becomes the staged entry's shared-memory byte offset
+//   with one prmt, and the lane writes its vectors in pairs with 256-bit
+//   stores (32 contiguous bytes per lane, no L1 allocation for the
+//   write-once slot).
 // * fp32 accumulation uses add.rn.f32.f16 (fp16 -> fp32 conversion fused into
 //   the add; exact conversion, one rounding, same result as cvt + add.rn).
 
@@ -43,21 +49,22 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kTileVecs = 128;                 // vectors per warp tile
 constexpr int kJ = kTileVecs / 32;             // vectors per lane per tile
 constexpr int kCopyTileBytes = 2048;           // bytes per warp tile of a raw copy
+constexpr int kInt8TileElems = 512;            // int8 elements per warp tile (16 per lane)
 constexpr int kSmemBudget = 200 * 1024;        // codebook staging limit per CTA
 constexpr int kMaxDevices = 64;
 
-enum JobKind : uint8_t { JOB_RVQ = 0, JOB_COPY = 1 };
+enum JobKind : uint8_t { JOB_RVQ = 0, JOB_COPY = 1, JOB_INT8 = 2 };
 enum GatherMode : uint8_t { GATHER_SMEM_F16 = 0, GATHER_SMEM_F32 = 1, GATHER_GLOBAL = 2 };
 
 struct Job {
-    const void* idx;
+    const void* idx;        // RVQ: code planes; COPY: source; INT8: q
     const void* cb;
     const void* scales;
     const void* tail;
     void* out;
-    uint32_t nvec;          // RVQ: vectors; COPY: bytes
+    uint32_t nvec;          // RVQ: vectors; COPY: bytes; INT8: trimmed elements
     uint32_t stage_stride;  // elements
-    FastDiv gv;
+    FastDiv gv;             // RVQ: vectors per scale; INT8: elements per scale
     uint32_t full_vecs;     // vectors with all 8 elements < trimmed
     uint32_t tail_numel;
     uint64_t trimmed;
@@ -133,6 +140,13 @@ __device__ __forceinline__ void store_vec(const Job& job, uint32_t n, const floa
         if (base + t < job.trimmed) store_from_f32(job.out, (int64_t)(base + t), job.out_kind, v[t]);
 }
 
+// 16-byte slot of entry (k, c), copy p, in the fp16 staging (layouts above).
+__device__ __forceinline__ uint32_t staged_slot(const Job& job, uint32_t k, uint32_t c, uint32_t p) {
+    if (job.fast_ok) return ((k >> 1) << 12) | (c << 4) | ((k & 1) << 3) | p;
+    const uint32_t nc = job.ncodes ? job.ncodes : 65536u;
+    return ((k * nc + c) << job.copies_log2) + p;
+}
+
 // Stage job.cb into shared memory.  Returns the gather mode every thread of
 // the CTA agrees on.  Must be called by all threads of the CTA.
 __device__ int stage_codebook(const Job& job, uint4* smem) {
@@ -162,9 +176,11 @@ __device__ int stage_codebook(const Job& job, uint4* smem) {
             }
             // rotate the copy index with the lane so the 8 lanes of a phase
             // write 8 different bank quads
+            const uint32_t nc = job.ncodes ? job.ncodes : 65536u;
+            const uint32_t k = (uint32_t)e / nc, c = (uint32_t)e - k * nc;
             for (int i = 0; i < copies; ++i) {
                 int cp = (i + lane) & (copies - 1);
-                smem[(size_t)e * copies + cp] = q;
+                smem[staged_slot(job, k, c, (uint32_t)cp)] = q;
             }
         }
         inexact = __syncthreads_or(inexact);
@@ -181,65 +197,74 @@ __device__ int stage_codebook(const Job& job, uint4* smem) {
     return GATHER_GLOBAL;
 }
 
-// Fast path: u8 indices over 256 codes, fp16 staging with 8 copies, KT = 4
+// Fast path: u8 indices over 256 codes, fp16 staging with 8 copies, K = 4
 // stages (the compressor's default), 16-bit output (bf16 or fp16 fixed at
-// compile time, so each pack is one conversion), every vector of every tile
-// complete.  The staged fp16 pairs are added into the fp32 accumulators with
-// add.rn.f32.f16 on their register halves (no unpacking instructions).  Each warp
-// walks tiles ta+warp, ta+warp+32, ... and prefetches the next tile's index
-// words and scales while it decodes the current one.  Codes travel by
-// shuffle: lane L loads index word L of a plane (codes of vectors 4L..4L+3)
-// and lane l takes byte (l & 3) of lane 8j + l/4's word for vector 32j + l.
-template <int KT, bool OUT_BF16>
+// compile time, so each pack is one conversion), a 32-byte aligned output,
+// every vector of every tile complete.  Lane L owns vectors 4L .. 4L + 3 of
+// the warp's tile: its index word of plane k holds their stage-k codes in
+// bytes 0..3, and one prmt of that word with the lane's constant bits gives
+// the byte offset of the staged entry (k / 2 << 16 | code << 8 | k % 2 << 7 |
+// (L & 7) << 4).  The staged fp16 pairs are added into the fp32 accumulators
+// with add.rn.f32.f16 on their register halves, the scale is applied with
+// packed fp32x2 multiplies (same IEEE products), and vector pairs leave as
+// 256-bit stores.  Each warp walks tiles ta + warp, ta + warp + 32, ... and
+// loads the next tile's index words while it decodes the current one.
+// SCALE4: group_vecs is a multiple of 4, so a lane's 4 vectors share a scale.
+template <bool OUT_BF16, bool SCALE4>
 __device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane,
-                                         const uint4* smem) {
+                                         const char* smem) {
     // the few job fields the loop needs, read once from parameter space
     const uint32_t* idx32 = reinterpret_cast<const uint32_t*>(job.idx);
     const uint32_t plane32 = job.stage_stride >> 2;
     uint4* out = reinterpret_cast<uint4*>(job.out);
     const unsigned short* scales = reinterpret_cast<const unsigned short*>(job.scales);
     const FastDiv gv = job.gv;
-    const uint32_t cpy = lane & 7;
-    const uint32_t bsel = 0x4440u | (lane & 3);
+    uint32_t lb[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        lb[k] = ((uint32_t)(k & 1) << 7) | ((uint32_t)(lane & 7) << 4) | ((uint32_t)(k >> 1) << 16);
     uint32_t t = ta + warp;
-    uint32_t w[KT];
+    uint32_t w[4];
     if (t < tb) {
 #pragma unroll
-        for (int k = 0; k < KT; ++k) w[k] = __ldg(idx32 + (size_t)k * plane32 + ((t * kTileVecs) >> 2) + lane);
+        for (int k = 0; k < 4; ++k) w[k] = __ldg(idx32 + (size_t)k * plane32 + t * 32u + lane);
     }
     for (; t < tb; t += kWarps) {
-        // next tile's index words are requested before this tile is decoded;
-        // scales are a few hundred bytes per CTA and stay in L1
-        uint32_t wn[KT];
+        uint32_t wn[4];
         if (t + kWarps < tb) {
 #pragma unroll
-            for (int k = 0; k < KT; ++k)
-                wn[k] = __ldg(idx32 + (size_t)k * plane32 + (((t + kWarps) * kTileVecs) >> 2) + lane);
+            for (int k = 0; k < 4; ++k) wn[k] = __ldg(idx32 + (size_t)k * plane32 + (t + kWarps) * 32u + lane);
         }
-        const uint32_t v0 = t * kTileVecs;
+        const uint32_t n0 = t * kTileVecs + 4u * lane;
+        float s4 = 0.f;
+        if (SCALE4) s4 = __half2float(__ushort_as_half(__ldg(scales + fastdiv(n0, gv))));
+        uint4 prev;
 #pragma unroll
-        for (int j = 0; j < kJ; ++j) {
-            const uint32_t n = v0 + 32 * j + lane;
-            const float s = __half2float(__ushort_as_half(__ldg(scales + fastdiv(n, gv))));
+        for (int i = 0; i < 4; ++i) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int k = 0; k < KT; ++k) {
-                const uint32_t c = __byte_perm(__shfl_sync(0xffffffffu, w[k], 8 * j + (lane >> 2)), 0, bsel);
-                const uint4 q = smem[((k * 256u + c) << 3) + cpy];
+            for (int k = 0; k < 4; ++k) {
+                const uint4 q = *reinterpret_cast<const uint4*>(smem + __byte_perm(w[k], lb[k], 0x7604 | (i << 4)));
                 add_f16x2_f32(acc[0], acc[1], q.x);
                 add_f16x2_f32(acc[2], acc[3], q.y);
                 add_f16x2_f32(acc[4], acc[5], q.z);
                 add_f16x2_f32(acc[6], acc[7], q.w);
             }
+            const float s = SCALE4 ? s4 : __half2float(__ushort_as_half(__ldg(scales + fastdiv(n0 + i, gv))));
+            mul2_f32(acc[0], acc[1], s);
+            mul2_f32(acc[2], acc[3], s);
+            mul2_f32(acc[4], acc[5], s);
+            mul2_f32(acc[6], acc[7], s);
             uint4 q;
-            q.x = pack2(__fmul_rn(acc[0], s), __fmul_rn(acc[1], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
-            q.y = pack2(__fmul_rn(acc[2], s), __fmul_rn(acc[3], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
-            q.z = pack2(__fmul_rn(acc[4], s), __fmul_rn(acc[5], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
-            q.w = pack2(__fmul_rn(acc[6], s), __fmul_rn(acc[7], s), OUT_BF16 ? RVQ_BF16 : RVQ_F16);
-            out[n] = q;
+            q.x = pack2(acc[0], acc[1], OUT_BF16 ? RVQ_BF16 : RVQ_F16);
+            q.y = pack2(acc[2], acc[3], OUT_BF16 ? RVQ_BF16 : RVQ_F16);
+            q.z = pack2(acc[4], acc[5], OUT_BF16 ? RVQ_BF16 : RVQ_F16);
+            q.w = pack2(acc[6], acc[7], OUT_BF16 ? RVQ_BF16 : RVQ_F16);
+            if (i & 1) store_v8_na(out + n0 + i - 1, prev, q);
+            else prev = q;
         }
 #pragma unroll
-        for (int k = 0; k < KT; ++k) w[k] = wn[k];
+        for (int k = 0; k < 4; ++k) w[k] = wn[k];
     }
 }
 
@@ -260,7 +285,7 @@ __device__ void tile_generic(const Job& job, uint32_t tile, int lane, const uint
             uint32_t e = k * ncodes + c;
             float v[8];
             if (mode == GATHER_SMEM_F16) {
-                uint4 q = smem[(e << job.copies_log2) + cpy];
+                uint4 q = smem[staged_slot(job, (uint32_t)k, c, cpy)];
                 uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -320,6 +345,45 @@ __device__ void copy_tail(const Job& job) {
     }
 }
 
+// One warp tile (512 elements) of an int8_groupwise job: lane L owns elements
+// 16 L .. 16 L + 15; out = cast(float(q) * float(scale)), the product one fp32
+// multiply and the cast round-to-nearest-even (_decode_int8_into,
+// infer_compressed_layerwise_single_slot.py:110-120).  fast_ok: q and out
+// 16-byte aligned, 16-bit output and 16 | group_size (one scale per lane).
+__device__ void int8_tile(const Job& job, uint32_t tile, int lane) {
+    const uint32_t e0 = tile * kInt8TileElems + 16u * (uint32_t)lane;
+    const int8_t* q = reinterpret_cast<const int8_t*>(job.idx);
+    if (job.fast_ok && e0 + 16u <= job.nvec) {
+        const int4 raw = __ldg(reinterpret_cast<const int4*>(q + e0));
+        const float s = load_as_f32(job.scales, fastdiv(e0, job.gv), job.scale_kind);
+        const uint32_t w[4] = {(uint32_t)raw.x, (uint32_t)raw.y, (uint32_t)raw.z, (uint32_t)raw.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float a = (float)(int8_t)(w[i >> 1] >> (16 * (i & 1)));
+            const float b = (float)(int8_t)(w[i >> 1] >> (16 * (i & 1) + 8));
+            o[i] = pack2(__fmul_rn(a, s), __fmul_rn(b, s), job.out_kind);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(job.out) + e0);
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        return;
+    }
+    for (uint32_t i = 0; i < 16u; ++i) {
+        const uint32_t e = e0 + i;
+        if (e >= job.nvec) break;
+        const float s = load_as_f32(job.scales, fastdiv(e, job.gv), job.scale_kind);
+        store_from_f32(job.out, (int64_t)e, job.out_kind, __fmul_rn((float)q[e], s));
+    }
+}
+
+// Tiles [a, e) (job-local) of one int8 job; `owner` copies the tail.
+__device__ __forceinline__ void process_int8(const Job& job, uint32_t a, uint32_t e, bool owner, int warp,
+                                             int lane) {
+    if (owner) copy_tail(job);
+    for (uint32_t t = a + warp; t < e; t += kWarps) int8_tile(job, t, lane);
+}
+
 // Decode tiles [a, e) (job-local) of one RVQ job; `owner` copies the tail.
 // All threads of the CTA call it.
 __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t e, bool owner, int warp,
@@ -336,8 +400,15 @@ __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t
     if (mode == GATHER_SMEM_F16 && job.fast_ok) {
         const uint32_t fe = min(e, job.full_tiles);
         if (a < fe) {
-            if (job.out_kind == RVQ_BF16) run_fast<4, true>(job, a, fe, warp, lane, smem);
-            else run_fast<4, false>(job, a, fe, warp, lane, smem);
+            const char* cs = reinterpret_cast<const char*>(smem);
+            const bool s4 = (job.gv.d & 3u) == 0;
+            if (job.out_kind == RVQ_BF16) {
+                if (s4) run_fast<true, true>(job, a, fe, warp, lane, cs);
+                else run_fast<true, false>(job, a, fe, warp, lane, cs);
+            } else {
+                if (s4) run_fast<false, true>(job, a, fe, warp, lane, cs);
+                else run_fast<false, false>(job, a, fe, warp, lane, cs);
+            }
             g = fe;
         }
     }
@@ -358,10 +429,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
         }
         for (int j = 0; j < p.njobs; ++j) {
             const Job& job = p.jobs[j];
-            if (job.kind != JOB_RVQ || b < job.cta_begin || b >= job.cta_begin + job.cta_count) continue;
+            if (job.kind == JOB_COPY || b < job.cta_begin || b >= job.cta_begin + job.cta_count) continue;
             const uint32_t r = b - job.cta_begin, cc = job.cta_count, tc = job.tile_count;
             const uint32_t a = (uint32_t)(((uint64_t)tc * r) / cc), e = (uint32_t)(((uint64_t)tc * (r + 1)) / cc);
-            process_rvq(job, a, e, r == 0, warp, lane, smem, staged_once);
+            if (job.kind == JOB_INT8) process_int8(job, a, e, r == 0, warp, lane);
+            else process_rvq(job, a, e, r == 0, warp, lane, smem, staged_once);
         }
         return;
     }
@@ -375,6 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
         const Job& job = p.jobs[j];
         if (job.kind == JOB_COPY) {
             for (uint32_t t = a + warp; t < e; t += kWarps) copy_tile(job, t - jb, lane);
+            continue;
+        }
+        if (job.kind == JOB_INT8) {
+            process_int8(job, a - jb, e - jb, a == jb, warp, lane);
             continue;
         }
         process_rvq(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
@@ -456,6 +532,42 @@ static int check_entry(const rvq_entry* e) {
     return RVQ_OK;
 }
 
+static int check_int8_entry(const rvq_int8_entry* e) {
+    if (!e) return RVQ_ERR_INVALID;
+    if (!is_float_kind(e->out_kind) || !is_float_kind(e->scale_kind) || !is_float_kind(e->tail_kind))
+        return RVQ_ERR_UNSUPPORTED;
+    if (e->trimmed < 0 || e->tail_numel < 0 || e->group_size < 1) return RVQ_ERR_INVALID;
+    if (e->trimmed % e->group_size != 0) return RVQ_ERR_INVALID;
+    if (e->trimmed >= (1ll << 31) || e->tail_numel >= (1ll << 31) || e->group_size >= (1ll << 31))
+        return RVQ_ERR_TOO_LARGE;
+    if (!e->out) return RVQ_ERR_INVALID;
+    if (e->trimmed > 0 && (!e->q || !e->scales)) return RVQ_ERR_INVALID;
+    if (e->tail_numel > 0 && !e->tail) return RVQ_ERR_INVALID;
+    return RVQ_OK;
+}
+
+static void fill_int8_job(const rvq_int8_entry* e, Job& j) {
+    memset(&j, 0, sizeof(j));
+    j.kind = JOB_INT8;
+    j.idx = e->q;
+    j.scales = e->scales;
+    j.tail = e->tail;
+    j.out = e->out;
+    j.nvec = (uint32_t)e->trimmed;
+    j.gv = make_fastdiv((uint32_t)e->group_size);
+    j.trimmed = (uint64_t)e->trimmed;
+    j.tail_numel = (uint32_t)e->tail_numel;
+    j.scale_kind = (uint8_t)e->scale_kind;
+    j.tail_kind = (uint8_t)e->tail_kind;
+    j.out_kind = (uint8_t)e->out_kind;
+    j.out_aligned = ((uintptr_t)e->out & 15) == 0;
+    j.fast_ok = j.out_aligned && ((uintptr_t)e->q & 15) == 0 && e->group_size % 16 == 0 &&
+                (e->out_kind == RVQ_BF16 || e->out_kind == RVQ_F16);
+    uint32_t tiles = (uint32_t)((e->trimmed + kInt8TileElems - 1) / kInt8TileElems);
+    if (tiles == 0 && e->tail_numel > 0) tiles = 1;
+    j.tile_count = tiles;
+}
+
 static size_t stage_bytes_f16(int copies_log2, int64_t entries) { return (size_t)entries * 16u << copies_log2; }
 
 static int fill_rvq_job(const rvq_entry* e, Job& j, size_t& smem_need) {
@@ -497,7 +609,7 @@ static int fill_rvq_job(const rvq_entry* e, Job& j, size_t& smem_need) {
     const uint64_t complete = (uint64_t)(e->nvec < (int64_t)j.full_vecs ? e->nvec : j.full_vecs);
     j.full_tiles = (uint32_t)(complete / kTileVecs);
     j.fast_ok = e->index_kind == RVQ_U8 && e->ncodes == 256 && e->stages == 4 && cl == 3 &&
-                (e->out_kind == RVQ_BF16 || e->out_kind == RVQ_F16) && j.out_aligned &&
+                (e->out_kind == RVQ_BF16 || e->out_kind == RVQ_F16) && ((uintptr_t)e->out & 31) == 0 &&
                 e->scale_kind == RVQ_F16 &&
                 ((uintptr_t)e->indices & 3) == 0 && (e->stage_stride & 3) == 0;
     return RVQ_OK;
@@ -511,14 +623,14 @@ static uint32_t plan_per_cta(LayerParams& p, uint32_t sms) {
     uint32_t n_rvq = 0;
     uint64_t total = 0;
     for (int i = 0; i < p.njobs; ++i)
-        if (p.jobs[i].kind == JOB_RVQ && p.jobs[i].tile_count) { ++n_rvq; total += p.jobs[i].tile_count; }
+        if (p.jobs[i].kind != JOB_COPY && p.jobs[i].tile_count) { ++n_rvq; total += p.jobs[i].tile_count; }
     if (n_rvq == 0 || 2 * n_rvq > sms) return 0;
     double ideal[RVQ_MAX_LAYER_JOBS] = {0};
     uint32_t cnt[RVQ_MAX_LAYER_JOBS] = {0};
     uint32_t sum = 0;
     for (int i = 0; i < p.njobs; ++i) {
         const Job& j = p.jobs[i];
-        if (j.kind != JOB_RVQ || !j.tile_count) continue;
+        if (j.kind == JOB_COPY || !j.tile_count) continue;
         ideal[i] = (double)sms * j.tile_count / (double)total;
         uint32_t c = (uint32_t)ideal[i];
         if (c < 1) c = 1;
@@ -539,7 +651,7 @@ static uint32_t plan_per_cta(LayerParams& p, uint32_t sms) {
         int best = -1;
         double bd = -1e30;
         for (int i = 0; i < p.njobs; ++i)
-            if (p.jobs[i].kind == JOB_RVQ && cnt[i] && cnt[i] < p.jobs[i].tile_count && ideal[i] - cnt[i] > bd) {
+            if (p.jobs[i].kind != JOB_COPY && cnt[i] && cnt[i] < p.jobs[i].tile_count && ideal[i] - cnt[i] > bd) {
                 bd = ideal[i] - cnt[i];
                 best = i;
             }
@@ -550,7 +662,7 @@ static uint32_t plan_per_cta(LayerParams& p, uint32_t sms) {
     uint32_t begin = 0, copy_owner = 0;
     for (int i = 0; i < p.njobs; ++i) {
         Job& j = p.jobs[i];
-        if (j.kind == JOB_RVQ) {
+        if (j.kind != JOB_COPY) {
             j.cta_begin = begin;
             j.cta_count = cnt[i];
             begin += cnt[i];
@@ -604,8 +716,20 @@ int rvq_decode(const rvq_entry* e, void* stream) {
 
 int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* copies, int n_copies,
                      void* stream) {
-    if (n_entries < 0 || n_copies < 0 || n_entries + n_copies > RVQ_MAX_LAYER_JOBS) return RVQ_ERR_INVALID;
-    if ((n_entries && !entries) || (n_copies && !copies)) return RVQ_ERR_INVALID;
+    return rvq_decode_layer_mixed(entries, n_entries, nullptr, 0, copies, n_copies, stream);
+}
+
+int rvq_check_int8_entry(const rvq_int8_entry* e) { return check_int8_entry(e); }
+
+int rvq_decode_int8(const rvq_int8_entry* e, void* stream) {
+    return rvq_decode_layer_mixed(nullptr, 0, e, 1, nullptr, 0, stream);
+}
+
+int rvq_decode_layer_mixed(const rvq_entry* entries, int n_entries, const rvq_int8_entry* int8s, int n_int8,
+                           const rvq_copy* copies, int n_copies, void* stream) {
+    if (n_entries < 0 || n_int8 < 0 || n_copies < 0 || n_entries + n_int8 + n_copies > RVQ_MAX_LAYER_JOBS)
+        return RVQ_ERR_INVALID;
+    if ((n_entries && !entries) || (n_int8 && !int8s) || (n_copies && !copies)) return RVQ_ERR_INVALID;
     LayerParams p;
     memset(&p, 0, sizeof(p));
     size_t smem = 0;
@@ -615,6 +739,11 @@ int rvq_decode_layer(const rvq_entry* entries, int n_entries, const rvq_copy* co
         rc = fill_rvq_job(&entries[i], p.jobs[p.njobs], smem);
         if (rc != RVQ_OK) return rc;
         p.njobs++;
+    }
+    for (int i = 0; i < n_int8; ++i) {
+        const int rc = check_int8_entry(&int8s[i]);
+        if (rc != RVQ_OK) return rc;
+        fill_int8_job(&int8s[i], p.jobs[p.njobs++]);
     }
     for (int i = 0; i < n_copies; ++i) {
         const rvq_copy& c = copies[i];

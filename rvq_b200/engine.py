@@ -5,6 +5,9 @@ Mirrors the reference's engine-level entry points so they stay drop-ins:
 * ``decode_into(entry, codebooks, out)``  -- infer_compressed_layerwise_triton.py:161-176
 * ``decode_to_tensor(entry, codebooks, device, runtime_dtype)`` -- same file, 179-188
 
+(``int8_groupwise`` entries, which the reference's Triton engine rejects,
+decode here as in the single-slot engine),
+
 and adds ``LayerDecodePlan``: all entries of one decoder layer (7 RVQ
 projections + 4 bf16 norm copies for Qwen3) decoded by ONE kernel launch,
 with the C descriptors built once and reused every time the layer is
@@ -25,12 +28,51 @@ from .triton_decode_kernels import decode_rvq_triton_into, prepare_entry, rvq_tr
 RVQ_METHODS = ("rvq_groupwise", "rvq_mlp")
 
 
+def prepare_int8_entry(entry: Dict[str, object], out: torch.Tensor):
+    """Validate an int8_groupwise entry (compress_full_model.py:414-425) for
+    ``out`` and return (C struct, tensors to keep alive)."""
+    if not out.is_cuda or not out.is_contiguous():
+        raise ValueError("Output tensor must be a contiguous CUDA tensor.")
+    q, scales, tail = entry["q"], entry["scales"], entry["tail"]
+    for name, t in (("q", q), ("scales", scales), ("tail", tail)):
+        if t.numel() and not t.is_cuda:
+            raise ValueError(f"Entry tensor {name} must be on CUDA.")
+    if q.dtype != torch.int8:
+        raise NotImplementedError(f"int8_groupwise codes must be int8, got {q.dtype}")
+    trimmed, group_size = int(entry["trimmed_numel"]), int(entry["group_size"])
+    if q.numel() != trimmed or out.numel() < trimmed + tail.numel():
+        raise ValueError("int8 entry does not match the output tensor")
+    q = q.contiguous()
+    if scales.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        scales = scales.to(torch.float32)
+    scales = scales.contiguous()
+    tail = tail.contiguous()
+    st = _native.make_int8_entry(q, scales, tail, out.view(-1), group_size=group_size, trimmed=trimmed)
+    return st, (q, scales, tail)
+
+
+def decode_int8_into(entry: Dict[str, object], out: torch.Tensor) -> torch.Tensor:
+    """One int8_groupwise entry into ``out`` on the current stream: the
+    single-slot engine's ``_decode_int8_into``
+    (infer_compressed_layerwise_single_slot.py:110-120) on the GPU."""
+    st, keep = prepare_int8_entry(entry, out)
+    with torch.cuda.device(out.device):
+        _native.check(_native.load().rvq_decode_int8(ctypes.byref(st), ctypes.c_void_p(
+            torch.cuda.current_stream(out.device).cuda_stream)), "rvq_decode_int8")
+    del keep
+    return out
+
+
 def decode_into(entry: Dict[str, object], codebooks: Dict[str, torch.Tensor], out: torch.Tensor):
-    """Reference: infer_compressed_layerwise_triton.py:161-176."""
+    """Reference: infer_compressed_layerwise_triton.py:161-176.  The reference
+    engine raises for ``int8_groupwise`` entries; this one decodes them as the
+    single-slot engine does (infer_compressed_layerwise_single_slot.py:155-157)."""
     method = entry["method"]
     if method == "bf16_raw":
         flat_data = entry["data"].view(torch.int16)
         out.view(torch.int16).copy_(flat_data, non_blocking=True)
+    elif method == "int8_groupwise":
+        decode_int8_into(entry, out)
     elif method in RVQ_METHODS:
         codebook = codebooks[entry["codebook_id"]]
         if not rvq_triton_supported(entry, out):
@@ -62,6 +104,7 @@ class LayerDecodePlan:
                  codebooks: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor]):
         self.keys: List[str] = []
         entries: List[_native.RvqEntry] = []
+        int8s: List[_native.RvqInt8Entry] = []
         copies: List[Tuple[int, int, int]] = []
         self._keep: list = []
         self.algorithmic_bytes = 0
@@ -81,6 +124,13 @@ class LayerDecodePlan:
                 nbytes = data.numel() * 2
                 copies.append((data.data_ptr(), out.data_ptr(), nbytes))
                 self.algorithmic_bytes += 2 * nbytes
+            elif method == "int8_groupwise":
+                st, keep = prepare_int8_entry(entry, out)
+                self._keep.append(keep)
+                int8s.append(st)
+                self.algorithmic_bytes += (out.numel() * out.element_size() + entry["q"].numel()
+                                           + entry["scales"].numel() * entry["scales"].element_size()
+                                           + entry["tail"].numel() * entry["tail"].element_size())
             elif method in RVQ_METHODS:
                 cb = codebooks[entry["codebook_id"]]
                 if not rvq_triton_supported(entry, out):
@@ -97,14 +147,16 @@ class LayerDecodePlan:
                 raise ValueError(f"Unsupported decode method: {method}")
             self.keys.append(key)
         self.batches = []
-        jobs = [("e", e) for e in entries] + [("c", c) for c in copies]
+        jobs = [("e", e) for e in entries] + [("i", e) for e in int8s] + [("c", c) for c in copies]
         for i in range(0, len(jobs), _native.RVQ_MAX_LAYER_JOBS):
             chunk = jobs[i:i + _native.RVQ_MAX_LAYER_JOBS]
             es = [j for t, j in chunk if t == "e"]
+            qs = [j for t, j in chunk if t == "i"]
             cs = [j for t, j in chunk if t == "c"]
             earr = (_native.RvqEntry * max(len(es), 1))(*es)
+            qarr = (_native.RvqInt8Entry * max(len(qs), 1))(*qs)
             carr = (_native.RvqCopy * max(len(cs), 1))(*[_native.RvqCopy(*c) for c in cs])
-            self.batches.append((earr, len(es), carr, len(cs)))
+            self.batches.append((earr, len(es), qarr, len(qs), carr, len(cs)))
         self._lib = _native.load()
 
     @property
@@ -115,7 +167,7 @@ class LayerDecodePlan:
         if stream is None:
             stream = torch.cuda.current_stream().cuda_stream
         s = ctypes.c_void_p(stream)
-        for earr, ne, carr, nc in self.batches:
-            rc = self._lib.rvq_decode_layer(earr, ne, carr, nc, s)
+        for earr, ne, qarr, nq, carr, nc in self.batches:
+            rc = self._lib.rvq_decode_layer_mixed(earr, ne, qarr, nq, carr, nc, s)
             if rc:
-                _native.check(rc, "rvq_decode_layer")
+                _native.check(rc, "rvq_decode_layer_mixed")

@@ -67,10 +67,47 @@ class GoldenCase:
 
 
 def case_names() -> List[str]:
-    """Decode fixtures (engine fixtures are named engine_*)."""
+    """RVQ decode fixtures (engine fixtures are named engine_*, int8 ones int8_*)."""
     return sorted(os.path.splitext(os.path.basename(p))[0]
                   for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith("engine_"))
+                  if not os.path.basename(p).startswith(("engine_", "int8_")))
+
+
+def int8_case_names() -> List[str]:
+    """int8_groupwise fixtures (made by make_golden_int8.py)."""
+    return sorted(os.path.splitext(os.path.basename(p))[0]
+                  for p in glob.glob(os.path.join(GOLDEN_DIR, "int8_*.npz")))
+
+
+@dataclass
+class Int8Case:
+    name: str
+    meta: dict
+    q: np.ndarray                  # int8 [trimmed]
+    scales_f16: np.ndarray         # uint16 bits, one per group
+    tail_bf16: np.ndarray          # uint16 bits
+    expected: Dict[int, np.ndarray]
+
+    def entry_torch(self, device="cpu"):
+        """The artifact-format entry dict (compress_full_model.py:414-425)."""
+        import torch
+        gs = int(self.meta["group_size"])
+        return {
+            "method": "int8_groupwise", "shape": list(self.meta["shape"]), "dtype": "bfloat16",
+            "group_size": gs, "trimmed_numel": int(self.meta["trimmed_numel"]),
+            "q": torch.from_numpy(self.q.copy()).view(-1, gs).to(device),
+            "scales": torch.from_numpy(self.scales_f16.astype(np.int16)).view(torch.float16).to(device),
+            "tail": torch.from_numpy(self.tail_bf16.astype(np.int16)).view(torch.bfloat16).to(device),
+            "mse": 0.0, "rel_rmse": 0.0,
+        }
+
+
+def load_int8_case(name: str) -> Int8Case:
+    z = np.load(os.path.join(GOLDEN_DIR, f"{name}.npz"))
+    meta = json.loads(bytes(z["meta_json"]).decode())
+    expected = {kind: z[f"expected_{key}"] for kind, key in KIND_KEYS.items()}
+    return Int8Case(name=name, meta=meta, q=z["q"], scales_f16=z["scales_f16"], tail_bf16=z["tail_bf16"],
+                    expected=expected)
 
 
 def load_case(name: str) -> GoldenCase:

@@ -180,3 +180,22 @@ def test_no_device_means_unavailable():
         import torch as _t
         entry = {"d": 8, "group_size": 8, "trimmed_numel": 8, "method": "rvq_groupwise"}
         tdk.decode_rvq_triton_into(entry, _t.zeros(1, 256, 8), _t.zeros(8))
+
+
+def test_int8_entry_checks(lib):
+    """Host-side validation of rvq_int8_entry (no device memory touched)."""
+    assert ctypes.sizeof(_native.RvqInt8Entry) == 4 * 8 + 3 * 8 + 4 * 4
+    e = _native.RvqInt8Entry()
+    e.q, e.scales, e.out = 0x1000, 0x2000, 0x3000
+    e.trimmed, e.group_size, e.tail_numel = 4096, 128, 0
+    e.scale_kind, e.tail_kind, e.out_kind = _native.RVQ_F16, _native.RVQ_BF16, _native.RVQ_BF16
+    assert lib.rvq_check_int8_entry(ctypes.byref(e)) == _native.RVQ_OK
+    e.trimmed = 4000                                   # not a multiple of the group size
+    assert lib.rvq_check_int8_entry(ctypes.byref(e)) == _native.RVQ_ERR_INVALID
+    e.trimmed, e.out_kind = 4096, _native.RVQ_U8
+    assert lib.rvq_check_int8_entry(ctypes.byref(e)) == _native.RVQ_ERR_UNSUPPORTED
+    e.out_kind, e.tail_numel, e.tail = _native.RVQ_BF16, 5, None
+    assert lib.rvq_check_int8_entry(ctypes.byref(e)) == _native.RVQ_ERR_INVALID
+    e.tail_numel, e.trimmed = 0, 1 << 31
+    assert lib.rvq_check_int8_entry(ctypes.byref(e)) == _native.RVQ_ERR_TOO_LARGE
+    assert lib.rvq_decode_layer_mixed(None, 0, None, 40, None, 0, None) == _native.RVQ_ERR_INVALID

@@ -114,3 +114,24 @@ def test_torch_port_matches_reference(name, kind):
     bits = out.view(torch.int32 if kind == OUT_F32 else torch.int16).numpy()
     bits = bits.view(np.uint32 if kind == OUT_F32 else np.uint16)
     assert bits_equal(bits, case.expected[kind], kind), name
+
+
+@pytest.mark.parametrize("name", __import__("tests._golden", fromlist=["int8_case_names"]).int8_case_names())
+@pytest.mark.parametrize("kind", KINDS)
+def test_int8_oracles_match_reference(name, kind):
+    """numpy oracle and the PyTorch restatement of _decode_int8_into against
+    the reference's own int8 golden output."""
+    import torch
+    from oracle.rvq_oracle import bf16_bits_to_f32, decode_int8_bits, f16_bits_to_f32
+    from oracle.torch_port import decode_int8_into
+    from tests._golden import load_int8_case
+    case = load_int8_case(name)
+    numel = int(np.prod(case.meta["shape"]))
+    got = decode_int8_bits(case.q, f16_bits_to_f32(case.scales_f16), bf16_bits_to_f32(case.tail_bf16),
+                           int(case.meta["group_size"]), numel, kind)
+    assert bits_equal(got, case.expected[kind], kind), name
+    dt = {OUT_F16: torch.float16, OUT_BF16: torch.bfloat16, OUT_F32: torch.float32}[kind]
+    out = torch.zeros(numel, dtype=dt)
+    decode_int8_into(case.entry_torch(), out)
+    b = out.view(torch.int32 if kind == OUT_F32 else torch.int16).numpy()
+    assert bits_equal(b.view(np.uint32 if kind == OUT_F32 else np.uint16), case.expected[kind], kind), name
