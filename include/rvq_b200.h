@@ -141,6 +141,14 @@ int rvq_decode_int8(const rvq_int8_entry* e, void* stream);
 int rvq_decode_layer_mixed(const rvq_entry* entries, int n_entries, const rvq_int8_entry* int8s,
                            int n_int8, const rvq_copy* copies, int n_copies, void* stream);
 
+/* rvq_decode_layer_mixed on at most `max_ctas` CTAs (0: one per SM; each
+ * CTA takes a whole SM).  A decode on a side stream that leaves SMs free lets
+ * the kernels of the layer being computed on the main stream run beside it
+ * (the ping-pong of infer_compressed_layerwise_triton.py:246-277) instead of
+ * queueing behind it. */
+int rvq_decode_layer_ctas(const rvq_entry* entries, int n_entries, const rvq_int8_entry* int8s,
+                          int n_int8, const rvq_copy* copies, int n_copies, int max_ctas, void* stream);
+
 /* One fused dequant-GEMV y = W x for a batch of one (no counterpart in the
  * reference, which reconstructs W into the slot and then calls F.linear:
  * infer_compressed_layerwise_triton.py:290-292 / lines 296-297).  W is an
@@ -367,6 +375,42 @@ int rvq_gemv_tiles_exact(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream
  * artifact. */
 int64_t rvq_tile_codes_bytes(int64_t rows, int64_t cols);
 int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64_t cols, void* out, void* stream);
+
+/* Small-batch fused dequant-GEMM on the tensor cores (no counterpart in the
+ * reference, which reconstructs W into the slot and calls F.linear:
+ * infer_compressed_layerwise_triton.py:290-292):
+ *   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < tokens (1..256)
+ * W is rebuilt bit-identically to rvq_decode's bf16 slot values straight into
+ * shared memory as the A operand of tcgen05.mma (M = 128 weight rows, N =
+ * tokens rounded up to 16, fp32 accumulation in TMEM); only the codes, scales
+ * and x are read from HBM.  W: K=4 stages, 256 codes, uint8 codes in the
+ * tile-major layout of rvq_tile_codes (weight.indices, 16-byte aligned), no
+ * tail; codebook fp32, fp16 or bf16.  x bf16 [tokens][cols] row-major, 16-byte
+ * aligned, cols a multiple of 8; y bf16 [tokens][rows].  Deterministic: split-K
+ * pieces are added in a fixed order. */
+typedef struct rvq_gemv_batch_job {
+    rvq_entry weight;         /* weight.out is ignored */
+    const void* x;            /* device, [tokens][cols] */
+    void* y;                  /* device, [tokens][rows] */
+    int64_t rows;
+    int64_t cols;
+    int64_t tokens;
+    int32_t x_kind;           /* RVQ_BF16 */
+    int32_t y_kind;           /* RVQ_BF16 */
+} rvq_gemv_batch_job;
+
+/* Bytes of workspace rvq_gemv_batch needs for this job on the current device
+ * (split-K partial sums and one ticket per 128-row tile); 0 if the job is not
+ * supported.  The workspace is 256-byte aligned device memory, zero-filled
+ * once when allocated (every launch leaves its tickets at zero again);
+ * launches that share a workspace must not overlap on the GPU. */
+size_t rvq_gemv_batch_workspace_size(const rvq_gemv_batch_job* job);
+int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads and clears the sticky flag set when an rvq_gemv_batch wait on an
+ * mbarrier gave up (the result of that launch is then invalid).  Synchronises
+ * the current device.  Returns 1 if set, 0 if not, or -RVQ_ERR_CUDA. */
+int rvq_take_batch_timeout(void);
 
 /* Prefill GEMM with the weight decoded into shared memory, never into HBM:
  *   y[m][n] = bf16( sum_k x[m][k] * W[n][k] )

@@ -125,6 +125,9 @@ def load() -> ctypes.CDLL:
     lib.rvq_decode_layer_mixed.restype = i32
     lib.rvq_decode_layer_mixed.argtypes = [ctypes.POINTER(RvqEntry), i32, ctypes.POINTER(RvqInt8Entry), i32,
                                            ctypes.POINTER(RvqCopy), i32, vp]
+    lib.rvq_decode_layer_ctas.restype = i32
+    lib.rvq_decode_layer_ctas.argtypes = [ctypes.POINTER(RvqEntry), i32, ctypes.POINTER(RvqInt8Entry), i32,
+                                          ctypes.POINTER(RvqCopy), i32, i32, vp]
     lib.rvq_take_index_error.restype = i32
     lib.rvq_take_index_error.argtypes = []
     lib.rvq_last_cuda_error.restype = i32

@@ -384,8 +384,14 @@ __device__ __forceinline__ void process_int8(const Job& job, uint32_t a, uint32_
     for (uint32_t t = a + warp; t < e; t += kWarps) int8_tile(job, t, lane);
 }
 
+// Fast-path variant a launch is compiled for (one inlined copy of the hot loop
+// per kernel keeps it free of register spills): 0 none, 1 bf16 output with
+// group_vecs % 4 == 0, 2 bf16, 3 fp16 with group_vecs % 4 == 0, 4 fp16.
+constexpr int kFastVariants = 5;
+
 // Decode tiles [a, e) (job-local) of one RVQ job; `owner` copies the tail.
 // All threads of the CTA call it.
+template <int FV>
 __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t e, bool owner, int warp,
                                             int lane, uint4* smem, bool& staged_once) {
     if (job.nvec == 0) {                    // tail-only entry: nothing to stage
@@ -397,24 +403,17 @@ __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t
     const int mode = stage_codebook(job, smem);
     if (owner) copy_tail(job);
     uint32_t g = a;                         // first tile left for the generic path
-    if (mode == GATHER_SMEM_F16 && job.fast_ok) {
+    if (FV != 0 && mode == GATHER_SMEM_F16 && job.fast_ok) {      // the host matched job and variant
         const uint32_t fe = min(e, job.full_tiles);
         if (a < fe) {
-            const char* cs = reinterpret_cast<const char*>(smem);
-            const bool s4 = (job.gv.d & 3u) == 0;
-            if (job.out_kind == RVQ_BF16) {
-                if (s4) run_fast<true, true>(job, a, fe, warp, lane, cs);
-                else run_fast<true, false>(job, a, fe, warp, lane, cs);
-            } else {
-                if (s4) run_fast<false, true>(job, a, fe, warp, lane, cs);
-                else run_fast<false, false>(job, a, fe, warp, lane, cs);
-            }
+            run_fast<FV == 1 || FV == 2, FV == 1 || FV == 3>(job, a, fe, warp, lane, reinterpret_cast<const char*>(smem));
             g = fe;
         }
     }
     for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t, lane, smem, mode);
 }
 
+template <int FV>
 __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_constant__ LayerParams p) {
     extern __shared__ uint4 smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -433,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
             const uint32_t r = b - job.cta_begin, cc = job.cta_count, tc = job.tile_count;
             const uint32_t a = (uint32_t)(((uint64_t)tc * r) / cc), e = (uint32_t)(((uint64_t)tc * (r + 1)) / cc);
             if (job.kind == JOB_INT8) process_int8(job, a, e, r == 0, warp, lane);
-            else process_rvq(job, a, e, r == 0, warp, lane, smem, staged_once);
+            else process_rvq<FV>(job, a, e, r == 0, warp, lane, smem, staged_once);
         }
         return;
     }
@@ -453,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
             process_int8(job, a - jb, e - jb, a == jb, warp, lane);
             continue;
         }
-        process_rvq(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
+        process_rvq<FV>(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
     }
 }
 
@@ -469,6 +468,31 @@ struct DeviceInfo {
 };
 
 static DeviceInfo g_devices[kMaxDevices];
+
+using LayerKernel = void (*)(LayerParams);
+static LayerKernel layer_kernel(int fv) {
+    switch (fv) {
+        case 1: return rvq_layer_kernel<1>;
+        case 2: return rvq_layer_kernel<2>;
+        case 3: return rvq_layer_kernel<3>;
+        case 4: return rvq_layer_kernel<4>;
+        default: return rvq_layer_kernel<0>;
+    }
+}
+
+// The fast-path variant of a launch: that of its first fast job; fast jobs of
+// another variant lose the fast path (and its staging layout) in this launch.
+static int choose_variant(LayerParams& p) {
+    int fv = 0;
+    for (int i = 0; i < p.njobs; ++i) {
+        Job& j = p.jobs[i];
+        if (j.kind != JOB_RVQ || !j.fast_ok) continue;
+        const int v = (j.out_kind == RVQ_BF16 ? 1 : 3) + ((j.gv.d & 3u) == 0 ? 0 : 1);
+        if (fv == 0) fv = v;
+        if (v != fv) j.fast_ok = 0;
+    }
+    return fv;
+}
 static std::mutex g_dev_mutex;
 
 static int cuda_fail(cudaError_t e) {
@@ -493,13 +517,16 @@ static int device_info(DeviceInfo** out) {
             di.ok = false;
         } else {
             di.sm_count = prop.multiProcessorCount;
-            cudaFuncAttributes fa;
-            e = cudaFuncGetAttributes(&fa, rvq_layer_kernel);
-            // dynamic shared memory may use what the kernel's static shared memory leaves
-            di.max_smem = (int)prop.sharedMemPerBlockOptin - (e == cudaSuccess ? (int)fa.sharedSizeBytes : 0);
-            if (e == cudaSuccess)
-                e = cudaFuncSetAttribute(rvq_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         di.max_smem);
+            di.max_smem = (int)prop.sharedMemPerBlockOptin;
+            for (int v = 0; v < kFastVariants && e == cudaSuccess; ++v) {
+                cudaFuncAttributes fa;
+                e = cudaFuncGetAttributes(&fa, layer_kernel(v));
+                // dynamic shared memory may use what the kernel's static shared memory leaves
+                const int avail = (int)prop.sharedMemPerBlockOptin - (int)fa.sharedSizeBytes;
+                if (e == cudaSuccess) e = cudaFuncSetAttribute(layer_kernel(v), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                             avail);
+                if (avail < di.max_smem) di.max_smem = avail;
+            }
             di.ok = (e == cudaSuccess);
             if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
         }
@@ -673,10 +700,11 @@ static uint32_t plan_per_cta(LayerParams& p, uint32_t sms) {
     return begin;
 }
 
-static int launch_jobs(LayerParams& p, size_t smem_need, void* stream) {
+static int launch_jobs(LayerParams& p, size_t smem_need, int max_ctas, void* stream) {
     DeviceInfo* di = nullptr;
     int rc = device_info(&di);
     if (rc != RVQ_OK) return rc;
+    const uint32_t ctas = (max_ctas > 0 && max_ctas < di->sm_count) ? (uint32_t)max_ctas : (uint32_t)di->sm_count;
     uint32_t total = 0;
     for (int i = 0; i < p.njobs; ++i) {
         p.jobs[i].tile_begin = total;
@@ -685,13 +713,14 @@ static int launch_jobs(LayerParams& p, size_t smem_need, void* stream) {
     p.total_tiles = total;
     if (total == 0) return RVQ_OK;
     if (smem_need > (size_t)di->max_smem) return RVQ_ERR_TOO_LARGE;
-    uint32_t grid = plan_per_cta(p, (uint32_t)di->sm_count);
+    uint32_t grid = plan_per_cta(p, ctas);
     p.per_cta_jobs = grid ? 1u : 0u;
     if (!grid) {
-        grid = (uint32_t)di->sm_count;
+        grid = ctas;
         if (grid > total) grid = total;
     }
-    rvq_layer_kernel<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
+    const int fv = choose_variant(p);
+    layer_kernel(fv)<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return RVQ_OK;
@@ -727,6 +756,12 @@ int rvq_decode_int8(const rvq_int8_entry* e, void* stream) {
 
 int rvq_decode_layer_mixed(const rvq_entry* entries, int n_entries, const rvq_int8_entry* int8s, int n_int8,
                            const rvq_copy* copies, int n_copies, void* stream) {
+    return rvq_decode_layer_ctas(entries, n_entries, int8s, n_int8, copies, n_copies, 0, stream);
+}
+
+int rvq_decode_layer_ctas(const rvq_entry* entries, int n_entries, const rvq_int8_entry* int8s, int n_int8,
+                          const rvq_copy* copies, int n_copies, int max_ctas, void* stream) {
+    if (max_ctas < 0) return RVQ_ERR_INVALID;
     if (n_entries < 0 || n_int8 < 0 || n_copies < 0 || n_entries + n_int8 + n_copies > RVQ_MAX_LAYER_JOBS)
         return RVQ_ERR_INVALID;
     if ((n_entries && !entries) || (n_int8 && !int8s) || (n_copies && !copies)) return RVQ_ERR_INVALID;
@@ -758,7 +793,7 @@ int rvq_decode_layer_mixed(const rvq_entry* entries, int n_entries, const rvq_in
         j.nvec = (uint32_t)c.nbytes;
         j.tile_count = (uint32_t)((c.nbytes + kCopyTileBytes - 1) / kCopyTileBytes);
     }
-    return launch_jobs(p, smem, stream);
+    return launch_jobs(p, smem, max_ctas, stream);
 }
 
 int rvq_take_index_error(void) {

@@ -1,0 +1,476 @@
+// Small-batch fused dequant-GEMM on the tensor cores (sm_100a):
+//
+//   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < T tokens (1..256), W an RVQ entry
+//
+// The reference materialises W into the slot and calls F.linear
+// (infer_compressed_layerwise_triton.py:290-292).  Here W never reaches HBM:
+// it stays the A operand of tcgen05.mma.  A CTA owns 128-row tiles of W and
+// ranges of 64-column chunks ("segments"); for every chunk, 16 decoder warps
+// rebuild the 128 x 64 weights bit-identically to the slot's bf16 values
+// (rvq_vecdecode.cuh) straight into shared memory in the K-major
+// 128-byte-swizzled layout (one RVQ vector = one 16-byte swizzle chunk), the
+// issuer warp loads x[0:T][chunk] by TMA (rows past T read as zero) and issues
+// four tcgen05.mma (kind::f16, M = 128 weight rows, N = T rounded up to 16,
+// K = 16), accumulating in TMEM.  Four epilogue warps read each finished
+// segment with tcgen05.ld; two accumulators alternate, so the next segment's
+// MMAs run while the previous one is read out.
+//
+// Work split: the (row tile, chunk) units in row-tile order are cut into one
+// contiguous range per SM, so every CTA decodes the same number of chunks.  A
+// tile cut into several pieces writes fp32 partial sums to the workspace; the
+// CTA that finishes a tile's last piece (ticket counter) adds the pieces in
+// piece order and writes y, so results do not depend on timing.  Tiles held
+// by one CTA write y directly.
+//
+// Only the codes (0.5 B per weight), the scales and x are read from HBM.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string.h>
+#include <vector>
+
+#include "rvq_common.cuh"
+#include "rvq_sm100.cuh"
+#include "rvq_vecdecode.cuh"
+
+namespace rvq {
+namespace batch {
+
+using namespace sm100;
+
+constexpr int kDecodeWarps = 16;
+constexpr int kEpiWarps = 4;
+constexpr int kIssuer = kDecodeWarps + kEpiWarps;           // warp index of the issuer
+constexpr int kThreads = (kIssuer + 1) * 32;                 // 672
+constexpr int kTileRows = 128;                               // MMA M: weight rows per tile
+constexpr int kChunk = 64;                                   // columns per chunk (one 128-byte swizzle row)
+constexpr int kChunkVecs = kChunk / 8;
+constexpr int kWStageBytes = kTileRows * kChunk * 2;         // 16 KB
+constexpr int kMaxStages = 4;
+constexpr int kMaxTokens = 256;
+constexpr int kMaxCtas = 160;
+constexpr int kMaxSegs = 512;
+constexpr int kMaxSegsPerCta = 8;
+constexpr long long kWaitLimit = 1ll << 24;
+constexpr int kBudget = 226 * 1024;                          // dynamic shared memory limit used per CTA
+
+__device__ int g_batch_timeout;
+
+struct Seg {
+    uint32_t tile_piece;      // tile << 12 | piece << 6 | npieces
+    uint32_t chunks;          // kc0 << 16 | kc1
+    int32_t slot;             // first workspace slot of the tile's pieces (npieces > 1)
+};
+
+struct BParams {
+    CUtensorMap xmap;         // x [T][K] bf16, box {64, npad}, 128-byte swizzle
+    const uint32_t* codes;    // tile-major code lines [ceil(K/256)][R][32]
+    const void* cb;
+    const void* scales;
+    __nv_bfloat16* y;         // [T][R]
+    float* part;              // workspace: [slots][T][128] fp32
+    uint32_t* tickets;        // workspace: [tiles]
+    int32_t R, G, T, npad, stages, n_ctas;
+    int32_t cb_kind, scale_kind, row_scales;
+    FastDiv gvdiv, rpsdiv;
+    int32_t seg_first[kMaxCtas + 1];
+    Seg segs[kMaxSegs];
+};
+
+__device__ __forceinline__ int seg_tile(const Seg& s) { return (int)(s.tile_piece >> 12); }
+__device__ __forceinline__ int seg_piece(const Seg& s) { return (int)((s.tile_piece >> 6) & 63u); }
+__device__ __forceinline__ int seg_np(const Seg& s) { return (int)(s.tile_piece & 63u); }
+__device__ __forceinline__ int seg_kc0(const Seg& s) { return (int)(s.chunks >> 16); }
+__device__ __forceinline__ int seg_kc1(const Seg& s) { return (int)(s.chunks & 0xffffu); }
+
+__device__ __forceinline__ float load_scale_at(const BParams& p, int row, int g) {
+    if (p.row_scales) return load_as_f32(p.scales, fastdiv((uint32_t)row, p.rpsdiv), p.scale_kind);
+    if (g >= p.G) return 0.f;
+    return load_as_f32(p.scales, fastdiv((uint32_t)row * (uint32_t)p.G + (uint32_t)g, p.gvdiv), p.scale_kind);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __grid_constant__ BParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    char* cbs = reinterpret_cast<char*>(base);                               // 128 KB codebook
+    uint8_t* ws = base + vdec::kCbBytes;                                     // W stages
+    const int xstage_bytes = p.npad * 128;
+    uint8_t* xs = ws + p.stages * kWStageBytes;                              // x stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(xs + p.stages * xstage_bytes);
+    // w_full[S] | x_full[S] | done[S] | acc_full[2] | acc_free[2]
+    const uint32_t bar_w = smem_addr(bars), bar_x = bar_w + 8 * kMaxStages, bar_done = bar_x + 8 * kMaxStages;
+    const uint32_t bar_accf = bar_done + 8 * kMaxStages, bar_acce = bar_accf + 16;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kMaxStages + 4);
+    __shared__ int last_piece;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = p.stages;
+    const int s_first = p.seg_first[blockIdx.x], s_last = p.seg_first[blockIdx.x + 1];
+    const uint32_t tmem_cols = p.npad * 2 <= 32 ? 32u : (p.npad * 2 <= 64 ? 64u : (p.npad * 2 <= 128 ? 128u
+                                                       : (p.npad * 2 <= 256 ? 256u : 512u)));
+
+    if (tid == 0) {
+        for (int s = 0; s < kMaxStages; ++s) {
+            mbar_init(bar_w + 8 * s, kDecodeWarps);
+            mbar_init(bar_x + 8 * s, 1);
+            mbar_init(bar_done + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar_accf + 8 * a, 1);
+            mbar_init(bar_acce + 8 * a, kEpiWarps);
+        }
+        mbar_init_fence();
+    }
+    if (warp == 0) tmem_alloc(smem_addr(tmem_slot), tmem_cols);
+    const bool cb_smem = vdec::stage_cb8(p.cb, p.cb_kind, cbs, tid, kThreads);   // ends with a barrier
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < kDecodeWarps) {
+        // ---- decoders: thread (v = tid & 7, r = tid / 8 + 64 j) rebuilds vector v of rows r of each chunk
+        uint32_t lb[4];
+        vdec::lane_bits(lane, lb);
+        const int v = tid & 7;
+        int g = 0;
+        for (int si = s_first; si < s_last; ++si) {
+            const Seg sg = p.segs[si];
+            const int tile = seg_tile(sg), kc1 = seg_kc1(sg);
+            for (int kc = seg_kc0(sg); kc < kc1; ++kc, ++g) {
+                const int st = g % S;
+                if (g >= S) {                                      // the MMAs of chunk g - S left stage st
+                    if (lane == 0) mbar_wait(bar_done + 8 * st, ((g / S) - 1) & 1, kWaitLimit, &g_batch_timeout);
+                    __syncwarp();
+                }
+                const uint32_t* lines = p.codes + ((int64_t)(kc >> 2) * p.R) * 32 + (kc & 3) * kChunkVecs + v;
+                uint8_t* wst = ws + st * kWStageBytes;
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int r = (tid >> 3) + 64 * j;
+                    const int row = tile * kTileRows + r;
+                    uint32_t w = 0u;
+                    float s = 0.f;
+                    if (row < p.R) {
+                        w = __ldg(lines + (int64_t)row * 32);
+                        s = load_scale_at(p, row, kc * kChunkVecs + v);
+                    }
+                    const uint4 q = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, w, lb, s)
+                                            : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, w, lb, s);
+                    *reinterpret_cast<uint4*>(wst + r * 128 + ((v ^ (r & 7)) << 4)) = q;
+                }
+                fence_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_w + 8 * st);
+            }
+        }
+    } else if (warp == kIssuer) {
+        // ---- issuer: x by TMA (S - 1 chunks ahead), MMAs once a chunk's weights are decoded
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc_bf16(kTileRows, p.npad);
+            // chunk index g -> column chunk, walking the segments
+            auto chunk_of = [&](int g) -> int {
+                for (int si = s_first; si < s_last; ++si) {
+                    const int n = seg_kc1(p.segs[si]) - seg_kc0(p.segs[si]);
+                    if (g < n) return seg_kc0(p.segs[si]) + g;
+                    g -= n;
+                }
+                return -1;
+            };
+            auto load_x = [&](int g) {
+                const int kc = chunk_of(g);
+                if (kc < 0) return;
+                const int st = g % S;
+                mbar_expect_tx(bar_x + 8 * st, (uint32_t)xstage_bytes);
+                tma_load_2d(smem_addr(xs + st * xstage_bytes), &p.xmap, kc * kChunk, 0, bar_x + 8 * st);
+            };
+            for (int g = 0; g < S - 1; ++g) load_x(g);
+            int g = 0;
+            for (int si = s_first; si < s_last; ++si) {
+                const Seg sg = p.segs[si];
+                const int acc = (si - s_first) & 1, n_seg = si - s_first;
+                if (n_seg >= 2)                                    // the epilogue has read this accumulator
+                    mbar_wait(bar_acce + 8 * acc, ((n_seg >> 1) - 1) & 1, kWaitLimit, &g_batch_timeout);
+                tc_fence_after();
+                const int kc0 = seg_kc0(sg), kc1 = seg_kc1(sg);
+                for (int kc = kc0; kc < kc1; ++kc, ++g) {
+                    const int st = g % S;
+                    mbar_wait(bar_w + 8 * st, (g / S) & 1, kWaitLimit, &g_batch_timeout);
+                    mbar_wait(bar_x + 8 * st, (g / S) & 1, kWaitLimit, &g_batch_timeout);
+                    tc_fence_after();
+                    const uint32_t wa = smem_addr(ws + st * kWStageBytes), xa = smem_addr(xs + st * xstage_bytes);
+#pragma unroll
+                    for (int ks = 0; ks < kChunk / 16; ++ks)
+                        mma_bf16(tmem + (uint32_t)(acc * p.npad), sw128_desc(wa + 32 * ks), sw128_desc(xa + 32 * ks),
+                                 idesc, kc > kc0 || ks > 0);
+                    mma_commit(bar_done + 8 * st);
+                    if (kc + 1 == kc1) mma_commit(bar_accf + 8 * acc);
+                    // x of chunk g + S - 1 goes to chunk g - 1's stage once its MMAs are done
+                    if (g >= 1) {
+                        mbar_wait(bar_done + 8 * ((g - 1) % S), ((g - 1) / S) & 1, kWaitLimit, &g_batch_timeout);
+                        load_x(g + S - 1);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---- epilogue warps: warp e reads TMEM lanes 32 e .. 32 e + 31 (tile rows)
+        const int e = warp - kDecodeWarps;
+        const int r = 32 * e + lane;
+        for (int si = s_first; si < s_last; ++si) {
+            const Seg sg = p.segs[si];
+            const int acc = (si - s_first) & 1, n_seg = si - s_first;
+            const int tile = seg_tile(sg), np = seg_np(sg);
+            const int row = tile * kTileRows + r;
+            if (lane == 0) mbar_wait(bar_accf + 8 * acc, (n_seg >> 1) & 1, kWaitLimit, &g_batch_timeout);
+            __syncwarp();
+            tc_fence_after();
+            float* part = p.part + ((int64_t)(sg.slot + seg_piece(sg)) * p.T) * kTileRows + r;
+            for (int c0 = 0; c0 < p.npad; c0 += 32) {
+                uint32_t vals[32];
+                tmem_ld32(tmem + ((uint32_t)(32 * e) << 16) + (uint32_t)(acc * p.npad + c0), vals);
+                tmem_ld_wait();
+                const int tn = min(32, p.T - c0);
+                if (np == 1) {
+                    if (row < p.R) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (i < tn) p.y[(int64_t)(c0 + i) * p.R + row] = __float2bfloat16_rn(__uint_as_float(vals[i]));
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (i < tn) part[(int64_t)(c0 + i) * kTileRows] = __uint_as_float(vals[i]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acce + 8 * acc);
+            if (np > 1) {
+                // the CTA that finishes the tile's last piece adds the pieces in piece order
+                __threadfence();
+                asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
+                if (e == 0 && lane == 0) last_piece = atomicAdd(&p.tickets[tile], 1u) == (uint32_t)(np - 1);
+                asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
+                if (last_piece) {
+                    __threadfence();
+                    const float* base_p = p.part + ((int64_t)sg.slot * p.T) * kTileRows + r;
+                    if (row < p.R) {
+                        for (int t = 0; t < p.T; ++t) {
+                            float sum = __ldcg(base_p + (int64_t)t * kTileRows);
+                            for (int q = 1; q < np; ++q) sum += __ldcg(base_p + ((int64_t)q * p.T + t) * kTileRows);
+                            p.y[(int64_t)t * p.R + row] = __float2bfloat16_rn(sum);
+                        }
+                    }
+                    if (e == 0 && lane == 0) p.tickets[tile] = 0u;     // ready for the next launch
+                }
+                asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, tmem_cols);
+}
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+std::mutex g_mu;
+bool g_ready[64] = {}, g_ok[64] = {};
+int g_sms[64] = {};
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int prepare(int* sms) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+        last_cuda_error_slot() = (int)e;
+        return RVQ_ERR_UNAVAILABLE;
+    }
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_ready[dev]) {
+        g_ready[dev] = true;
+        cudaDeviceProp prop;
+        e = cudaGetDeviceProperties(&prop, dev);
+        if (e == cudaSuccess && prop.major == 10 && prop.sharedMemPerBlockOptin >= (size_t)kBudget) {
+            g_sms[dev] = prop.multiProcessorCount;
+            e = cudaFuncSetAttribute(rvq_gemv_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBudget);
+            if (e == cudaSuccess && g_encode == nullptr) {
+                void* fn = nullptr;
+                cudaDriverEntryPointQueryResult q;
+                e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+                if (e == cudaSuccess && q == cudaDriverEntryPointSuccess)
+                    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+            }
+            g_ok[dev] = e == cudaSuccess && g_encode != nullptr;
+        }
+        if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
+    }
+    *sms = g_sms[dev];
+    return g_ok[dev] ? RVQ_OK : RVQ_ERR_UNAVAILABLE;
+}
+
+int npad_of(int64_t T) { return (int)((T + 15) / 16 * 16); }
+
+int stages_for(int npad) {
+    const int per = kWStageBytes + npad * 128;
+    int s = (kBudget - 1024 - vdec::kCbBytes - 256) / per;
+    return s > kMaxStages ? kMaxStages : s;
+}
+
+// Segments of the balanced split.  Returns the workspace bytes it needs
+// (partials, then one ticket per tile) or a negative status.
+int64_t plan(const rvq_gemv_batch_job& j, int sms, BParams* p) {
+    const int64_t R = j.rows, G = j.cols / 8, T = j.tokens;
+    const int64_t KC = (G + kChunkVecs - 1) / kChunkVecs;
+    const int64_t NT = (R + kTileRows - 1) / kTileRows;
+    const int64_t U = NT * KC;
+    int64_t ctas = sms < kMaxCtas ? sms : kMaxCtas;
+    if (ctas > U) ctas = U;
+    // pieces of every tile: the CTA ranges that overlap it
+    int nseg = 0, slots = 0;
+    std::vector<int> tile_np((size_t)NT, 0), tile_slot((size_t)NT, 0);
+    for (int pass = 0; pass < 2; ++pass) {
+        nseg = 0;
+        std::vector<int> piece((size_t)NT, 0);
+        for (int64_t c = 0; c < ctas; ++c) {
+            const int64_t u0 = U * c / ctas, u1 = U * (c + 1) / ctas;
+            if (p) p->seg_first[c] = nseg;
+            int in_cta = 0;
+            for (int64_t u = u0; u < u1;) {
+                const int64_t tile = u / KC, kc0 = u % KC;
+                const int64_t kc1 = (u1 - tile * KC) < KC ? (u1 - tile * KC) : KC;
+                if (pass == 0) {
+                    tile_np[(size_t)tile] += 1;
+                } else {
+                    if (nseg >= kMaxSegs || ++in_cta > kMaxSegsPerCta) return -RVQ_ERR_TOO_LARGE;
+                    Seg& s = p->segs[nseg];
+                    const int np = tile_np[(size_t)tile];
+                    s.tile_piece = ((uint32_t)tile << 12) | ((uint32_t)piece[(size_t)tile] << 6) | (uint32_t)np;
+                    s.chunks = ((uint32_t)kc0 << 16) | (uint32_t)kc1;
+                    s.slot = np > 1 ? tile_slot[(size_t)tile] : 0;
+                    piece[(size_t)tile] += 1;
+                }
+                ++nseg;
+                u = tile * KC + kc1;
+            }
+        }
+        if (pass == 0) {
+            for (int64_t t = 0; t < NT; ++t) {
+                if (tile_np[(size_t)t] > 63) return -RVQ_ERR_TOO_LARGE;
+                if (tile_np[(size_t)t] > 1) {
+                    tile_slot[(size_t)t] = slots;
+                    slots += tile_np[(size_t)t];
+                }
+            }
+            if (!p) break;
+        }
+    }
+    if (p) {
+        p->seg_first[ctas] = nseg;
+        p->n_ctas = (int32_t)ctas;
+    }
+    const int64_t part_bytes = ((int64_t)slots * T * kTileRows * 4 + 255) / 256 * 256;
+    return part_bytes + NT * 4;
+}
+
+int check_job(const rvq_gemv_batch_job* j) {
+    if (j == nullptr || j->x == nullptr || j->y == nullptr) return RVQ_ERR_INVALID;
+    const rvq_entry& w = j->weight;
+    int rc = rvq_check_entry(&w);
+    if (rc != RVQ_OK) return rc;
+    if (w.stages != 4 || w.ncodes != 256 || w.index_kind != RVQ_U8 || w.d != 8) return RVQ_ERR_UNSUPPORTED;
+    if (j->rows < 1 || j->cols < 8 || j->cols % 8 || j->tokens < 1 || j->tokens > kMaxTokens)
+        return RVQ_ERR_UNSUPPORTED;
+    if (j->rows * (j->cols / 8) != w.nvec || w.trimmed != w.nvec * 8 || w.tail_numel != 0) return RVQ_ERR_UNSUPPORTED;
+    if (j->x_kind != RVQ_BF16 || j->y_kind != RVQ_BF16) return RVQ_ERR_UNSUPPORTED;
+    if (w.codebook_kind != RVQ_F32 && w.codebook_kind != RVQ_F16 && w.codebook_kind != RVQ_BF16)
+        return RVQ_ERR_UNSUPPORTED;
+    if (((uintptr_t)w.indices & 15) || ((uintptr_t)j->x & 15) || ((j->cols * 2) & 15)) return RVQ_ERR_INVALID;
+    if (w.nvec >= (1ll << 32) || j->rows >= (1ll << 24) || (j->cols / kChunk) >= (1 << 16)) return RVQ_ERR_TOO_LARGE;
+    return RVQ_OK;
+}
+
+}  // namespace batch
+}  // namespace rvq
+
+using namespace rvq;
+using namespace rvq::batch;
+
+extern "C" {
+
+size_t rvq_gemv_batch_workspace_size(const rvq_gemv_batch_job* job) {
+    if (check_job(job) != RVQ_OK) return 0;
+    int sms = 0;
+    if (prepare(&sms) != RVQ_OK) return 0;
+    const int64_t b = plan(*job, sms, nullptr);
+    return b < 0 ? 0 : (size_t)b;
+}
+
+int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = check_job(job);
+    if (rc != RVQ_OK) return rc;
+    int sms = 0;
+    rc = prepare(&sms);
+    if (rc != RVQ_OK) return rc;
+    static thread_local BParams p;
+    memset(&p, 0, sizeof(p));
+    const int64_t need = plan(*job, sms, &p);
+    if (need < 0) return (int)-need;
+    if (workspace == nullptr || workspace_bytes < (size_t)need || ((uintptr_t)workspace & 255)) return RVQ_ERR_INVALID;
+    const rvq_entry& w = job->weight;
+    p.npad = npad_of(job->tokens);
+    p.stages = stages_for(p.npad);
+    const cuuint64_t dims[2] = {(cuuint64_t)job->cols, (cuuint64_t)job->tokens};
+    const cuuint64_t strides[1] = {(cuuint64_t)job->cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kChunk, (cuuint32_t)p.npad};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult cr = g_encode(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(job->x), dims, strides,
+                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return RVQ_ERR_INVALID;
+    const int64_t NT = (job->rows + kTileRows - 1) / kTileRows;
+    p.codes = reinterpret_cast<const uint32_t*>(w.indices);
+    p.cb = w.codebook;
+    p.scales = w.scales;
+    p.y = reinterpret_cast<__nv_bfloat16*>(job->y);
+    p.part = reinterpret_cast<float*>(workspace);
+    p.tickets = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(workspace) + (size_t)need - (size_t)NT * 4);
+    p.R = (int32_t)job->rows;
+    p.G = (int32_t)(job->cols / 8);
+    p.T = (int32_t)job->tokens;
+    p.cb_kind = w.codebook_kind;
+    p.scale_kind = w.scale_kind;
+    const uint32_t gv = (uint32_t)w.group_vecs;
+    p.gvdiv = make_fastdiv(gv);
+    p.row_scales = gv % (uint32_t)p.G == 0;
+    p.rpsdiv = make_fastdiv(p.row_scales ? gv / (uint32_t)p.G : 1u);
+    const size_t smem = 1024 + (size_t)vdec::kCbBytes + (size_t)p.stages * (kWStageBytes + p.npad * 128) + 256;
+    rvq_gemv_batch_kernel<<<p.n_ctas, kThreads, smem, (cudaStream_t)stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        last_cuda_error_slot() = (int)e;
+        return RVQ_ERR_CUDA;
+    }
+    return RVQ_OK;
+}
+
+int rvq_take_batch_timeout(void) {
+    int v = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_batch_timeout, sizeof(int));
+    const int zero = 0;
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_batch_timeout, &zero, sizeof(int));
+    if (e != cudaSuccess) {
+        last_cuda_error_slot() = (int)e;
+        return -RVQ_ERR_CUDA;
+    }
+    return v;
+}
+
+}  // extern "C"

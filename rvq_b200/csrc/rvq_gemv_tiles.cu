@@ -36,6 +36,7 @@
 #include <string.h>
 
 #include "rvq_common.cuh"
+#include "rvq_vecdecode.cuh"
 
 namespace rvq {
 namespace tiles {
@@ -523,84 +524,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
 // lane g of a warp owns group g of the tile, and a warp takes 8 rows per
 // batch, reduced over the lanes with reduce8.
 //
-// The codebook sits in shared memory as fp16 with 8 copies per entry: entry
-// (k, c), copy p at byte (k / 2) << 16 | c << 8 | (k % 2) << 7 | p << 4, so
-// one prmt of the code word gives a lane's address, and the 8 lanes of every
-// quarter-warp phase (p = lane & 7) read 8 different bank quads.  A codebook
-// that fp16 cannot hold exactly is read from global memory in fp32 instead.
+// The codebook sits in shared memory as fp16 with 8 copies per entry
+// (rvq_vecdecode.cuh); a codebook that fp16 cannot hold exactly is read from
+// global memory in fp32 instead.
 // Code words are loaded straight from the tile-major lines, one batch ahead.
 // ---------------------------------------------------------------------------
 namespace exact {
 constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr int kBatchRows = kWarps * 8;                       // 8 rows per warp and batch
-constexpr int kCopies = 8;
-constexpr int kCbBytes = kStages * kCodes * 16 * kCopies;    // 128 KB
+constexpr int kCbBytes = vdec::kCbBytes;                     // 128 KB
 constexpr int kMaxStagedTiles = 64;                          // operand partial tiles staged (64 KB)
 constexpr size_t kSmemBytes = (size_t)kCbBytes + (size_t)(kMaxStagedTiles + 1) * kTileCols * 4;
 constexpr int kSwitchRows = 256;                             // starting a unit ~ 256 rows
 }  // namespace exact
-
-// fp16 codebook rows into the 8-copy layout; false if some value is not an
-// exact fp16 number (then the rows are read from global memory instead).
-__device__ __forceinline__ bool stage_cb_exact(const TJob& J, char* cbs) {
-    const int lane = threadIdx.x & 31;
-    int inexact = 0;
-    for (int e = threadIdx.x; e < kPairs; e += exact::kThreads) {
-        uint4 q;
-        if (J.cb_kind == RVQ_F16) {
-            q = __ldg(reinterpret_cast<const uint4*>(J.cb) + e);
-        } else {
-            uint32_t w[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const float f0 = load_as_f32(J.cb, (int64_t)e * 8 + 2 * t, J.cb_kind);
-                const float f1 = load_as_f32(J.cb, (int64_t)e * 8 + 2 * t + 1, J.cb_kind);
-                const __half2 h = __floats2half2_rn(f0, f1);
-                inexact |= (__float_as_uint(__low2float(h)) != __float_as_uint(f0)) |
-                           (__float_as_uint(__high2float(h)) != __float_as_uint(f1)) | isnan(f0) | isnan(f1);
-                w[t] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-            q = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        char* base = cbs + ((e >> 9) << 16) + ((e & 255) << 8) + (((e >> 8) & 1) << 7);
-#pragma unroll
-        for (int i = 0; i < exact::kCopies; ++i) {
-            const int cp = (i + lane) & (exact::kCopies - 1);
-            *reinterpret_cast<uint4*>(base + cp * 16) = q;
-        }
-    }
-    return !__syncthreads_or(inexact);
-}
-
-// bf16 weights of one vector: RNE(fp32(scale) * (((0 + cb0) + cb1) + cb2) + cb3)
-template <bool SMEM>
-__device__ __forceinline__ uint4 exact_weights(const char* cbs, const TJob& J, uint32_t w, const uint32_t (&lb)[4],
-                                               float s) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (SMEM) {
-#pragma unroll
-        for (int k = 0; k < kStages; ++k) {
-            const uint4 q = *reinterpret_cast<const uint4*>(cbs + __byte_perm(w, lb[k], 0x7604 | (k << 4)));
-            add_f16x2_f32(acc[0], acc[1], q.x);
-            add_f16x2_f32(acc[2], acc[3], q.y);
-            add_f16x2_f32(acc[4], acc[5], q.z);
-            add_f16x2_f32(acc[6], acc[7], q.w);
-        }
-    } else {
-        for (int k = 0; k < kStages; ++k) {
-            const int64_t row = (int64_t)(k * kCodes + ((w >> (8 * k)) & 0xffu)) * 8;
-#pragma unroll
-            for (int t = 0; t < 8; ++t) acc[t] = __fadd_rn(acc[t], load_as_f32(J.cb, row + t, J.cb_kind));
-        }
-    }
-    uint4 r;
-    r.x = pack2(__fmul_rn(acc[0], s), __fmul_rn(acc[1], s), RVQ_BF16);
-    r.y = pack2(__fmul_rn(acc[2], s), __fmul_rn(acc[3], s), RVQ_BF16);
-    r.z = pack2(__fmul_rn(acc[4], s), __fmul_rn(acc[5], s), RVQ_BF16);
-    r.w = pack2(__fmul_rn(acc[6], s), __fmul_rn(acc[7], s), RVQ_BF16);
-    return r;
-}
 
 // sum over t of w[t] * x[t] in fp32, t = 0..7 in order (bf16 x bf16 products are exact)
 __device__ __forceinline__ float dot8_bf16(const uint4& w, const uint32_t (&xh)[4]) {
@@ -653,7 +590,7 @@ __device__ __forceinline__ void exact_rows(const TJob& J, const char* cbs, int t
                     s = load_as_f32(J.scales, fastdiv((uint32_t)r * (uint32_t)J.G + g_global, J.gvdiv),
                                     J.scale_kind);
             }
-            v[i] = dot8_bf16(exact_weights<SMEM>(cbs, J, wc[i], lb, s), xh);
+            v[i] = dot8_bf16(vdec::weights_bf16<SMEM>(cbs, J.cb, J.cb_kind, wc[i], lb, s), xh);
         }
         const float tot = reduce8(v);
         const int r = r0 + b * exact::kBatchRows + orow;
@@ -668,9 +605,7 @@ __global__ void __launch_bounds__(exact::kThreads, 1) rvq_gemv_exact_kernel(cons
     float* xs = staged + exact::kMaxStagedTiles * kTileCols;     // the tile's operand slice
     const int tid = threadIdx.x, lane = tid & 31;
     uint32_t lb[4];
-#pragma unroll
-    for (int k = 0; k < kStages; ++k)
-        lb[k] = ((uint32_t)(k & 1) << 7) | ((uint32_t)(lane & 7) << 4) | ((uint32_t)(k >> 1) << 16);
+    vdec::lane_bits(lane, lb);
     pdl_launch_dependents();
     const int u_first = p.cta_first[blockIdx.x], u_last = p.cta_first[blockIdx.x + 1];
     int cb_job = -1;
@@ -685,7 +620,7 @@ __global__ void __launch_bounds__(exact::kThreads, 1) rvq_gemv_exact_kernel(cons
         if (u != u_first) __syncthreads();                       // the previous unit is done with shared memory
         if (ji != cb_job) {
             cb_job = ji;
-            cb_smem = stage_cb_exact(J, cbs);
+            cb_smem = vdec::stage_cb8(J.cb, J.cb_kind, cbs, tid, exact::kThreads);
         }
         if (u == u_first) pdl_wait();                            // the operand comes from the previous kernel
         const bool has_gate = J.gate.ptr != nullptr;

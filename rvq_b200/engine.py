@@ -95,13 +95,14 @@ class LayerDecodePlan:
     """Everything one layer-slot fill needs, resolved once.
 
     ``items``: ``(key, entry)`` pairs of one layer; ``outs[key]``: the slot
-    tensor each entry decodes into.  ``launch(stream)`` queues the whole
+    tensor each entry decodes into; ``max_ctas``: CTA budget of the launch (0:
+    one CTA per SM; fewer leaves SMs to the kernels of the layer being computed).  ``launch(stream)`` queues the whole
     layer as ceil(jobs / 32) launches (one for a Qwen3 layer: 11 jobs).
     The tensors referenced by the plan must outlive it.
     """
 
     def __init__(self, items: Sequence[Tuple[str, Dict[str, object]]],
-                 codebooks: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor]):
+                 codebooks: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor], max_ctas: int = 0):
         self.keys: List[str] = []
         entries: List[_native.RvqEntry] = []
         int8s: List[_native.RvqInt8Entry] = []
@@ -158,6 +159,7 @@ class LayerDecodePlan:
             carr = (_native.RvqCopy * max(len(cs), 1))(*[_native.RvqCopy(*c) for c in cs])
             self.batches.append((earr, len(es), qarr, len(qs), carr, len(cs)))
         self._lib = _native.load()
+        self.max_ctas = int(max_ctas)
 
     @property
     def launches(self) -> int:
@@ -168,6 +170,6 @@ class LayerDecodePlan:
             stream = torch.cuda.current_stream().cuda_stream
         s = ctypes.c_void_p(stream)
         for earr, ne, qarr, nq, carr, nc in self.batches:
-            rc = self._lib.rvq_decode_layer_mixed(earr, ne, qarr, nq, carr, nc, s)
+            rc = self._lib.rvq_decode_layer_ctas(earr, ne, qarr, nq, carr, nc, self.max_ctas, s)
             if rc:
-                _native.check(rc, "rvq_decode_layer_mixed")
+                _native.check(rc, "rvq_decode_layer_ctas")
