@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true",
                     help="skip the batch-1 generation ms/token leg")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="skip the config-1 ping-pong overlap leg")
     return ap.parse_args()
 
 
@@ -418,6 +420,28 @@ def time_e2e(rel, cbs_host, device, steps, warmup, stream):
     return start.elapsed_time(end), h2d, d2h, launches * steps
 
 
+def overlap_leg(device):
+    """Config 1's ping-pong overlap: the next layer decoded into the other slot
+    on a low-priority side stream while the batch-1 bf16 block forward runs on
+    the main stream, overlap = (t_dec + t_fwd - t_both) / min(t_dec, t_fwd).
+    Reported with the decode on every SM (fastest alone) and with a CTA budget
+    of half the SMs (the other half free for the forward's kernels)."""
+    from rvq_b200 import bench_overlap
+    try:
+        half = torch.cuda.get_device_properties(device).multi_processor_count // 2
+        res = {"all_sms": bench_overlap.run(30, device, max_ctas=0),
+               "half_sms": bench_overlap.run(30, device, max_ctas=half)}
+        for r in res.values():
+            r.pop("workload", None)
+            r.pop("timing", None)
+        best = max(res, key=lambda k: res[k]["overlap"])
+        return {"overlap": res[best]["overlap"], "config": best, **res,
+                "definition": "(t_dec + t_fwd - t_both) / min(t_dec, t_fwd), us per layer, CUDA graphs on two "
+                              "streams (forward high priority), config-1 block, bf16 forward on resident weights"}
+    except Exception as exc:                     # reported in the line; the decode figures stand
+        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+
 def batch1_leg(world, device, peak):
     """Batch-1 greedy generation, ms/token (the metric's second half).  N=1:
     the 36-layer 2560/9728 model in every weight mode (dense bf16, slot
@@ -500,6 +524,10 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baselines(args.cpu_seconds)
 
+    overlap = None
+    if rank == 0 and world == 1 and not args.no_overlap:
+        overlap = overlap_leg(device)
+
     batch1 = None
     if not args.no_batch1:
         batch1 = batch1_leg(world, device, peak)
@@ -524,6 +552,7 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
+        "overlap": overlap,
         "batch1": batch1,
     }
     print(json.dumps(line), flush=True)

@@ -447,6 +447,17 @@ int rvq_take_wait_timeout(void);
  * the current device.  Returns 1 if the flag was set, 0 if not, or -RVQ_ERR_CUDA. */
 int rvq_take_index_error(void);
 
+/* ---- Artifact pack loader ---------------------------------------------------
+ * Replaces the artifact load of infer_compressed_layerwise_triton.py:421-432
+ * (torch.load of the compressor's pickle, compress_full_model.py:624-631, then
+ * one host-to-device copy per tensor) for an artifact rewritten once as a pack
+ * (rvq_b200/pack.py: a JSON header, then every tensor's bytes at page-aligned
+ * offsets).  Copies `nbytes` bytes of the file at `path`, starting at byte
+ * `offset`, to device memory `device_dst`: a reader thread fills a ring of
+ * pinned buffers with pread() while the copies run on `stream`.  Returns once
+ * the bytes are on the device (it waits for its own copies only). */
+int rvq_pack_load(const char* path, uint64_t offset, uint64_t nbytes, void* device_dst, void* stream);
+
 /* Last CUDA error code seen by this library on the calling thread (0 = none). */
 int rvq_last_cuda_error(void);
 

@@ -98,6 +98,10 @@ struct LayerParams {
 
 __device__ unsigned int g_index_error;
 
+// The kernels' dynamic shared memory (the staged codebook), named at namespace
+// scope so the fast path's loads are shared-memory loads by construction.
+extern __shared__ uint4 g_dyn_smem[];
+
 // ---------------------------------------------------------------------------
 // Device pieces
 // ---------------------------------------------------------------------------
@@ -211,8 +215,8 @@ __device__ int stage_codebook(const Job& job, uint4* smem) {
 // loads the next tile's index words while it decodes the current one.
 // SCALE4: group_vecs is a multiple of 4, so a lane's 4 vectors share a scale.
 template <bool OUT_BF16, bool SCALE4>
-__device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane,
-                                         const char* smem) {
+__device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane) {
+    const char* smem = reinterpret_cast<const char*>(g_dyn_smem);
     // the few job fields the loop needs, read once from parameter space
     const uint32_t* idx32 = reinterpret_cast<const uint32_t*>(job.idx);
     const uint32_t plane32 = job.stage_stride >> 2;
@@ -384,14 +388,14 @@ __device__ __forceinline__ void process_int8(const Job& job, uint32_t a, uint32_
     for (uint32_t t = a + warp; t < e; t += kWarps) int8_tile(job, t, lane);
 }
 
-// Fast-path variant a launch is compiled for (one inlined copy of the hot loop
-// per kernel keeps it free of register spills): 0 none, 1 bf16 output with
-// group_vecs % 4 == 0, 2 bf16, 3 fp16 with group_vecs % 4 == 0, 4 fp16.
-constexpr int kFastVariants = 5;
+// Fast-path variant FV a launch is compiled for (one inlined copy of the hot
+// loop per kernel): 0 none, 1 bf16 output with group_vecs % 4 == 0, 2 bf16,
+// 3 fp16 with group_vecs % 4 == 0, 4 fp16.  GEN: the generic tile path is
+// compiled in.
 
 // Decode tiles [a, e) (job-local) of one RVQ job; `owner` copies the tail.
 // All threads of the CTA call it.
-template <int FV>
+template <int FV, bool GEN>
 __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t e, bool owner, int warp,
                                             int lane, uint4* smem, bool& staged_once) {
     if (job.nvec == 0) {                    // tail-only entry: nothing to stage
@@ -406,16 +410,17 @@ __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t
     if (FV != 0 && mode == GATHER_SMEM_F16 && job.fast_ok) {      // the host matched job and variant
         const uint32_t fe = min(e, job.full_tiles);
         if (a < fe) {
-            run_fast<FV == 1 || FV == 2, FV == 1 || FV == 3>(job, a, fe, warp, lane, reinterpret_cast<const char*>(smem));
+            run_fast<FV == 1 || FV == 2, FV == 1 || FV == 3>(job, a, fe, warp, lane);
             g = fe;
         }
     }
-    for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t, lane, smem, mode);
+    if (GEN)                               // the host leaves GEN off only when no tile needs it
+        for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t, lane, smem, mode);
 }
 
-template <int FV>
+template <int FV, bool GEN>
 __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_constant__ LayerParams p) {
-    extern __shared__ uint4 smem[];
+    uint4* smem = g_dyn_smem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t G = gridDim.x, b = blockIdx.x;
     bool staged_once = false;
@@ -432,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
             const uint32_t r = b - job.cta_begin, cc = job.cta_count, tc = job.tile_count;
             const uint32_t a = (uint32_t)(((uint64_t)tc * r) / cc), e = (uint32_t)(((uint64_t)tc * (r + 1)) / cc);
             if (job.kind == JOB_INT8) process_int8(job, a, e, r == 0, warp, lane);
-            else process_rvq<FV>(job, a, e, r == 0, warp, lane, smem, staged_once);
+            else process_rvq<FV, GEN>(job, a, e, r == 0, warp, lane, smem, staged_once);
         }
         return;
     }
@@ -452,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
             process_int8(job, a - jb, e - jb, a == jb, warp, lane);
             continue;
         }
-        process_rvq<FV>(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
+        process_rvq<FV, GEN>(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
     }
 }
 
@@ -470,18 +475,26 @@ struct DeviceInfo {
 static DeviceInfo g_devices[kMaxDevices];
 
 using LayerKernel = void (*)(LayerParams);
-static LayerKernel layer_kernel(int fv) {
-    switch (fv) {
-        case 1: return rvq_layer_kernel<1>;
-        case 2: return rvq_layer_kernel<2>;
-        case 3: return rvq_layer_kernel<3>;
-        case 4: return rvq_layer_kernel<4>;
-        default: return rvq_layer_kernel<0>;
+// v = 0..8: variant 0 (generic), variants 1..4 with the generic path (v = 1..4)
+// and without it (v = 5..8, every RVQ tile on the fast path).
+static LayerKernel layer_kernel(int v) {
+    switch (v) {
+        case 1: return rvq_layer_kernel<1, true>;
+        case 2: return rvq_layer_kernel<2, true>;
+        case 3: return rvq_layer_kernel<3, true>;
+        case 4: return rvq_layer_kernel<4, true>;
+        case 5: return rvq_layer_kernel<1, false>;
+        case 6: return rvq_layer_kernel<2, false>;
+        case 7: return rvq_layer_kernel<3, false>;
+        case 8: return rvq_layer_kernel<4, false>;
+        default: return rvq_layer_kernel<0, true>;
     }
 }
+constexpr int kKernelVariants = 9;
 
-// The fast-path variant of a launch: that of its first fast job; fast jobs of
-// another variant lose the fast path (and its staging layout) in this launch.
+// The kernel of a launch: the fast-path variant of its first fast job (fast
+// jobs of another variant lose the fast path, and its staging layout, in this
+// launch), without the generic path when every RVQ tile is a full fast tile.
 static int choose_variant(LayerParams& p) {
     int fv = 0;
     for (int i = 0; i < p.njobs; ++i) {
@@ -491,7 +504,12 @@ static int choose_variant(LayerParams& p) {
         if (fv == 0) fv = v;
         if (v != fv) j.fast_ok = 0;
     }
-    return fv;
+    if (fv == 0) return 0;
+    for (int i = 0; i < p.njobs; ++i) {
+        const Job& j = p.jobs[i];
+        if (j.kind == JOB_RVQ && j.nvec > 0 && (!j.fast_ok || j.full_tiles < j.tile_count)) return fv;
+    }
+    return fv + 4;
 }
 static std::mutex g_dev_mutex;
 
@@ -518,7 +536,7 @@ static int device_info(DeviceInfo** out) {
         } else {
             di.sm_count = prop.multiProcessorCount;
             di.max_smem = (int)prop.sharedMemPerBlockOptin;
-            for (int v = 0; v < kFastVariants && e == cudaSuccess; ++v) {
+            for (int v = 0; v < kKernelVariants && e == cudaSuccess; ++v) {
                 cudaFuncAttributes fa;
                 e = cudaFuncGetAttributes(&fa, layer_kernel(v));
                 // dynamic shared memory may use what the kernel's static shared memory leaves

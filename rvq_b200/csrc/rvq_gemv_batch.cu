@@ -108,8 +108,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = p.stages;
     const int s_first = p.seg_first[blockIdx.x], s_last = p.seg_first[blockIdx.x + 1];
-    const uint32_t tmem_cols = p.npad * 2 <= 32 ? 32u : (p.npad * 2 <= 64 ? 64u : (p.npad * 2 <= 128 ? 128u
-                                                       : (p.npad * 2 <= 256 ? 256u : 512u)));
+    // two accumulators of npad columns; the epilogue reads 32 columns at a time
+    const int tmem_need = p.npad + (p.npad > 32 ? p.npad : 32);
+    const uint32_t tmem_cols = tmem_need <= 32 ? 32u : (tmem_need <= 64 ? 64u : (tmem_need <= 128 ? 128u
+                                                       : (tmem_need <= 256 ? 256u : 512u)));
 
     if (tid == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
@@ -207,11 +209,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
                                  idesc, kc > kc0 || ks > 0);
                     mma_commit(bar_done + 8 * st);
                     if (kc + 1 == kc1) mma_commit(bar_accf + 8 * acc);
-                    // x of chunk g + S - 1 goes to chunk g - 1's stage once its MMAs are done
-                    if (g >= 1) {
+                    // x of chunk g + S - 1 goes to stage (g + S - 1) % S: still unused when
+                    // g = 0, else chunk g - 1's, once its MMAs are done
+                    if (g >= 1)
                         mbar_wait(bar_done + 8 * ((g - 1) % S), ((g - 1) / S) & 1, kWaitLimit, &g_batch_timeout);
-                        load_x(g + S - 1);
-                    }
+                    load_x(g + S - 1);
                 }
             }
         }

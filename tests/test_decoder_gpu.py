@@ -159,10 +159,13 @@ def test_native_step_tracks_torch_step(mode, cuda_device):
         assert rel(a, b) < tol, (i, rel(a, b))
 
 
-def bf16_ulp(v: float) -> float:
-    """Spacing of bf16 numbers at |v| (8 significant bits)."""
-    import math
-    return 2.0 ** (math.floor(math.log2(abs(v))) - 7) if v else 2.0 ** -133
+def explained_flip(ours, ref, want: int, got: int) -> bool:
+    """A greedy choice that differs from the reference's is only acceptable
+    when the reference's own margin between the two tokens is no larger than
+    this decoder's measured logit deviation on exactly those two tokens."""
+    gap = float(ref[want] - ref[got])
+    dev = float((ours[want] - ref[want]).abs() + (ours[got] - ref[got]).abs())
+    return gap <= dev
 
 
 def test_greedy_ids_identical_to_engine_strict(cuda_device):
@@ -171,30 +174,31 @@ def test_greedy_ids_identical_to_engine_strict(cuda_device):
     slots, bit-identical to the oracle engine pinned to the reference
     engine's own output).
 
-    The logits are bf16 in both, and greedy takes the first maximum, so when
-    the reference's top two logits are within one bf16 ulp of each other
-    (a tie at its own output precision) the choice depends on the last
-    rounding of that logit, which no other kernel sequence reproduces.
-    Everywhere else the ids must be identical: teacher-forced on the
-    reference's tokens, every step's argmax of the dense, slot and
-    exact-weight fused decoders must equal the reference's id unless that
-    step is such a tie, and free-running generation must reproduce the
-    reference's ids up to the first tie (all 32 when there is none)."""
+    Teacher-forced on the reference's tokens, every one of the 32 steps is
+    checked (not only up to the first divergence): the dense, slot and
+    exact-weight fused decoders must pick the reference's id at each step,
+    except where the reference's margin between its pick and ours is within
+    our measured deviation of those two logits (both are bf16 logits computed
+    with other fp32 summation orders, so a near-tie at the last bits cannot be
+    reproduced); at most one such step in 32.  Free-running generation must
+    reproduce the reference's ids up to the first such step (all 32 when there
+    is none)."""
     vocab, layers, new = 32768, 8, 32
     art = synthetic.make_tp_shard_artifact(QW, layers, vocab, 0, 1, seed=40, device=cuda_device)
     cfg = synthetic.qwen3_config(QW, layers, vocab)
     prompt = torch.randint(0, vocab, (32,), generator=torch.Generator().manual_seed(41)).to(cuda_device)
     ref_ids, ref_logits = engine_run(art, cfg, prompt, new, cuda_device)
-    ties = {i for i in range(new)
-            if margin(ref_logits[i]) <= bf16_ulp(float(ref_logits[i].max()))}
-    assert len(ties) <= new // 8, sorted(ties)
     for mode in ("dense", "slot", "fused_exact"):
         dec = Qwen3Decoder(cfg, art, cuda_device, mode=mode, max_len=96, artifact_is_shard=True)
         forced = teacher_forced(dec, prompt, ref_ids)
+        flips = []
         for i in range(new):
-            if i not in ties:
-                assert int(forced[i].argmax()) == int(ref_ids[i]), (mode, i, margin(ref_logits[i]))
+            want, got = int(ref_ids[i]), int(forced[i].argmax())
+            if got != want:
+                assert explained_flip(forced[i], ref_logits[i], want, got), (mode, i, margin(ref_logits[i]))
+                flips.append(i)
+        assert len(flips) <= 1, (mode, flips)
         ids = dec.generate(prompt, new)
         first = next((i for i in range(new) if int(ids[i]) != int(ref_ids[i])), None)
-        assert first is None or first in ties, (mode, first, margin(ref_logits[first]))
+        assert first is None or first in flips, (mode, first, flips)
         dec.close()
