@@ -98,10 +98,6 @@ struct LayerParams {
 
 __device__ unsigned int g_index_error;
 
-// The kernels' dynamic shared memory (the staged codebook), named at namespace
-// scope so the fast path's loads are shared-memory loads by construction.
-extern __shared__ uint4 g_dyn_smem[];
-
 // ---------------------------------------------------------------------------
 // Device pieces
 // ---------------------------------------------------------------------------
@@ -215,8 +211,8 @@ __device__ int stage_codebook(const Job& job, uint4* smem) {
 // loads the next tile's index words while it decodes the current one.
 // SCALE4: group_vecs is a multiple of 4, so a lane's 4 vectors share a scale.
 template <bool OUT_BF16, bool SCALE4>
-__device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane) {
-    const char* smem = reinterpret_cast<const char*>(g_dyn_smem);
+__device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane,
+                                         const char* smem) {
     // the few job fields the loop needs, read once from parameter space
     const uint32_t* idx32 = reinterpret_cast<const uint32_t*>(job.idx);
     const uint32_t plane32 = job.stage_stride >> 2;
@@ -388,14 +384,8 @@ __device__ __forceinline__ void process_int8(const Job& job, uint32_t a, uint32_
     for (uint32_t t = a + warp; t < e; t += kWarps) int8_tile(job, t, lane);
 }
 
-// Fast-path variant FV a launch is compiled for (one inlined copy of the hot
-// loop per kernel): 0 none, 1 bf16 output with group_vecs % 4 == 0, 2 bf16,
-// 3 fp16 with group_vecs % 4 == 0, 4 fp16.  GEN: the generic tile path is
-// compiled in.
-
 // Decode tiles [a, e) (job-local) of one RVQ job; `owner` copies the tail.
 // All threads of the CTA call it.
-template <int FV, bool GEN>
 __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t e, bool owner, int warp,
                                             int lane, uint4* smem, bool& staged_once) {
     if (job.nvec == 0) {                    // tail-only entry: nothing to stage
@@ -407,20 +397,26 @@ __device__ __forceinline__ void process_rvq(const Job& job, uint32_t a, uint32_t
     const int mode = stage_codebook(job, smem);
     if (owner) copy_tail(job);
     uint32_t g = a;                         // first tile left for the generic path
-    if (FV != 0 && mode == GATHER_SMEM_F16 && job.fast_ok) {      // the host matched job and variant
+    if (mode == GATHER_SMEM_F16 && job.fast_ok) {
         const uint32_t fe = min(e, job.full_tiles);
         if (a < fe) {
-            run_fast<FV == 1 || FV == 2, FV == 1 || FV == 3>(job, a, fe, warp, lane);
+            const char* cs = reinterpret_cast<const char*>(smem);
+            const bool s4 = (job.gv.d & 3u) == 0;
+            if (job.out_kind == RVQ_BF16) {
+                if (s4) run_fast<true, true>(job, a, fe, warp, lane, cs);
+                else run_fast<true, false>(job, a, fe, warp, lane, cs);
+            } else {
+                if (s4) run_fast<false, true>(job, a, fe, warp, lane, cs);
+                else run_fast<false, false>(job, a, fe, warp, lane, cs);
+            }
             g = fe;
         }
     }
-    if (GEN)                               // the host leaves GEN off only when no tile needs it
-        for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t, lane, smem, mode);
+    for (uint32_t t = g + warp; t < e; t += kWarps) tile_generic(job, t, lane, smem, mode);
 }
 
-template <int FV, bool GEN>
 __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_constant__ LayerParams p) {
-    uint4* smem = g_dyn_smem;
+    extern __shared__ uint4 smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t G = gridDim.x, b = blockIdx.x;
     bool staged_once = false;
@@ -437,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
             const uint32_t r = b - job.cta_begin, cc = job.cta_count, tc = job.tile_count;
             const uint32_t a = (uint32_t)(((uint64_t)tc * r) / cc), e = (uint32_t)(((uint64_t)tc * (r + 1)) / cc);
             if (job.kind == JOB_INT8) process_int8(job, a, e, r == 0, warp, lane);
-            else process_rvq<FV, GEN>(job, a, e, r == 0, warp, lane, smem, staged_once);
+            else process_rvq(job, a, e, r == 0, warp, lane, smem, staged_once);
         }
         return;
     }
@@ -457,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
             process_int8(job, a - jb, e - jb, a == jb, warp, lane);
             continue;
         }
-        process_rvq<FV, GEN>(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
+        process_rvq(job, a - jb, e - jb, a == jb, warp, lane, smem, staged_once);
     }
 }
 
@@ -473,44 +469,6 @@ struct DeviceInfo {
 };
 
 static DeviceInfo g_devices[kMaxDevices];
-
-using LayerKernel = void (*)(LayerParams);
-// v = 0..8: variant 0 (generic), variants 1..4 with the generic path (v = 1..4)
-// and without it (v = 5..8, every RVQ tile on the fast path).
-static LayerKernel layer_kernel(int v) {
-    switch (v) {
-        case 1: return rvq_layer_kernel<1, true>;
-        case 2: return rvq_layer_kernel<2, true>;
-        case 3: return rvq_layer_kernel<3, true>;
-        case 4: return rvq_layer_kernel<4, true>;
-        case 5: return rvq_layer_kernel<1, false>;
-        case 6: return rvq_layer_kernel<2, false>;
-        case 7: return rvq_layer_kernel<3, false>;
-        case 8: return rvq_layer_kernel<4, false>;
-        default: return rvq_layer_kernel<0, true>;
-    }
-}
-constexpr int kKernelVariants = 9;
-
-// The kernel of a launch: the fast-path variant of its first fast job (fast
-// jobs of another variant lose the fast path, and its staging layout, in this
-// launch), without the generic path when every RVQ tile is a full fast tile.
-static int choose_variant(LayerParams& p) {
-    int fv = 0;
-    for (int i = 0; i < p.njobs; ++i) {
-        Job& j = p.jobs[i];
-        if (j.kind != JOB_RVQ || !j.fast_ok) continue;
-        const int v = (j.out_kind == RVQ_BF16 ? 1 : 3) + ((j.gv.d & 3u) == 0 ? 0 : 1);
-        if (fv == 0) fv = v;
-        if (v != fv) j.fast_ok = 0;
-    }
-    if (fv == 0) return 0;
-    for (int i = 0; i < p.njobs; ++i) {
-        const Job& j = p.jobs[i];
-        if (j.kind == JOB_RVQ && j.nvec > 0 && (!j.fast_ok || j.full_tiles < j.tile_count)) return fv;
-    }
-    return fv + 4;
-}
 static std::mutex g_dev_mutex;
 
 static int cuda_fail(cudaError_t e) {
@@ -535,16 +493,13 @@ static int device_info(DeviceInfo** out) {
             di.ok = false;
         } else {
             di.sm_count = prop.multiProcessorCount;
-            di.max_smem = (int)prop.sharedMemPerBlockOptin;
-            for (int v = 0; v < kKernelVariants && e == cudaSuccess; ++v) {
-                cudaFuncAttributes fa;
-                e = cudaFuncGetAttributes(&fa, layer_kernel(v));
-                // dynamic shared memory may use what the kernel's static shared memory leaves
-                const int avail = (int)prop.sharedMemPerBlockOptin - (int)fa.sharedSizeBytes;
-                if (e == cudaSuccess) e = cudaFuncSetAttribute(layer_kernel(v), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                             avail);
-                if (avail < di.max_smem) di.max_smem = avail;
-            }
+            cudaFuncAttributes fa;
+            e = cudaFuncGetAttributes(&fa, rvq_layer_kernel);
+            // dynamic shared memory may use what the kernel's static shared memory leaves
+            di.max_smem = (int)prop.sharedMemPerBlockOptin - (e == cudaSuccess ? (int)fa.sharedSizeBytes : 0);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(rvq_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         di.max_smem);
             di.ok = (e == cudaSuccess);
             if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
         }
@@ -737,8 +692,7 @@ static int launch_jobs(LayerParams& p, size_t smem_need, int max_ctas, void* str
         grid = ctas;
         if (grid > total) grid = total;
     }
-    const int fv = choose_variant(p);
-    layer_kernel(fv)<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
+    rvq_layer_kernel<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return RVQ_OK;

@@ -5,10 +5,11 @@
 // .to(device) per tensor) becomes a single streamed host-to-device copy into
 // one device buffer, with no unpickling and no per-tensor transfers.
 //
-// The data region is read with pread() by a reader thread into a ring of
+// The data region is read with pread() by four reader threads into a ring of
 // pinned host buffers while the calling thread issues one cudaMemcpyAsync per
-// filled buffer on the caller's stream; a CUDA event per buffer tells the
-// reader when it may refill it.  File reads and DMA overlap.
+// filled buffer, in file order, on the caller's stream; a CUDA event per
+// buffer tells its reader when it may refill it.  File reads (page-cache
+// copies or disk) run in parallel and overlap the DMA.
 
 #include <cuda_runtime.h>
 #include <errno.h>
@@ -29,14 +30,16 @@
 namespace rvq {
 namespace pack {
 
-constexpr size_t kBufBytes = 32u << 20;      // one pinned staging buffer
-constexpr int kBufs = 3;
+constexpr size_t kBufBytes = 16u << 20;      // one pinned staging buffer
+constexpr int kReaders = 4;                  // pread threads
+constexpr int kBufs = 2 * kReaders;          // ring: each reader owns buffers r and r + kReaders
 
 struct Ring {
     std::mutex mu;
     std::condition_variable cv;
-    size_t filled[kBufs] = {0, 0, 0};        // bytes ready in buffer i (0: empty)
-    bool ready[kBufs] = {false, false, false};
+    int64_t holds[kBufs];                    // chunk whose bytes buffer b holds (-1: none)
+    int64_t copied = -1;                     // highest chunk whose copy has been issued
+    size_t len[kBufs];
     bool failed = false;
     int err = 0;
 };
@@ -50,9 +53,11 @@ int load(const char* path, uint64_t offset, uint64_t nbytes, void* dst, cudaStre
         return RVQ_ERR_INVALID;
     }
     posix_fadvise(fd, (off_t)offset, (off_t)nbytes, POSIX_FADV_SEQUENTIAL);
-    void* host[kBufs] = {nullptr, nullptr, nullptr};
-    cudaEvent_t done[kBufs] = {nullptr, nullptr, nullptr};
+    void* host[kBufs] = {};
+    cudaEvent_t done[kBufs] = {};
     int rc = RVQ_OK;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) rc = RVQ_ERR_UNAVAILABLE;
     for (int i = 0; i < kBufs && rc == RVQ_OK; ++i) {
         cudaError_t e = cudaHostAlloc(&host[i], kBufBytes, cudaHostAllocDefault);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming);
@@ -63,74 +68,81 @@ int load(const char* path, uint64_t offset, uint64_t nbytes, void* dst, cudaStre
     }
     if (rc == RVQ_OK && nbytes > 0) {
         Ring ring;
-        const uint64_t nchunks = (nbytes + kBufBytes - 1) / kBufBytes;
-        // reader: chunk c goes to buffer c % kBufs once the copy of chunk c - kBufs is done
-        std::thread reader([&]() {
-            for (uint64_t c = 0; c < nchunks; ++c) {
-                const int b = (int)(c % kBufs);
-                {
-                    std::unique_lock<std::mutex> lk(ring.mu);
-                    ring.cv.wait(lk, [&] { return !ring.ready[b] || ring.failed; });
-                    if (ring.failed) return;
-                }
-                if (c >= (uint64_t)kBufs) {
-                    const cudaError_t e = cudaEventSynchronize(done[b]);
-                    if (e != cudaSuccess) {
-                        std::lock_guard<std::mutex> lk(ring.mu);
-                        ring.failed = true;
-                        ring.err = RVQ_ERR_CUDA;
-                        last_cuda_error_slot() = (int)e;
-                        ring.cv.notify_all();
-                        return;
+        for (int b = 0; b < kBufs; ++b) ring.holds[b] = -1;
+        const int64_t nchunks = (int64_t)((nbytes + kBufBytes - 1) / kBufBytes);
+        auto fail = [&](int code) {
+            std::lock_guard<std::mutex> lk(ring.mu);
+            ring.failed = true;
+            ring.err = code;
+            ring.cv.notify_all();
+        };
+        // reader r reads chunks r, r + kReaders, ...; chunk c goes to buffer c % kBufs once
+        // the copy of chunk c - kBufs (the buffer's previous content) has been issued and finished
+        std::vector<std::thread> readers;
+        for (int r = 0; r < kReaders; ++r) {
+            readers.emplace_back([&, r]() {
+                cudaSetDevice(device);               // the events belong to the caller's device
+                for (int64_t c = r; c < nchunks; c += kReaders) {
+                    const int b = (int)(c % kBufs);
+                    {
+                        std::unique_lock<std::mutex> lk(ring.mu);
+                        ring.cv.wait(lk, [&] { return ring.failed || ring.copied >= c - kBufs; });
+                        if (ring.failed) return;
                     }
-                }
-                const uint64_t begin = c * kBufBytes;
-                const size_t len = (size_t)((nbytes - begin) < kBufBytes ? (nbytes - begin) : kBufBytes);
-                size_t got = 0;
-                while (got < len) {
-                    const ssize_t r = pread(fd, (char*)host[b] + got, len - got, (off_t)(offset + begin + got));
-                    if (r < 0 && errno == EINTR) continue;
-                    if (r <= 0) {
-                        std::lock_guard<std::mutex> lk(ring.mu);
-                        ring.failed = true;
-                        ring.err = RVQ_ERR_INVALID;
-                        ring.cv.notify_all();
-                        return;
+                    if (c >= kBufs) {
+                        const cudaError_t e = cudaEventSynchronize(done[b]);
+                        if (e != cudaSuccess) {
+                            last_cuda_error_slot() = (int)e;
+                            fail(RVQ_ERR_CUDA);
+                            return;
+                        }
                     }
-                    got += (size_t)r;
+                    const uint64_t begin = (uint64_t)c * kBufBytes;
+                    const size_t len = (size_t)((nbytes - begin) < kBufBytes ? (nbytes - begin) : kBufBytes);
+                    size_t got = 0;
+                    while (got < len) {
+                        const ssize_t n = pread(fd, (char*)host[b] + got, len - got, (off_t)(offset + begin + got));
+                        if (n < 0 && errno == EINTR) continue;
+                        if (n <= 0) {
+                            fail(RVQ_ERR_INVALID);
+                            return;
+                        }
+                        got += (size_t)n;
+                    }
+                    std::lock_guard<std::mutex> lk(ring.mu);
+                    ring.len[b] = len;
+                    ring.holds[b] = c;
+                    ring.cv.notify_all();
                 }
-                std::lock_guard<std::mutex> lk(ring.mu);
-                ring.filled[b] = len;
-                ring.ready[b] = true;
-                ring.cv.notify_all();
-            }
-        });
-        for (uint64_t c = 0; c < nchunks; ++c) {
+            });
+        }
+        // copies in chunk order, each as soon as its buffer is filled
+        for (int64_t c = 0; c < nchunks; ++c) {
             const int b = (int)(c % kBufs);
             size_t len = 0;
             {
                 std::unique_lock<std::mutex> lk(ring.mu);
-                ring.cv.wait(lk, [&] { return ring.ready[b] || ring.failed; });
+                ring.cv.wait(lk, [&] { return ring.failed || ring.holds[b] == c; });
                 if (ring.failed) {
                     rc = ring.err;
                     break;
                 }
-                len = ring.filled[b];
+                len = ring.len[b];
             }
-            cudaError_t e = cudaMemcpyAsync((char*)dst + c * kBufBytes, host[b], len, cudaMemcpyHostToDevice, stream);
+            cudaError_t e = cudaMemcpyAsync((char*)dst + (uint64_t)c * kBufBytes, host[b], len,
+                                            cudaMemcpyHostToDevice, stream);
             if (e == cudaSuccess) e = cudaEventRecord(done[b], stream);
-            std::lock_guard<std::mutex> lk(ring.mu);
             if (e != cudaSuccess) {
                 last_cuda_error_slot() = (int)e;
                 rc = RVQ_ERR_CUDA;
-                ring.failed = true;
-                ring.cv.notify_all();
+                fail(RVQ_ERR_CUDA);
                 break;
             }
-            ring.ready[b] = false;            // the reader refills it after done[b]
+            std::lock_guard<std::mutex> lk(ring.mu);
+            ring.copied = c;
             ring.cv.notify_all();
         }
-        reader.join();
+        for (auto& t : readers) t.join();
         if (rc == RVQ_OK && ring.failed) rc = ring.err;
     }
     // the pinned buffers are freed only after their copies have finished

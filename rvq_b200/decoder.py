@@ -345,6 +345,13 @@ class Qwen3Decoder:
         self.h = torch.zeros(d.hidden, dtype=dt, device=dev)
         self.x_final = torch.zeros(d.hidden, dtype=dt, device=dev)
         self.logits_buf = torch.zeros(d.vocab, dtype=dt, device=dev)
+        # tensor parallel: each rank computes the logits of its vocab slice of
+        # the (replicated) head, then one all-gather inside the step
+        self.head_sharded = self.tp > 1 and d.vocab % self.tp == 0
+        if self.head_sharded:
+            rank, part = dist.get_rank(self.tp_group), d.vocab // self.tp
+            self.lm_head_local = self.lm_head[rank * part:(rank + 1) * part]
+            self.logits_local = torch.zeros(part, dtype=dt, device=dev)
         self.step_ops = []
         fused = self.fused
         exact = self.mode == "fused_exact"
@@ -461,7 +468,11 @@ class Qwen3Decoder:
             elif not fused:
                 self._allreduce(self.down)
         self.final_op.launch()
-        self._mv(self.lm_head, self.x_final, self.logits_buf)
+        if self.head_sharded:
+            self._mv(self.lm_head_local, self.x_final, self.logits_local)
+            dist.all_gather_into_tensor(self.logits_buf, self.logits_local, group=self.tp_group)
+        else:
+            self._mv(self.lm_head, self.x_final, self.logits_buf)
         return self.logits_buf
 
     # -- prefill (eager) and graph-replayed decode steps -------------------------------

@@ -4,8 +4,10 @@ Both run the same full model: the TP ranks shard it (rvq_b200/shard.py) and
 sum the row-parallel outputs inside the captured step, either by peer stores
 into landing buffers (``tp_reduce="push"``, rvq_b200/tp.py) or by an NCCL
 all-reduce.  The sums are re-associated across ranks, so logits agree within
-a tolerance and greedy ids agree wherever the single-GPU margin is above that
-noise; both ranks always produce the same ids.  The 2-rank tests are skipped
+a tolerance, and greedy ids agree except at a near-tie that the measured
+logit deviations on the two competing tokens explain; both ranks always
+produce the same ids.  The vocab head is sharded over the ranks (one
+all-gather of the logits per step).  The 2-rank tests are skipped
 with fewer than 2 devices; the bounded landing wait is tested on one.
 """
 
@@ -71,9 +73,13 @@ def test_two_rank_decoder_matches_single_gpu(mode, reduce):
         worst = max(worst, float((a - b).abs().max()))
         assert float((a - b).norm() / b.norm()) < 2e-2
     for i in range(ref_ids.numel()):
-        if int(ids0[i]) != int(ref_ids[i]):
-            top = torch.topk(ref_logits[i], 2).values
-            assert float(top[0] - top[1]) < 4 * worst, i
+        want, got = int(ref_ids[i]), int(ids0[i])
+        if got != want:
+            # only a near-tie that the two runs' own logit deviations on these
+            # two tokens explain may flip (the prefixes are equal up to here)
+            gap = float(ref_logits[i][want] - ref_logits[i][got])
+            dev = float((logits0[i][want] - ref_logits[i][want]).abs() + (logits0[i][got] - ref_logits[i][got]).abs())
+            assert gap <= dev, (i, gap, dev)
             break
 
 
