@@ -376,14 +376,16 @@ int rvq_gemv_tiles_exact(const rvq_gemv_tile_job* jobs, int n_jobs, void* stream
 int64_t rvq_tile_codes_bytes(int64_t rows, int64_t cols);
 int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64_t cols, void* out, void* stream);
 
-/* Small-batch fused dequant-GEMM on the tensor cores (no counterpart in the
- * reference, which reconstructs W into the slot and calls F.linear:
- * infer_compressed_layerwise_triton.py:290-292):
- *   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < tokens (1..256)
+/* Fused dequant-GEMM on the tensor cores for small batches and prompts (no
+ * counterpart in the reference, which reconstructs W into the slot and calls
+ * F.linear: infer_compressed_layerwise_triton.py:263, 290-292):
+ *   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < tokens (1..65536)
  * W is rebuilt bit-identically to rvq_decode's bf16 slot values straight into
- * shared memory as the A operand of tcgen05.mma (M = 128 weight rows, N =
- * tokens rounded up to 16, fp32 accumulation in TMEM); only the codes, scales
- * and x are read from HBM.  W: K=4 stages, 256 codes, uint8 codes in the
+ * shared memory as the A operand of tcgen05.mma (M = 128 weight rows, N = a
+ * block of up to 256 tokens, fp32 accumulation in TMEM); only the codes,
+ * scales and x are read from HBM.  More than 256 tokens run as blocks of 256,
+ * each weight chunk decoded once per block.  A job whose split needs more
+ * than the kernel's segment table returns RVQ_ERR_TOO_LARGE.  W: K=4 stages, 256 codes, uint8 codes in the
  * tile-major layout of rvq_tile_codes (weight.indices, 16-byte aligned), no
  * tail; codebook fp32, fp16 or bf16.  x bf16 [tokens][cols] row-major, 16-byte
  * aligned, cols a multiple of 8; y bf16 [tokens][rows].  Deterministic: split-K

@@ -7,7 +7,10 @@ and the replay timed with CUDA events, so host launch cost is excluded --
 with weights rotated over 16 resident copies (no copy's codes stay in L2
 between uses):
 
-* ``fused``:  rvq_gemv (batch 1), W never materialised;
+* ``fused``:  rvq_gemv / rvq_gemv_tiles (batch 1, table GEMV) and
+  rvq_gemv_tiles_exact (bit-exact bf16 weights), W never materialised;
+* ``fused_tc``: rvq_gemv_batch, W decoded bit-exactly into shared memory as
+  the tcgen05 MMA operand (every batch size, and the 2048-token prefill);
 * ``decode+gemm``: rvq_decode_layer into a bf16 slot, then torch.matmul
   (cuBLAS) -- the reference's dataflow (infer_compressed_layerwise_triton.py:
   263, 290-292);
@@ -25,7 +28,7 @@ import torch
 
 from . import synthetic
 from .engine import LayerDecodePlan
-from .gemm import GemmPlan
+from .gemm import BatchGemvPlan, GemmPlan
 from .gemv import GemvPlan, GemvTilesPlan, interleave_codes, tile_codes, tiles_count
 
 ROWS, COLS = 9728, 2560
@@ -87,6 +90,10 @@ def run(reps: int = 200, device="cuda:0"):
     t = _time(lambda i: tplans[i % COPIES].launch(), reps, stream)
     out["results"]["fused_tiles_b1"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
                                         "algorithmic_bytes": algo, "output": "fp32 partials [10, rows]"}
+    eplans = [GemvTilesPlan([(c, cbd, x1, p)], exact=True) for c, p in zip(tl, parts)]
+    t = _time(lambda i: eplans[i % COPIES].launch(), reps, stream)
+    out["results"]["fused_exact_tiles_b1"] = {"us": round(t, 2), "GB/s": round(algo / t / 1e3, 1),
+                                              "output": "fp32 partials, bit-exact bf16 weights"}
     y1 = torch.empty(ROWS, dtype=torch.float32, device=device)
 
     def tiles_sum(i):
@@ -119,6 +126,14 @@ def run(reps: int = 200, device="cuda:0"):
             torch.matmul(x, dense[i % COPIES].t(), out=y)
 
         r = reps if b < 2048 else max(20, reps // 10)
+        # the tensor-core fused GEMM (W decoded into shared memory, never to HBM)
+        y_fb = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)
+        bplans = [BatchGemvPlan(c, cbd, x, y_fb) for c in tl]
+        t_fb = _time(lambda i: bplans[i % COPIES].launch(), r, stream)
+        flops = 2.0 * b * ROWS * COLS
+        out["results"][f"fused_tc_b{b}"] = {"us": round(t_fb, 2), "TFLOP/s": round(flops / t_fb / 1e6, 2),
+                                            "GB/s": round((code_bytes + b * (COLS + ROWS) * 2) / t_fb / 1e3, 1)}
+        del bplans
         if b >= 64:
             # prefill-style: weight decoded into shared memory feeding tcgen05 MMAs
             y_fg = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)

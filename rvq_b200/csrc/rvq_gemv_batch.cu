@@ -1,6 +1,6 @@
-// Small-batch fused dequant-GEMM on the tensor cores (sm_100a):
+// Fused dequant-GEMM on the tensor cores for small batches and prompts (sm_100a):
 //
-//   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < T tokens (1..256), W an RVQ entry
+//   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < T tokens, W an RVQ entry
 //
 // The reference materialises W into the slot and calls F.linear
 // (infer_compressed_layerwise_triton.py:290-292).  Here W never reaches HBM:
@@ -10,17 +10,19 @@
 // (rvq_vecdecode.cuh) straight into shared memory in the K-major
 // 128-byte-swizzled layout (one RVQ vector = one 16-byte swizzle chunk), the
 // issuer warp loads x[0:T][chunk] by TMA (rows past T read as zero) and issues
-// four tcgen05.mma (kind::f16, M = 128 weight rows, N = T rounded up to 16,
-// K = 16), accumulating in TMEM.  Four epilogue warps read each finished
-// segment with tcgen05.ld; two accumulators alternate, so the next segment's
-// MMAs run while the previous one is read out.
+// four tcgen05.mma (kind::f16, M = 128 weight rows, N = a block of up to 256
+// tokens, K = 16), accumulating in TMEM.  Four epilogue warps read each
+// finished segment with tcgen05.ld; two accumulators alternate, so the next
+// segment's MMAs run while the previous one is read out.  A prompt of T > 256
+// tokens runs as token blocks of 256: each weight chunk is decoded once per
+// block and feeds 128 x 256 x 64 MACs.
 //
-// Work split: the (row tile, chunk) units in row-tile order are cut into one
-// contiguous range per SM, so every CTA decodes the same number of chunks.  A
-// tile cut into several pieces writes fp32 partial sums to the workspace; the
-// CTA that finishes a tile's last piece (ticket counter) adds the pieces in
-// piece order and writes y, so results do not depend on timing.  Tiles held
-// by one CTA write y directly.
+// Work split: the (row tile, token block, chunk) units in that order are cut
+// into one contiguous range per SM, so every CTA decodes the same number of
+// chunks.  A (tile, block) cut into several pieces writes fp32 partial sums
+// to the workspace; the CTA that finishes its last piece (ticket counter)
+// adds the pieces in piece order and writes y, so results do not depend on
+// timing.  Units held by one CTA write y directly.
 //
 // Only the codes (0.5 B per weight), the scales and x are read from HBM.
 
@@ -49,19 +51,21 @@ constexpr int kChunk = 64;                                   // columns per chun
 constexpr int kChunkVecs = kChunk / 8;
 constexpr int kWStageBytes = kTileRows * kChunk * 2;         // 16 KB
 constexpr int kMaxStages = 4;
-constexpr int kMaxTokens = 256;
+constexpr int kBlockTokens = 256;                          // MMA N per token block (max)
+constexpr int kMaxTokens = 65536;
 constexpr int kMaxCtas = 160;
-constexpr int kMaxSegs = 512;
-constexpr int kMaxSegsPerCta = 8;
+constexpr int kMaxSegs = 1536;
+constexpr int kMaxSegsPerCta = 16;
 constexpr long long kWaitLimit = 1ll << 24;
 constexpr int kBudget = 226 * 1024;                          // dynamic shared memory limit used per CTA
 
 __device__ int g_batch_timeout;
 
 struct Seg {
-    uint32_t tile_piece;      // tile << 12 | piece << 6 | npieces
+    uint32_t unit;            // tile * blocks + token block
+    uint32_t piece_np;        // piece << 8 | npieces
     uint32_t chunks;          // kc0 << 16 | kc1
-    int32_t slot;             // first workspace slot of the tile's pieces (npieces > 1)
+    int32_t slot;             // first workspace slot of the unit's pieces (npieces > 1)
 };
 
 struct BParams {
@@ -70,18 +74,17 @@ struct BParams {
     const void* cb;
     const void* scales;
     __nv_bfloat16* y;         // [T][R]
-    float* part;              // workspace: [slots][T][128] fp32
-    uint32_t* tickets;        // workspace: [tiles]
-    int32_t R, G, T, npad, stages, n_ctas;
+    float* part;              // workspace: [slots][npad][128] fp32
+    uint32_t* tickets;        // workspace: [units]
+    int32_t R, G, T, npad, blocks, stages, n_ctas;
     int32_t cb_kind, scale_kind, row_scales;
     FastDiv gvdiv, rpsdiv;
     int32_t seg_first[kMaxCtas + 1];
     Seg segs[kMaxSegs];
 };
 
-__device__ __forceinline__ int seg_tile(const Seg& s) { return (int)(s.tile_piece >> 12); }
-__device__ __forceinline__ int seg_piece(const Seg& s) { return (int)((s.tile_piece >> 6) & 63u); }
-__device__ __forceinline__ int seg_np(const Seg& s) { return (int)(s.tile_piece & 63u); }
+__device__ __forceinline__ int seg_piece(const Seg& s) { return (int)(s.piece_np >> 8); }
+__device__ __forceinline__ int seg_np(const Seg& s) { return (int)(s.piece_np & 255u); }
 __device__ __forceinline__ int seg_kc0(const Seg& s) { return (int)(s.chunks >> 16); }
 __device__ __forceinline__ int seg_kc1(const Seg& s) { return (int)(s.chunks & 0xffffu); }
 
@@ -140,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         int g = 0;
         for (int si = s_first; si < s_last; ++si) {
             const Seg sg = p.segs[si];
-            const int tile = seg_tile(sg), kc1 = seg_kc1(sg);
+            const int tile = (int)sg.unit / p.blocks, kc1 = seg_kc1(sg);
             for (int kc = seg_kc0(sg); kc < kc1; ++kc, ++g) {
                 const int st = g % S;
                 if (g >= S) {                                      // the MMAs of chunk g - S left stage st
@@ -172,21 +175,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         // ---- issuer: x by TMA (S - 1 chunks ahead), MMAs once a chunk's weights are decoded
         if (lane == 0) {
             const uint32_t idesc = instr_desc_bf16(kTileRows, p.npad);
-            // chunk index g -> column chunk, walking the segments
-            auto chunk_of = [&](int g) -> int {
+            // x of the CTA's chunk number g: column chunk and token block, walking the segments
+            auto load_x = [&](int g) {
                 for (int si = s_first; si < s_last; ++si) {
-                    const int n = seg_kc1(p.segs[si]) - seg_kc0(p.segs[si]);
-                    if (g < n) return seg_kc0(p.segs[si]) + g;
+                    const Seg& sg = p.segs[si];
+                    const int n = seg_kc1(sg) - seg_kc0(sg);
+                    if (g < n) {
+                        const int st = g % S, kc = seg_kc0(sg) + g, blk = (int)sg.unit % p.blocks;
+                        mbar_expect_tx(bar_x + 8 * st, (uint32_t)xstage_bytes);
+                        tma_load_2d(smem_addr(xs + st * xstage_bytes), &p.xmap, kc * kChunk, blk * p.npad,
+                                    bar_x + 8 * st);
+                        return;
+                    }
                     g -= n;
                 }
-                return -1;
-            };
-            auto load_x = [&](int g) {
-                const int kc = chunk_of(g);
-                if (kc < 0) return;
-                const int st = g % S;
-                mbar_expect_tx(bar_x + 8 * st, (uint32_t)xstage_bytes);
-                tma_load_2d(smem_addr(xs + st * xstage_bytes), &p.xmap, kc * kChunk, 0, bar_x + 8 * st);
             };
             for (int g = 0; g < S - 1; ++g) load_x(g);
             int g = 0;
@@ -225,22 +227,24 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         for (int si = s_first; si < s_last; ++si) {
             const Seg sg = p.segs[si];
             const int acc = (si - s_first) & 1, n_seg = si - s_first;
-            const int tile = seg_tile(sg), np = seg_np(sg);
+            const int tile = (int)sg.unit / p.blocks, np = seg_np(sg);
+            const int t0 = ((int)sg.unit % p.blocks) * p.npad, nt = min(p.npad, p.T - t0);
             const int row = tile * kTileRows + r;
             if (lane == 0) mbar_wait(bar_accf + 8 * acc, (n_seg >> 1) & 1, kWaitLimit, &g_batch_timeout);
             __syncwarp();
             tc_fence_after();
-            float* part = p.part + ((int64_t)(sg.slot + seg_piece(sg)) * p.T) * kTileRows + r;
+            float* part = p.part + ((int64_t)(sg.slot + seg_piece(sg)) * p.npad) * kTileRows + r;
             for (int c0 = 0; c0 < p.npad; c0 += 32) {
                 uint32_t vals[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * e) << 16) + (uint32_t)(acc * p.npad + c0), vals);
                 tmem_ld_wait();
-                const int tn = min(32, p.T - c0);
+                const int tn = min(32, nt - c0);
                 if (np == 1) {
                     if (row < p.R) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
-                            if (i < tn) p.y[(int64_t)(c0 + i) * p.R + row] = __float2bfloat16_rn(__uint_as_float(vals[i]));
+                            if (i < tn)
+                                p.y[(int64_t)(t0 + c0 + i) * p.R + row] = __float2bfloat16_rn(__uint_as_float(vals[i]));
                     }
                 } else {
 #pragma unroll
@@ -255,19 +259,19 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
                 // the CTA that finishes the tile's last piece adds the pieces in piece order
                 __threadfence();
                 asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
-                if (e == 0 && lane == 0) last_piece = atomicAdd(&p.tickets[tile], 1u) == (uint32_t)(np - 1);
+                if (e == 0 && lane == 0) last_piece = atomicAdd(&p.tickets[sg.unit], 1u) == (uint32_t)(np - 1);
                 asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
                 if (last_piece) {
                     __threadfence();
-                    const float* base_p = p.part + ((int64_t)sg.slot * p.T) * kTileRows + r;
+                    const float* base_p = p.part + ((int64_t)sg.slot * p.npad) * kTileRows + r;
                     if (row < p.R) {
-                        for (int t = 0; t < p.T; ++t) {
+                        for (int t = 0; t < nt; ++t) {
                             float sum = __ldcg(base_p + (int64_t)t * kTileRows);
-                            for (int q = 1; q < np; ++q) sum += __ldcg(base_p + ((int64_t)q * p.T + t) * kTileRows);
-                            p.y[(int64_t)t * p.R + row] = __float2bfloat16_rn(sum);
+                            for (int q = 1; q < np; ++q) sum += __ldcg(base_p + ((int64_t)q * p.npad + t) * kTileRows);
+                            p.y[(int64_t)(t0 + t) * p.R + row] = __float2bfloat16_rn(sum);
                         }
                     }
-                    if (e == 0 && lane == 0) p.tickets[tile] = 0u;     // ready for the next launch
+                    if (e == 0 && lane == 0) p.tickets[sg.unit] = 0u;  // ready for the next launch
                 }
                 asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
             }
@@ -317,7 +321,7 @@ int prepare(int* sms) {
     return g_ok[dev] ? RVQ_OK : RVQ_ERR_UNAVAILABLE;
 }
 
-int npad_of(int64_t T) { return (int)((T + 15) / 16 * 16); }
+int npad_of(int64_t T) { return T >= kBlockTokens ? kBlockTokens : (int)((T + 15) / 16 * 16); }
 
 int stages_for(int npad) {
     const int per = kWStageBytes + npad * 128;
@@ -326,59 +330,68 @@ int stages_for(int npad) {
 }
 
 // Segments of the balanced split.  Returns the workspace bytes it needs
-// (partials, then one ticket per tile) or a negative status.
+// (partials, then one ticket per (tile, token block) unit) or a negative status.
 int64_t plan(const rvq_gemv_batch_job& j, int sms, BParams* p) {
     const int64_t R = j.rows, G = j.cols / 8, T = j.tokens;
     const int64_t KC = (G + kChunkVecs - 1) / kChunkVecs;
     const int64_t NT = (R + kTileRows - 1) / kTileRows;
-    const int64_t U = NT * KC;
+    const int64_t npad = npad_of(T), NB = (T + npad - 1) / npad;
+    const int64_t NU = NT * NB;                                   // (tile, token block) units
+    const int64_t U = NU * KC;
+    if (NU >= (1ll << 31)) return -RVQ_ERR_TOO_LARGE;
     int64_t ctas = sms < kMaxCtas ? sms : kMaxCtas;
     if (ctas > U) ctas = U;
-    // pieces of every tile: the CTA ranges that overlap it
-    int nseg = 0, slots = 0;
-    std::vector<int> tile_np((size_t)NT, 0), tile_slot((size_t)NT, 0);
+    // pieces of every unit: the CTA ranges that overlap it
+    int nseg = 0;
+    int64_t slots = 0;
+    std::vector<int> unit_np((size_t)NU, 0);
+    std::vector<int64_t> unit_slot((size_t)NU, 0);
     for (int pass = 0; pass < 2; ++pass) {
         nseg = 0;
-        std::vector<int> piece((size_t)NT, 0);
+        std::vector<int> piece(pass ? (size_t)NU : 0, 0);
         for (int64_t c = 0; c < ctas; ++c) {
             const int64_t u0 = U * c / ctas, u1 = U * (c + 1) / ctas;
             if (p) p->seg_first[c] = nseg;
             int in_cta = 0;
             for (int64_t u = u0; u < u1;) {
-                const int64_t tile = u / KC, kc0 = u % KC;
-                const int64_t kc1 = (u1 - tile * KC) < KC ? (u1 - tile * KC) : KC;
+                const int64_t unit = u / KC, kc0 = u % KC;
+                const int64_t kc1 = (u1 - unit * KC) < KC ? (u1 - unit * KC) : KC;
                 if (pass == 0) {
-                    tile_np[(size_t)tile] += 1;
+                    unit_np[(size_t)unit] += 1;
                 } else {
                     if (nseg >= kMaxSegs || ++in_cta > kMaxSegsPerCta) return -RVQ_ERR_TOO_LARGE;
                     Seg& s = p->segs[nseg];
-                    const int np = tile_np[(size_t)tile];
-                    s.tile_piece = ((uint32_t)tile << 12) | ((uint32_t)piece[(size_t)tile] << 6) | (uint32_t)np;
+                    const int np = unit_np[(size_t)unit];
+                    s.unit = (uint32_t)unit;
+                    s.piece_np = ((uint32_t)piece[(size_t)unit] << 8) | (uint32_t)np;
                     s.chunks = ((uint32_t)kc0 << 16) | (uint32_t)kc1;
-                    s.slot = np > 1 ? tile_slot[(size_t)tile] : 0;
-                    piece[(size_t)tile] += 1;
+                    s.slot = np > 1 ? (int32_t)unit_slot[(size_t)unit] : 0;
+                    piece[(size_t)unit] += 1;
                 }
                 ++nseg;
-                u = tile * KC + kc1;
+                u = unit * KC + kc1;
             }
         }
         if (pass == 0) {
-            for (int64_t t = 0; t < NT; ++t) {
-                if (tile_np[(size_t)t] > 63) return -RVQ_ERR_TOO_LARGE;
-                if (tile_np[(size_t)t] > 1) {
-                    tile_slot[(size_t)t] = slots;
-                    slots += tile_np[(size_t)t];
+            for (int64_t t = 0; t < NU; ++t) {
+                if (unit_np[(size_t)t] > 255) return -RVQ_ERR_TOO_LARGE;
+                if (unit_np[(size_t)t] > 1) {
+                    unit_slot[(size_t)t] = slots;
+                    slots += unit_np[(size_t)t];
                 }
             }
+            if (slots >= (1ll << 31)) return -RVQ_ERR_TOO_LARGE;
             if (!p) break;
         }
     }
     if (p) {
         p->seg_first[ctas] = nseg;
         p->n_ctas = (int32_t)ctas;
+        p->npad = (int32_t)npad;
+        p->blocks = (int32_t)NB;
     }
-    const int64_t part_bytes = ((int64_t)slots * T * kTileRows * 4 + 255) / 256 * 256;
-    return part_bytes + NT * 4;
+    const int64_t part_bytes = (slots * npad * kTileRows * 4 + 255) / 256 * 256;
+    return part_bytes + NU * 4;
 }
 
 int check_job(const rvq_gemv_batch_job* j) {
@@ -426,7 +439,6 @@ int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t worksp
     if (need < 0) return (int)-need;
     if (workspace == nullptr || workspace_bytes < (size_t)need || ((uintptr_t)workspace & 255)) return RVQ_ERR_INVALID;
     const rvq_entry& w = job->weight;
-    p.npad = npad_of(job->tokens);
     p.stages = stages_for(p.npad);
     const cuuint64_t dims[2] = {(cuuint64_t)job->cols, (cuuint64_t)job->tokens};
     const cuuint64_t strides[1] = {(cuuint64_t)job->cols * 2};
@@ -436,13 +448,13 @@ int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t worksp
                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return RVQ_ERR_INVALID;
-    const int64_t NT = (job->rows + kTileRows - 1) / kTileRows;
+    const int64_t NU = (job->rows + kTileRows - 1) / kTileRows * p.blocks;
     p.codes = reinterpret_cast<const uint32_t*>(w.indices);
     p.cb = w.codebook;
     p.scales = w.scales;
     p.y = reinterpret_cast<__nv_bfloat16*>(job->y);
     p.part = reinterpret_cast<float*>(workspace);
-    p.tickets = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(workspace) + (size_t)need - (size_t)NT * 4);
+    p.tickets = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(workspace) + (size_t)need - (size_t)NU * 4);
     p.R = (int32_t)job->rows;
     p.G = (int32_t)(job->cols / 8);
     p.T = (int32_t)job->tokens;

@@ -88,7 +88,7 @@ def rvq_matmul(x: torch.Tensor, entry: Dict[str, object], codebook: torch.Tensor
 
 
 # ---------------------------------------------------------------------------
-# Small batch (1..256 tokens): rvq_gemv_batch, weight-stationary tcgen05
+# Small batches and prompts: rvq_gemv_batch, weight-stationary tcgen05
 # ---------------------------------------------------------------------------
 
 class RvqGemvBatchJob(ctypes.Structure):
@@ -124,8 +124,8 @@ def take_batch_timeout() -> bool:
 
 
 class BatchGemvPlan:
-    """``y = x @ W^T`` for ``tokens`` (1..256) bf16 rows of x with W decoded on
-    chip into the tensor cores' operand (``rvq_gemv_batch``); fixed pointers,
+    """``y = x @ W^T`` for ``tokens`` bf16 rows of x (any number; blocks of 256)
+    with W decoded on chip into the tensor cores' operand (``rvq_gemv_batch``); fixed pointers,
     so a launch can be captured in a CUDA graph.  ``entry["codes_tiled"]``
     (from ``gemv.tile_codes``) is required.  The workspace (split-K partials
     and zeroed tickets) is allocated here once."""
@@ -169,7 +169,7 @@ class BatchGemvPlan:
 
 def rvq_linear_batch(x: torch.Tensor, entry: Dict[str, object], codebook: torch.Tensor,
                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``F.linear(x, W)`` for 1..256 rows of bf16 x, W decoded on chip."""
+    """``F.linear(x, W)`` for rows of bf16 x, W decoded on chip."""
     rows = int(entry["shape"][0])
     x2 = x.reshape(-1, x.shape[-1]).contiguous()
     if out is None:

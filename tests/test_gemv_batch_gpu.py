@@ -1,4 +1,4 @@
-"""GPU: rvq_gemv_batch (small-batch fused GEMM on tcgen05) against the oracle.
+"""GPU: rvq_gemv_batch (fused GEMM on tcgen05, batches and prompts) against the oracle.
 
 The kernel multiplies x by the bit-exact bf16 slot weights (the oracle's
 reconstruction rounded to nearest even) with fp32 accumulation in TMEM, then
@@ -45,6 +45,8 @@ def rel(got, want):
     (8, 8, 1, 8, torch.float32),               # one vector
     (3000, 1000, 17, 40, torch.float32),       # 5 vectors per scale
     (200, 512, 256, None, torch.float32),      # 256 tokens: two stages, 512 TMEM columns
+    (1000, 1024, 300, None, torch.float32),    # 300 tokens: a full and a partial token block
+    (9728, 2560, 2048, None, torch.float16),   # a 2048-token prompt on the gate projection
     (2048, 2560, 8, None, "f32_not_f16"),      # codebook fp16 cannot hold: global fp32 reads
 ])
 def test_batch_matches_bf16_reconstruction(rows, cols, tokens, group, cb_dtype, cuda_device):
@@ -62,12 +64,16 @@ def test_batch_matches_bf16_reconstruction(rows, cols, tokens, group, cb_dtype, 
     plan.launch()
     torch.cuda.synchronize()
     w = oracle_w_bf16(entry, cb)
-    want = x.double().numpy() @ w.T
     got = y.float().cpu().numpy()
     assert not np.isnan(got).any()
+    wd = torch.from_numpy(w).to(cuda_device)
+    if tokens <= 256:
+        want = x.double().numpy() @ w.T
+    else:                                       # large: the fp64 product on the GPU
+        want = (x.to(cuda_device).double() @ wd.t()).cpu().numpy()
     assert rel(got, want) <= TOL
     # the reference's reconstruct + F.linear on the same weights (config 3: 1e-2)
-    lin = F.linear(x.to(cuda_device), torch.from_numpy(w).to(torch.bfloat16).to(cuda_device)).float().cpu().numpy()
+    lin = F.linear(x.to(cuda_device), wd.to(torch.bfloat16)).float().cpu().numpy()
     assert rel(got, lin) <= 1e-2
     # deterministic across launches (tickets reset, pieces added in a fixed order)
     first = y.clone()
