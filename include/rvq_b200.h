@@ -449,6 +449,27 @@ int rvq_take_wait_timeout(void);
  * the current device.  Returns 1 if the flag was set, 0 if not, or -RVQ_ERR_CUDA. */
 int rvq_take_index_error(void);
 
+/* ---- Encoder (the offline compressor's hot loops on the GPU) -----------------
+ * Replace assign_codes / kmeans_train / encode_rvq_tensor's stage loop
+ * (compress_full_model.py:196-234, 337-366), which the reference runs on the
+ * CPU.  Distances are pairwise_sqdist's (|x|^2 + |c|^2) - 2 x.c in fp32; the
+ * argmin keeps the first minimum, as torch.argmin does.  Only d = 8. */
+
+/* codes[k][i] = nearest codeword of stage k to residual_k(i), residual_0 = x,
+ * residual_{k+1} = residual_k - codebooks[k][codes[k][i]] (fp32).  x: device
+ * fp32 [n][8], 16-byte aligned; codebooks: device fp32 [stages][ncodes][8]
+ * (ncodes <= 4096); codes: device [stages][n] of code_kind (RVQ_U8 when
+ * ncodes <= 256, or RVQ_I16); residual_out: device fp32 [n][8] or NULL. */
+int rvq_encode_vectors(const float* x, int64_t n, const float* codebooks, int stages, int ncodes, int d, void* codes,
+                       int code_kind, float* residual_out, void* stream);
+
+/* One Lloyd step's statistics: assign[i] = nearest centroid (or assign NULL),
+ * and when `sums` is set, sums[c][t] += round(x[i][t] * 2^32) and counts[c]
+ * += 1 in 64-bit integer atomics (order-independent: the same input always
+ * gives the same sums).  sums [k][8] and counts [k] must be zeroed before. */
+int rvq_kmeans_step(const float* x, int64_t n, const float* centroids, int k, int d, int32_t* assign,
+                    unsigned long long* sums, unsigned long long* counts, void* stream);
+
 /* ---- Artifact pack loader ---------------------------------------------------
  * Replaces the artifact load of infer_compressed_layerwise_triton.py:421-432
  * (torch.load of the compressor's pickle, compress_full_model.py:624-631, then

@@ -67,10 +67,10 @@ class GoldenCase:
 
 
 def case_names() -> List[str]:
-    """RVQ decode fixtures (engine fixtures are named engine_*, int8 ones int8_*)."""
+    """RVQ decode fixtures (others: engine_*, int8_* and encoder_* files)."""
     return sorted(os.path.splitext(os.path.basename(p))[0]
                   for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith(("engine_", "int8_")))
+                  if not os.path.basename(p).startswith(("engine_", "int8_", "encoder_")))
 
 
 def int8_case_names() -> List[str]:
