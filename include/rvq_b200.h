@@ -48,7 +48,11 @@ enum rvq_kind {
     RVQ_BF16 = 1,
     RVQ_F32 = 2,
     RVQ_U8 = 3,
-    RVQ_I16 = 4
+    RVQ_I16 = 4,
+    /* uint8 codes of exactly 4 stages in the "quad" layout this library
+     * writes with rvq_quad_codes: 16 bytes per 4 consecutive vectors, byte
+     * 4 k + j = the stage-k code of vector 4 q + j.  Not an artifact layout. */
+    RVQ_U8X4 = 5
 };
 
 /* One RVQ entry to decode.  Replaces the arguments that
@@ -201,6 +205,14 @@ int rvq_gemv_noalloc(const rvq_gemv_job* jobs, int n_jobs, void* stream);
 
 /* Size of the fixed workspace rvq_gemv_noalloc uses. */
 size_t rvq_gemv_noalloc_max_workspace(void);
+
+/* Repack uint8 code planes [4][stage_stride] of `nvec` vectors into the quad
+ * layout (index_kind RVQ_U8X4): out holds rvq_quad_codes_bytes(nvec) bytes
+ * (whole 128-vector tiles), 16-byte aligned, zero past the last vector.  A decode thread then gets the 4 stage
+ * codes of its 4 vectors with one 16-byte load instead of 4 plane loads (the
+ * resident layout of layer plans; the artifact keeps its planes). */
+int rvq_quad_codes(const void* planes, int64_t stage_stride, int64_t nvec, void* out, void* stream);
+int64_t rvq_quad_codes_bytes(int64_t nvec);
 
 /* Repack uint8 code planes [4][stage_stride] into one 32-bit word per vector
  * ([nvec][4] bytes, stage k in byte k), the layout rvq_gemv reads with one

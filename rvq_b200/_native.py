@@ -21,7 +21,7 @@ RVQ_ERR_UNAVAILABLE = 3
 RVQ_ERR_CUDA = 4
 RVQ_ERR_TOO_LARGE = 5
 
-RVQ_F16, RVQ_BF16, RVQ_F32, RVQ_U8, RVQ_I16 = 0, 1, 2, 3, 4
+RVQ_F16, RVQ_BF16, RVQ_F32, RVQ_U8, RVQ_I16, RVQ_U8X4 = 0, 1, 2, 3, 4, 5
 RVQ_MAX_LAYER_JOBS = 32
 
 KIND_OF_DTYPE = {

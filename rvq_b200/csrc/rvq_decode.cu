@@ -73,7 +73,7 @@ struct Job {
     uint16_t stages;
     uint16_t ncodes;        // 0 encodes 65536 (never produced by int16 indices)
     uint8_t kind;
-    uint8_t index_bytes;
+    uint8_t index_bytes;    // 1, 2, or 4 for the quad layout (RVQ_U8X4)
     uint8_t cb_kind;
     uint8_t scale_kind;
     uint8_t tail_kind;
@@ -83,7 +83,7 @@ struct Job {
     uint8_t f32_fits;       // fp32 staging fits in shared memory
     uint8_t out_aligned;    // out is 16-byte aligned
     uint8_t fast_ok;        // eligible for the streaming fast path (see fill_rvq_job)
-    uint8_t pad;
+    uint8_t slot_ok;        // eligible for rvq_slot_kernel (see fill_rvq_job)
     uint32_t full_tiles;    // tiles whose 128 vectors are all complete (< full_vecs, < nvec)
     uint32_t cta_begin;     // job-per-CTA schedule: first CTA of this job
     uint32_t cta_count;     // job-per-CTA schedule: CTAs of this job (copies: owning CTA in cta_begin)
@@ -98,6 +98,9 @@ struct LayerParams {
 
 __device__ unsigned int g_index_error;
 
+// The kernels' dynamic shared memory (the staged codebook).
+extern __shared__ uint4 g_dyn_smem[];
+
 // ---------------------------------------------------------------------------
 // Device pieces
 // ---------------------------------------------------------------------------
@@ -105,7 +108,8 @@ __device__ unsigned int g_index_error;
 __device__ __forceinline__ uint32_t load_code(const Job& job, int k, uint32_t n, bool& bad) {
     uint32_t c;
     size_t off = (size_t)k * job.stage_stride + n;
-    if (job.index_bytes == 1) c = __ldg(reinterpret_cast<const uint8_t*>(job.idx) + off);
+    if (job.index_bytes == 4) c = __ldg(reinterpret_cast<const uint8_t*>(job.idx) + (size_t)(n >> 2) * 16 + k * 4 + (n & 3));
+    else if (job.index_bytes == 1) c = __ldg(reinterpret_cast<const uint8_t*>(job.idx) + off);
     else c = (uint16_t)__ldg(reinterpret_cast<const short*>(job.idx) + off);
     uint32_t nc = job.ncodes ? job.ncodes : 65536u;
     if (c >= nc) { bad = true; c = 0; }
@@ -225,16 +229,15 @@ __device__ __forceinline__ void run_fast(const Job& job, uint32_t ta, uint32_t t
         lb[k] = ((uint32_t)(k & 1) << 7) | ((uint32_t)(lane & 7) << 4) | ((uint32_t)(k >> 1) << 16);
     uint32_t t = ta + warp;
     uint32_t w[4];
-    if (t < tb) {
+    // this lane's 4 code words of tile u (one word per plane)
+    auto load_words = [&](uint32_t u, uint32_t (&o)[4]) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) w[k] = __ldg(idx32 + (size_t)k * plane32 + t * 32u + lane);
-    }
+        for (int k = 0; k < 4; ++k) o[k] = __ldg(idx32 + (size_t)k * plane32 + u * 32u + lane);
+    };
+    if (t < tb) load_words(t, w);
     for (; t < tb; t += kWarps) {
         uint32_t wn[4];
-        if (t + kWarps < tb) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) wn[k] = __ldg(idx32 + (size_t)k * plane32 + (t + kWarps) * 32u + lane);
-        }
+        if (t + kWarps < tb) load_words(t + kWarps, wn);
         const uint32_t n0 = t * kTileVecs + 4u * lane;
         float s4 = 0.f;
         if (SCALE4) s4 = __half2float(__ushort_as_half(__ldg(scales + fastdiv(n0, gv))));
@@ -458,6 +461,128 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_layer_kernel(const __grid_con
 }
 
 // ---------------------------------------------------------------------------
+// The slot kernel: a layer slot whose RVQ entries all have quad-layout codes,
+// an fp16 codebook, fp16 scales and whole vectors, decoded into bf16 -- what a
+// layer plan uploads, with a multiple of 4 vectors per scale -- plus its raw copies.  The same arithmetic and
+// schedule as the fast path of rvq_layer_kernel, in a kernel that holds
+// nothing else, so the hot loop keeps every value in registers.  Lane L owns
+// vectors 4L .. 4L + 3 of a 128-vector tile and gets their 16 stage codes
+// with one 16-byte load; the last tile of an entry may be partial (the quad
+// buffer is zero-padded; stores and scale reads past nvec are skipped).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void slot_stage(const Job& job, char* smem) {
+    const int lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < 4 * 256; e += blockDim.x) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(job.cb) + e);
+        char* base = smem + ((e >> 9) << 16) + ((e & 255) << 8) + (((e >> 8) & 1) << 7);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(base + (((i + lane) & 7) << 4)) = q;
+    }
+}
+
+__device__ __forceinline__ void slot_tiles(const Job& job, uint32_t ta, uint32_t tb, int warp, int lane) {
+    const char* smem = reinterpret_cast<const char*>(g_dyn_smem);
+    const uint4* quads = reinterpret_cast<const uint4*>(job.idx);
+    uint4* out = reinterpret_cast<uint4*>(job.out);
+    const unsigned short* scales = reinterpret_cast<const unsigned short*>(job.scales);
+    const FastDiv gv = job.gv;
+    const uint32_t nvec = job.nvec;
+    uint32_t lb[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        lb[k] = ((uint32_t)(k & 1) << 7) | ((uint32_t)(lane & 7) << 4) | ((uint32_t)(k >> 1) << 16);
+    uint32_t t = ta + warp;
+    uint4 w;
+    if (t < tb) w = __ldg(quads + t * 32u + lane);
+    for (; t < tb; t += kWarps) {
+        uint4 wn;
+        if (t + kWarps < tb) wn = __ldg(quads + (t + kWarps) * 32u + lane);
+        const uint32_t n0 = t * kTileVecs + 4u * lane;
+        const bool whole = n0 + 4u <= nvec;
+        // group_vecs is a multiple of 4: the lane's 4 vectors share one scale
+        const float s = n0 < nvec ? __half2float(__ushort_as_half(__ldg(scales + fastdiv(n0, gv)))) : 0.f;
+        const uint32_t wk[4] = {w.x, w.y, w.z, w.w};
+        uint4 prev;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint4 q = *reinterpret_cast<const uint4*>(smem + __byte_perm(wk[k], lb[k], 0x7604 | (i << 4)));
+                add_f16x2_f32(acc[0], acc[1], q.x);
+                add_f16x2_f32(acc[2], acc[3], q.y);
+                add_f16x2_f32(acc[4], acc[5], q.z);
+                add_f16x2_f32(acc[6], acc[7], q.w);
+            }
+            mul2_f32(acc[0], acc[1], s);
+            mul2_f32(acc[2], acc[3], s);
+            mul2_f32(acc[4], acc[5], s);
+            mul2_f32(acc[6], acc[7], s);
+            uint4 q;
+            q.x = pack2(acc[0], acc[1], RVQ_BF16);
+            q.y = pack2(acc[2], acc[3], RVQ_BF16);
+            q.z = pack2(acc[4], acc[5], RVQ_BF16);
+            q.w = pack2(acc[6], acc[7], RVQ_BF16);
+            if (i & 1) {
+                if (whole) store_v8_na(out + n0 + i - 1, prev, q);
+                else {                                  // the partial last tile of the entry
+                    if (n0 + i - 1 < nvec) out[n0 + i - 1] = prev;
+                    if (n0 + i < nvec) out[n0 + i] = q;
+                }
+            } else {
+                prev = q;
+            }
+        }
+        w = wn;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) rvq_slot_kernel(const __grid_constant__ LayerParams p) {
+    char* smem = reinterpret_cast<char*>(g_dyn_smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t b = blockIdx.x;
+    // raw copies first (each owned by one CTA), then this CTA's share of its RVQ job
+    for (int j = 0; j < p.njobs; ++j) {
+        const Job& job = p.jobs[j];
+        if (job.kind == JOB_COPY && job.cta_begin == b)
+            for (uint32_t t = warp; t < job.tile_count; t += kWarps) copy_tile(job, t, lane);
+    }
+    for (int j = 0; j < p.njobs; ++j) {
+        const Job& job = p.jobs[j];
+        if (job.kind != JOB_RVQ || b < job.cta_begin || b >= job.cta_begin + job.cta_count) continue;
+        const uint32_t r = b - job.cta_begin, cc = job.cta_count, tc = job.tile_count;
+        const uint32_t a = (uint32_t)(((uint64_t)tc * r) / cc), e = (uint32_t)(((uint64_t)tc * (r + 1)) / cc);
+        slot_stage(job, smem);
+        __syncthreads();
+        if (r == 0) copy_tail(job);
+        slot_tiles(job, a, e, warp, lane);
+        return;                                  // the job-per-CTA schedule gives a CTA one RVQ job
+    }
+}
+
+// Quad layout: out[q] = the 4 stage words of vectors 4q .. 4q + 3 (byte 4 k + j
+// = stage k's code of vector 4 q + j), zero past nvec up to a whole 128-vector
+// tile (32 quads), so tile loads never leave the buffer.  One thread per quad.
+__global__ void quad_codes_kernel(const uint8_t* __restrict__ planes, int64_t stride, int64_t nvec,
+                                  uint4* __restrict__ out) {
+    const int64_t quads = (nvec + kTileVecs - 1) / kTileVecs * (kTileVecs / 4);
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < quads; q += (int64_t)gridDim.x * blockDim.x) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int64_t n = 4 * q + j;
+                if (n < nvec) v |= (uint32_t)planes[k * stride + n] << (8 * j);
+            }
+            w[k] = v;
+        }
+        out[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -500,6 +625,9 @@ static int device_info(DeviceInfo** out) {
             if (e == cudaSuccess)
                 e = cudaFuncSetAttribute(rvq_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          di.max_smem);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(rvq_slot_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         di.max_smem);
             di.ok = (e == cudaSuccess);
             if (e != cudaSuccess) last_cuda_error_slot() = (int)e;
         }
@@ -515,7 +643,9 @@ static int check_entry(const rvq_entry* e) {
     if (!e) return RVQ_ERR_INVALID;
     if (e->d != 8) return RVQ_ERR_UNSUPPORTED;
     if (!is_float_kind(e->out_kind)) return RVQ_ERR_UNSUPPORTED;
-    if (e->index_kind != RVQ_U8 && e->index_kind != RVQ_I16) return RVQ_ERR_UNSUPPORTED;
+    if (e->index_kind != RVQ_U8 && e->index_kind != RVQ_I16 && e->index_kind != RVQ_U8X4) return RVQ_ERR_UNSUPPORTED;
+    if (e->index_kind == RVQ_U8X4 && (e->stages != 4 || e->ncodes > 256 || ((uintptr_t)e->indices & 15)))
+        return RVQ_ERR_INVALID;
     if (e->codebook_kind != RVQ_F16 && e->codebook_kind != RVQ_F32) return RVQ_ERR_UNSUPPORTED;
     if (!is_float_kind(e->scale_kind) || !is_float_kind(e->tail_kind)) return RVQ_ERR_UNSUPPORTED;
     if (e->stages < 1 || e->stages > 65535 || e->ncodes < 1 || e->ncodes > 65536) return RVQ_ERR_INVALID;
@@ -587,7 +717,7 @@ static int fill_rvq_job(const rvq_entry* e, Job& j, size_t& smem_need) {
     j.tail_numel = (uint32_t)e->tail_numel;
     j.stages = (uint16_t)e->stages;
     j.ncodes = (uint16_t)(e->ncodes == 65536 ? 0 : e->ncodes);
-    j.index_bytes = (uint8_t)(e->index_kind == RVQ_U8 ? 1 : 2);
+    j.index_bytes = (uint8_t)(e->index_kind == RVQ_U8 ? 1 : (e->index_kind == RVQ_U8X4 ? 4 : 2));
     j.cb_kind = (uint8_t)e->codebook_kind;
     j.scale_kind = (uint8_t)e->scale_kind;
     j.tail_kind = (uint8_t)e->tail_kind;
@@ -608,10 +738,15 @@ static int fill_rvq_job(const rvq_entry* e, Job& j, size_t& smem_need) {
     j.tile_count = tiles;
     const uint64_t complete = (uint64_t)(e->nvec < (int64_t)j.full_vecs ? e->nvec : j.full_vecs);
     j.full_tiles = (uint32_t)(complete / kTileVecs);
-    j.fast_ok = e->index_kind == RVQ_U8 && e->ncodes == 256 && e->stages == 4 && cl == 3 &&
-                (e->out_kind == RVQ_BF16 || e->out_kind == RVQ_F16) && ((uintptr_t)e->out & 31) == 0 &&
-                e->scale_kind == RVQ_F16 &&
-                ((uintptr_t)e->indices & 3) == 0 && (e->stage_stride & 3) == 0;
+    const bool planes_ok = e->index_kind == RVQ_U8 && ((uintptr_t)e->indices & 3) == 0 && (e->stage_stride & 3) == 0 &&
+                           (e->out_kind == RVQ_BF16 || e->out_kind == RVQ_F16);
+    j.fast_ok = planes_ok && e->ncodes == 256 && e->stages == 4 && cl == 3 && ((uintptr_t)e->out & 31) == 0 &&
+                e->scale_kind == RVQ_F16;
+    // the slot kernel: quad codes, fp16 codebook (staged exactly), bf16 slot, whole vectors,
+    // 4 | group_vecs
+    j.slot_ok = e->index_kind == RVQ_U8X4 && e->ncodes == 256 && e->codebook_kind == RVQ_F16 &&
+                e->out_kind == RVQ_BF16 && e->scale_kind == RVQ_F16 && ((uintptr_t)e->out & 31) == 0 &&
+                e->trimmed == e->nvec * 8 && e->nvec > 0 && e->group_vecs % 4 == 0;
     return RVQ_OK;
 }
 
@@ -688,11 +823,15 @@ static int launch_jobs(LayerParams& p, size_t smem_need, int max_ctas, void* str
     if (smem_need > (size_t)di->max_smem) return RVQ_ERR_TOO_LARGE;
     uint32_t grid = plan_per_cta(p, ctas);
     p.per_cta_jobs = grid ? 1u : 0u;
+    bool slot = grid != 0;
+    for (int i = 0; i < p.njobs && slot; ++i)
+        if (p.jobs[i].kind == JOB_INT8 || (p.jobs[i].kind == JOB_RVQ && !p.jobs[i].slot_ok)) slot = false;
     if (!grid) {
         grid = ctas;
         if (grid > total) grid = total;
     }
-    rvq_layer_kernel<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
+    if (slot) rvq_slot_kernel<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
+    else rvq_layer_kernel<<<grid, kThreads, smem_need, (cudaStream_t)stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return RVQ_OK;
@@ -766,6 +905,20 @@ int rvq_decode_layer_ctas(const rvq_entry* entries, int n_entries, const rvq_int
         j.tile_count = (uint32_t)((c.nbytes + kCopyTileBytes - 1) / kCopyTileBytes);
     }
     return launch_jobs(p, smem, max_ctas, stream);
+}
+
+int64_t rvq_quad_codes_bytes(int64_t nvec) { return nvec < 1 ? 0 : (nvec + kTileVecs - 1) / kTileVecs * kTileVecs * 4; }
+
+int rvq_quad_codes(const void* planes, int64_t stage_stride, int64_t nvec, void* out, void* stream) {
+    if (!planes || !out || nvec < 1 || stage_stride < nvec || ((uintptr_t)out & 15)) return RVQ_ERR_INVALID;
+    const int64_t quads = (nvec + kTileVecs - 1) / kTileVecs * (kTileVecs / 4);
+    const int64_t blocks64 = (quads + 255) / 256;
+    const unsigned blocks = (unsigned)(blocks64 < 148 * 32 ? blocks64 : 148 * 32);
+    quad_codes_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const uint8_t*>(planes), stage_stride,
+                                                               nvec, reinterpret_cast<uint4*>(out));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return RVQ_OK;
 }
 
 int rvq_take_index_error(void) {

@@ -29,6 +29,7 @@ namespace enc {
 constexpr int kD = 8;
 constexpr int kThreads = 256;
 constexpr int kMaxCodes = 4096;                      // shared memory: 4096 x 9 floats = 144 KB
+constexpr int kMaxLocal = 1024;                      // k for block-local k-means totals (+72 KB)
 constexpr double kFixScale = 4294967296.0;           // 2^32
 
 __device__ __forceinline__ float sqnorm8(const float (&v)[kD]) {
@@ -109,28 +110,43 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const float* __restric
 
 // One Lloyd step's statistics: assign[i] = nearest centroid, and in fixed
 // point sums[c][t] += x[i][t] * 2^32, counts[c] += 1.
+// LOCAL: the block first adds into shared-memory totals (k <= kMaxLocal),
+// then adds each nonzero total to global memory once.
 __global__ void __launch_bounds__(kThreads) kmeans_kernel(const float* __restrict__ x, int64_t n,
                                                           const float* __restrict__ cent, int k, int32_t* assign,
-                                                          unsigned long long* sums, unsigned long long* counts) {
+                                                          unsigned long long* sums, unsigned long long* counts,
+                                                          int local) {
     extern __shared__ float sm[];
     float* cbs = sm;
     float* c2s = sm + k * kD;
-    stage_codebook(cent, k, cbs, c2s);
+    unsigned long long* ls = reinterpret_cast<unsigned long long*>(sm + ((k * (kD + 1) + 1) & ~1));
+    unsigned long long* lc = ls + k * kD;
+    if (sums && local)
+        for (int j = threadIdx.x; j < k * (kD + 1); j += blockDim.x) ls[j] = 0ull;
+    stage_codebook(cent, k, cbs, c2s);                       // ends with a barrier
     const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-    if (i >= n) return;
-    float v[kD];
-    const float4 a = __ldg(reinterpret_cast<const float4*>(x + i * kD));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(x + i * kD + 4));
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    const int c = nearest(v, cbs, c2s, k);
-    if (assign) assign[i] = c;
-    if (sums) {
+    if (i < n) {
+        float v[kD];
+        const float4 a = __ldg(reinterpret_cast<const float4*>(x + i * kD));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(x + i * kD + 4));
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        const int c = nearest(v, cbs, c2s, k);
+        if (assign) assign[i] = c;
+        if (sums) {
+            unsigned long long* ts = local ? ls : sums;
+            unsigned long long* tc = local ? lc : counts;
 #pragma unroll
-        for (int t = 0; t < kD; ++t) {
-            const long long q = __double2ll_rn((double)v[t] * kFixScale);
-            atomicAdd(sums + (int64_t)c * kD + t, (unsigned long long)q);
+            for (int t = 0; t < kD; ++t)
+                atomicAdd(ts + c * kD + t, (unsigned long long)__double2ll_rn((double)v[t] * kFixScale));
+            atomicAdd(tc + c, 1ull);
         }
-        atomicAdd(counts + c, 1ull);
+    }
+    if (sums && local) {
+        __syncthreads();
+        for (int j = threadIdx.x; j < k * kD; j += blockDim.x)
+            if (ls[j]) atomicAdd(sums + j, ls[j]);
+        for (int j = threadIdx.x; j < k; j += blockDim.x)
+            if (lc[j]) atomicAdd(counts + j, lc[j]);
     }
 }
 
@@ -147,7 +163,7 @@ int prepare() {
     std::lock_guard<std::mutex> lock(g_mu);
     if (!g_ready[dev]) {
         g_ready[dev] = true;
-        const int smem = kMaxCodes * (kD + 1) * 4;
+        const int smem = kMaxCodes * (kD + 1) * 4 + 8;
         e = cudaFuncSetAttribute(encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(kmeans_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         g_ok[dev] = e == cudaSuccess;
@@ -198,8 +214,11 @@ int rvq_kmeans_step(const float* x, int64_t n, const float* centroids, int k, in
     int rc = prepare();
     if (rc != RVQ_OK || n == 0) return rc;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
-    kmeans_kernel<<<(unsigned)blocks, kThreads, (size_t)k * (kD + 1) * 4, (cudaStream_t)stream>>>(
-        x, n, centroids, k, assign, sums, counts);
+    const int local = sums != nullptr && k <= kMaxLocal;
+    size_t smem = (size_t)(((k * (kD + 1) + 1) & ~1)) * 4;
+    if (local) smem += (size_t)k * (kD + 1) * 8;
+    kmeans_kernel<<<(unsigned)blocks, kThreads, smem, (cudaStream_t)stream>>>(x, n, centroids, k, assign, sums,
+                                                                             counts, local);
     return finish();
 }
 

@@ -96,14 +96,19 @@ class LayerDecodePlan:
 
     ``items``: ``(key, entry)`` pairs of one layer; ``outs[key]``: the slot
     tensor each entry decodes into; ``max_ctas``: CTA budget of the launch (0:
-    one CTA per SM; fewer leaves SMs to the kernels of the layer being computed).  ``launch(stream)`` queues the whole
+    one CTA per SM; fewer leaves SMs to the kernels of the layer being computed);
+    ``quad_codes``: repack eligible entries' codes once into the quad layout
+    the slot kernel streams with one 16-byte load per 4 vectors (the entries'
+    own planes are left as they are).  ``launch(stream)`` queues the whole
     layer as ceil(jobs / 32) launches (one for a Qwen3 layer: 11 jobs).
     The tensors referenced by the plan must outlive it.
     """
 
     def __init__(self, items: Sequence[Tuple[str, Dict[str, object]]],
-                 codebooks: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor], max_ctas: int = 0):
+                 codebooks: Dict[str, torch.Tensor], outs: Dict[str, torch.Tensor], max_ctas: int = 0,
+                 quad_codes: bool = True):
         self.keys: List[str] = []
+        fp16_codebooks: Dict[int, Optional[torch.Tensor]] = {}
         entries: List[_native.RvqEntry] = []
         int8s: List[_native.RvqInt8Entry] = []
         copies: List[Tuple[int, int, int]] = []
@@ -138,6 +143,8 @@ class LayerDecodePlan:
                     raise ValueError(f"Triton kernel does not support entry shape {entry['shape']}")
                 st, keep = prepare_entry(entry, cb, out)
                 self._keep.append(keep)
+                if quad_codes:
+                    self._to_quad(st, entry, cb, out, fp16_codebooks)
                 entries.append(st)
                 idx = entry["indices"]
                 self.algorithmic_bytes += (out.numel() * out.element_size()
@@ -160,6 +167,48 @@ class LayerDecodePlan:
             self.batches.append((earr, len(es), qarr, len(qs), carr, len(cs)))
         self._lib = _native.load()
         self.max_ctas = int(max_ctas)
+
+    def _to_quad(self, st: _native.RvqEntry, entry, codebook: torch.Tensor, out: torch.Tensor,
+                 fp16_codebooks: Dict[int, Optional[torch.Tensor]]) -> None:
+        """Point ``st`` at a one-time repack of its codes into the quad layout
+        (rvq_quad_codes) and at an fp16 copy of its codebook, when the entry
+        is one the slot kernel decodes: 4 stages of 256 uint8 codes, every
+        codebook value an exact fp16 number (checked once per codebook), a
+        bf16 slot, fp16 scales, whole vectors, a multiple of 4 vectors per
+        scale.  Otherwise ``st`` keeps the artifact's planes."""
+        idx = entry["indices"]
+        nvec = int(idx.shape[1]) if idx.dim() == 2 else 0
+        if not (idx.dtype == torch.uint8 and idx.dim() == 2 and int(idx.shape[0]) == 4 and nvec > 0
+                and int(codebook.shape[1]) == 256 and out.dtype == torch.bfloat16
+                and entry["scales"].dtype == torch.float16 and int(entry["trimmed_numel"]) == nvec * 8
+                and (int(entry["group_size"]) // 8) % 4 == 0 and out.data_ptr() % 32 == 0):
+            return
+        key = id(codebook)
+        if key not in fp16_codebooks:
+            h = codebook.to(torch.float16).contiguous()
+            fp16_codebooks[key] = h if torch.equal(h.to(codebook.dtype), codebook) else None
+        h = fp16_codebooks[key]
+        if h is None:
+            return
+        lib = _native.load()
+        lib.rvq_quad_codes_bytes.restype = ctypes.c_int64
+        lib.rvq_quad_codes_bytes.argtypes = [ctypes.c_int64]
+        lib.rvq_quad_codes.restype = ctypes.c_int
+        lib.rvq_quad_codes.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                                       ctypes.c_void_p]
+        planes = idx.contiguous()
+        quads = torch.empty(int(lib.rvq_quad_codes_bytes(nvec)), dtype=torch.uint8, device=idx.device)
+        with torch.cuda.device(idx.device):
+            _native.check(lib.rvq_quad_codes(ctypes.c_void_p(planes.data_ptr()), nvec, nvec,
+                                             ctypes.c_void_p(quads.data_ptr()),
+                                             ctypes.c_void_p(torch.cuda.current_stream(idx.device).cuda_stream)),
+                          "rvq_quad_codes")
+        self._keep.append((quads, h))
+        st.indices = quads.data_ptr()
+        st.stage_stride = nvec
+        st.index_kind = _native.RVQ_U8X4
+        st.codebook = h.data_ptr()
+        st.codebook_kind = _native.RVQ_F16
 
     @property
     def launches(self) -> int:
