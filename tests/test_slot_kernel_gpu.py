@@ -19,7 +19,7 @@ from rvq_b200.engine import LayerDecodePlan
 pytestmark = pytest.mark.gpu
 
 SHAPES = [
-    ("a", 4096, 2560, None),     # per-row scales, 80 whole tiles... per row
+    ("a", 4096, 2560, None),     # per-row scales (320 vectors each), whole 128-vector tiles
     ("b", 100, 96, 32),          # 4 vectors per scale, 1200 vectors: a partial last tile
     ("c", 1000, 64, 64),         # 8 vectors per scale, 8000 vectors: a partial last tile
     ("d", 333, 520, None),       # 65 vectors per scale: not a multiple of 4 -> planar path

@@ -78,3 +78,27 @@ def test_noalloc_rejects_jobs_beyond_its_workspace(cuda_device):
     assert plan.workspace_bytes > limit
     rc = lib.rvq_gemv_noalloc(plan.jobs, plan.n, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == _native.RVQ_ERR_TOO_LARGE
+
+
+def test_noalloc_calls_allocate_nothing(cuda_device):
+    """After the first call on the device (which looks up the array's
+    address), further calls change neither torch's allocator statistics nor
+    the device's free memory."""
+    lib = bind(_lib())
+    g = torch.Generator().manual_seed(7)
+    cb = synthetic.make_codebook(4, 256, 8, g).to(cuda_device, torch.float32)
+    entry = to_dev(synthetic.make_rvq_entry(4096, 2560, g), cuda_device)
+    x = torch.randn(2560, generator=g).to(cuda_device, torch.bfloat16)
+    y = torch.zeros(4096, dtype=torch.float32, device=cuda_device)
+    plan = GemvPlan([(entry, cb, x, y)])
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    assert lib.rvq_gemv_noalloc(plan.jobs, plan.n, stream) == _native.RVQ_OK       # warm-up call
+    torch.cuda.synchronize()
+    allocated, reserved = torch.cuda.memory_allocated(cuda_device), torch.cuda.memory_reserved(cuda_device)
+    free_before = torch.cuda.mem_get_info(cuda_device)[0]
+    for _ in range(5):
+        assert lib.rvq_gemv_noalloc(plan.jobs, plan.n, stream) == _native.RVQ_OK
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated(cuda_device) == allocated
+    assert torch.cuda.memory_reserved(cuda_device) == reserved
+    assert torch.cuda.mem_get_info(cuda_device)[0] == free_before
