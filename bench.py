@@ -44,6 +44,7 @@ WORKLOAD = ("config1 ping-pong slot fill: Qwen-style block hidden 2560 / interme
             "32q 8kv head 128, 7 RVQ projections (K=4, 256 codes, d=8, per-row fp16 scales) "
             "+ 4 bf16 norms -> bf16 slot")
 N_LAYERS_ROTATED = 8
+DECODE_KERNEL = "rvq_slot_kernel"           # what a layer plan launches (quad codes, fp16 codebook, bf16 slot)
 # slot writes + code reads + scale reads of the 7 projections, plus the 4 bf16 norm copies
 BYTES_PER_STEP = 252396544
 FALLBACK_HBM_GBS = 6650.0
@@ -545,8 +546,8 @@ def run_ours(args, world, rank, local):
         "config": gpu_config(world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": profile_traffic("rvq_layer_kernel"),
-                     "kernel": "rvq_layer_kernel",
+                     "traffic": profile_traffic(DECODE_KERNEL),
+                     "kernel": DECODE_KERNEL,
                      "algorithmic_bytes_per_launch": bytes_per_step // launches_per_step},
         "cpu_baseline": cpu,
         "e2e": e2e,

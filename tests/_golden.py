@@ -67,10 +67,10 @@ class GoldenCase:
 
 
 def case_names() -> List[str]:
-    """RVQ decode fixtures (others: engine_*, int8_* and encoder_* files)."""
+    """RVQ decode fixtures (others: engine_*, int8_*, encoder_* and proj_* files)."""
     return sorted(os.path.splitext(os.path.basename(p))[0]
                   for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith(("engine_", "int8_", "encoder_")))
+                  if not os.path.basename(p).startswith(("engine_", "int8_", "encoder_", "proj_")))
 
 
 def int8_case_names() -> List[str]:
@@ -141,3 +141,13 @@ def bits_equal(got: np.ndarray, want: np.ndarray, out_kind: int) -> bool:
         gv, wv = bf16_bits_to_f32(got), bf16_bits_to_f32(want)
     nan = np.isnan(gv) & np.isnan(wv)
     return bool(np.all((got == want) | nan))
+
+
+def load_projection() -> dict:
+    """The reference-encoded [1024, 2560] entry at group size 128
+    (make_golden_projection.py): planes, fp16 scales and codebooks, and the
+    sha256 of the reference's decode per output kind."""
+    z = np.load(os.path.join(GOLDEN_DIR, "proj_k_g128.npz"))
+    out = {k: z[k] for k in ("indices", "scales_f16", "codebook_f16")}
+    out["sha256"] = {kind: bytes(z[f"sha256_{key}"]).decode() for kind, key in KIND_KEYS.items()}
+    return out

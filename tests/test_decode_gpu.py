@@ -230,3 +230,29 @@ def test_layer_launch_many_mixed_entries(cuda_device):
     torch.cuda.synchronize()
     for key, want in wants.items():
         assert bits_equal(out_bits(outs[key]), want, OUT_BF16), key
+
+
+@pytest.mark.parametrize("kind", list(KINDS))
+def test_projection_shape_group128_matches_reference_hash(kind, cuda_device):
+    """The reference-encoded [1024, 2560] entry at the compressor's default
+    group size 128: the single-entry API (artifact planes) and, for bf16, the
+    layer plan's slot kernel (quad codes) hash to the reference's output."""
+    import hashlib
+    from rvq_b200.engine import LayerDecodePlan
+    from tests._golden import load_projection
+    p = load_projection()
+    cb = torch.from_numpy(p["codebook_f16"]).view(torch.float16).to(cuda_device).float()
+    entry = {"method": "rvq_groupwise", "codebook_id": "attn_k_proj", "shape": [1024, 2560], "dtype": "bfloat16",
+             "group_size": 128, "d": 8, "trimmed_numel": 1024 * 2560,
+             "scales": torch.from_numpy(p["scales_f16"]).view(torch.float16).to(cuda_device),
+             "indices": torch.from_numpy(p["indices"]).to(cuda_device),
+             "tail": torch.zeros(0, dtype=torch.bfloat16, device=cuda_device)}
+    out = torch.zeros(1024, 2560, dtype=KINDS[kind], device=cuda_device)
+    decode_rvq_triton_into(entry, cb, out)
+    torch.cuda.synchronize()
+    assert hashlib.sha256(out_bits(out).tobytes()).hexdigest() == p["sha256"][kind]
+    if KINDS[kind] == torch.bfloat16:
+        slot = torch.zeros_like(out)
+        LayerDecodePlan([("k", entry)], {"attn_k_proj": cb}, {"k": slot}).launch()
+        torch.cuda.synchronize()
+        assert hashlib.sha256(out_bits(slot).tobytes()).hexdigest() == p["sha256"][kind]

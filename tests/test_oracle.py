@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 
 from oracle.c_oracle import decode_rvq_bits_c
-from oracle.rvq_oracle import (OUT_BF16, OUT_F16, OUT_F32, decode_rvq_bits, f32_to_bf16_bits,
+from oracle.rvq_oracle import (OUT_BF16, OUT_F16, OUT_F32, RVQEntryNP, decode_rvq_bits, f32_to_bf16_bits,
                                f32_to_f16_bits)
 from tests._golden import bits_equal, case_names, load_case
 
@@ -135,3 +135,18 @@ def test_int8_oracles_match_reference(name, kind):
     decode_int8_into(case.entry_torch(), out)
     b = out.view(torch.int32 if kind == OUT_F32 else torch.int16).numpy()
     assert bits_equal(b.view(np.uint32 if kind == OUT_F32 else np.uint16), case.expected[kind], kind), name
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_oracles_match_reference_at_projection_shape(kind):
+    """The reference-encoded [1024, 2560] group-128 entry: the C oracle's
+    decode hashes to the reference's own output."""
+    import hashlib
+    from oracle.rvq_oracle import f16_bits_to_f32
+    from tests._golden import load_projection
+    p = load_projection()
+    ent = RVQEntryNP(indices=p["indices"], codebook=f16_bits_to_f32(p["codebook_f16"].view(np.uint16)),
+                     scales=f16_bits_to_f32(p["scales_f16"].view(np.uint16)), tail=np.zeros(0, np.float32), d=8,
+                     group_size=128, trimmed_numel=1024 * 2560, numel=1024 * 2560)
+    got = decode_rvq_bits_c(ent, kind, nthreads=4)
+    assert hashlib.sha256(got.tobytes()).hexdigest() == p["sha256"][kind]
