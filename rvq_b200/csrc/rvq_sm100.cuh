@@ -47,7 +47,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 }
 
 // 2-D tiled TMA load of box {x, y} at coordinates {c0, c1} into shared memory,
-// completing on `bar` (no multicast).
+// completing on `bar`; a plain load into this CTA only.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int c0, int c1, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
