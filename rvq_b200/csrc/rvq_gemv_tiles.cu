@@ -563,32 +563,40 @@ __device__ __forceinline__ void exact_rows(const TJob& J, const char* cbs, int t
     const uint32_t g_global = (uint32_t)tile * kGroups + lane;
     const int nb = (r1 - r0 + exact::kBatchRows - 1) / exact::kBatchRows;
     const int orow = warp * 8 + ((lane >> 2) & 7);
-    // this warp's 8 code words of batch b (zero past the unit's rows)
-    auto fetch = [&](int b, uint32_t (&w)[8]) {
+    // this warp's 8 code words of batch b (zero past the unit's rows), and with
+    // per-row scales, lane l's copy of the scale of the warp's row l & 7
+    auto fetch = [&](int b, uint32_t (&w)[8], float& rs) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = r0 + b * exact::kBatchRows + warp * 8 + i;
             w[i] = (b < nb && r < r1) ? __ldg(lines + (int64_t)r * kLineWords + lane) : 0u;
         }
+        const int r = r0 + b * exact::kBatchRows + warp * 8 + (lane & 7);
+        rs = (J.row_scales && b < nb && r < r1) ? load_as_f32(J.scales, fastdiv((uint32_t)r, J.rpsdiv), J.scale_kind)
+                                               : 0.f;
     };
     uint32_t wn[8];
-    fetch(0, wn);
+    float rsn;
+    fetch(0, wn, rsn);
     for (int b = 0; b < nb; ++b) {
         uint32_t wc[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) wc[i] = wn[i];
-        fetch(b + 1, wn);
+        const float rsc = rsn;
+        fetch(b + 1, wn, rsn);
         const int rb = r0 + b * exact::kBatchRows + warp * 8;
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = rb + i;
-            float s = 0.f;
-            if (r < r1) {
-                if (J.row_scales) s = load_as_f32(J.scales, fastdiv((uint32_t)r, J.rpsdiv), J.scale_kind);
-                else if (lane < gt)
-                    s = load_as_f32(J.scales, fastdiv((uint32_t)r * (uint32_t)J.G + g_global, J.gvdiv),
-                                    J.scale_kind);
+            float s;
+            if (J.row_scales) {
+                s = __shfl_sync(0xffffffffu, rsc, i);          // zero past the unit's rows
+            } else {
+                s = (r < r1 && lane < gt)
+                        ? load_as_f32(J.scales, fastdiv((uint32_t)r * (uint32_t)J.G + g_global, J.gvdiv),
+                                      J.scale_kind)
+                        : 0.f;
             }
             v[i] = dot8_bf16(vdec::weights_bf16<SMEM>(cbs, J.cb, J.cb_kind, wc[i], lb, s), xh);
         }
