@@ -260,48 +260,46 @@ __device__ __forceinline__ void build_lut_f16(uint32_t* __restrict__ lut, const 
     }
 }
 
-// The same table from an fp16 codebook ([4][256] rows of 8 halves, 16 KB) and
-// x' in fp16: one 16-byte broadcast load per codebook row instead of two, the
-// 8-term dot products by fma.rn.f32.f16 (exact products, fp32 accumulation in
-// element order, as the fp32 build).
-__device__ __forceinline__ float dot8_h(const uint4& c, const uint32_t (&xh)[4]) {
-    float acc;
-    asm("{\n .reg .b16 c0, c1, c2, c3, c4, c5, c6, c7, x0, x1, x2, x3, x4, x5, x6, x7;\n"
-        " mov.b32 {c0, c1}, %1;\n mov.b32 {c2, c3}, %2;\n mov.b32 {c4, c5}, %3;\n mov.b32 {c6, c7}, %4;\n"
-        " mov.b32 {x0, x1}, %5;\n mov.b32 {x2, x3}, %6;\n mov.b32 {x4, x5}, %7;\n mov.b32 {x6, x7}, %8;\n"
-        " fma.rn.f32.f16 %0, c0, x0, 0f00000000;\n fma.rn.f32.f16 %0, c1, x1, %0;\n"
-        " fma.rn.f32.f16 %0, c2, x2, %0;\n fma.rn.f32.f16 %0, c3, x3, %0;\n"
-        " fma.rn.f32.f16 %0, c4, x4, %0;\n fma.rn.f32.f16 %0, c5, x5, %0;\n"
-        " fma.rn.f32.f16 %0, c6, x6, %0;\n fma.rn.f32.f16 %0, c7, x7, %0;\n}\n"
-        : "=f"(acc)
-        : "r"(c.x), "r"(c.y), "r"(c.z), "r"(c.w), "r"(xh[0]), "r"(xh[1]), "r"(xh[2]), "r"(xh[3]));
-    return acc;
-}
-
-__device__ __forceinline__ void build_lut_h(uint32_t* __restrict__ lut, const uint4* __restrict__ cbh,
-                                            const float* __restrict__ xs, float xscale) {
+// The same table by tensor-core MMAs: LUT[(k, c)][g] = sum_t cb_k[c][t] x'_g[t]
+// is a [1024 x 8] x [8 x 32] product.  mma.sync m16n8k16 (fp16 operands, fp32
+// accumulation; K padded from 8 to 16 with zeros): an m16 block holds codes
+// 8 b .. 8 b + 7 at stage 2 p in rows 0-7 and at stage 2 p + 1 in rows 8-15,
+// so each thread's accumulators (c0, c2) and (c1, c3) are the stage pair of
+// one (code, group) and pack directly into the table's fp16-pair words.
+// Warp w computes m16 blocks w and w + 32 (pairs 0 and 1) for the 4 n8
+// blocks of groups: 8 MMAs.  Products of fp16 values are exact; only the
+// fp32 summation order may differ from the FFMA build.
+__device__ __forceinline__ void build_lut_mma(uint32_t* __restrict__ lut, const uint4* __restrict__ cbh,
+                                              const float* __restrict__ xs, float xscale) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t xh[4];
+    const int gid = lane >> 2, tig = lane & 3;
+    // B fragments: x' of groups 8 nb + gid, elements 2 tig and 2 tig + 1 (rows 8..15 zero)
+    uint32_t bx[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const __half2 h = __floats2half2_rn(xs[lane * 8 + 2 * i] * xscale, xs[lane * 8 + 2 * i + 1] * xscale);
-        xh[i] = *reinterpret_cast<const uint32_t*>(&h);
+    for (int nb = 0; nb < 4; ++nb) {
+        const int g = 8 * nb + gid;
+        const __half2 h = __floats2half2_rn(xs[8 * g + 2 * tig] * xscale, xs[8 * g + 2 * tig + 1] * xscale);
+        bx[nb] = *reinterpret_cast<const uint32_t*>(&h);
     }
-#pragma unroll 1
-    for (int p0 = warp; p0 < kCodes * 2; p0 += kWarps * 2) {
-        uint4 c[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {            // j = 2 * word + stage within the pair
-            const int p = p0 + (j >> 1) * kWarps, code = p >> 1, k = ((p & 1) << 1) + (j & 1);
-            c[j] = cbh[k * kCodes + code];
-        }
-        float acc[4];
+    for (int h = 0; h < 2; ++h) {
+        const int mb = warp + 32 * h;              // m16 block: pair p = mb / 32, code block b = mb % 32
+        const int p = mb >> 5, code = 8 * (mb & 31) + gid;
+        // A fragment: word tig of the fp16 codebook rows (stage 2p, code) and (stage 2p + 1, code)
+        const uint32_t a0 = reinterpret_cast<const uint32_t*>(cbh + (2 * p) * kCodes + code)[tig];
+        const uint32_t a1 = reinterpret_cast<const uint32_t*>(cbh + (2 * p + 1) * kCodes + code)[tig];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] = dot8_h(c[j], xh);
-#pragma unroll
-        for (int w = 0; w < 2; ++w) {
-            const __half2 h = __floats2half2_rn(acc[2 * w], acc[2 * w + 1]);    // low half: even stage
-            lut[(p0 + w * kWarps) * kGroups + lane] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int nb = 0; nb < 4; ++nb) {
+            float c0, c1, c2, c3;
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                "{%10, %10, %10, %10};\n"
+                : "=f"(c0), "=f"(c1), "=f"(c2), "=f"(c3)
+                : "r"(a0), "r"(a1), "r"(0u), "r"(0u), "r"(bx[nb]), "r"(0u), "f"(0.f));
+            const int g = 8 * nb + 2 * tig;
+            const __half2 w0 = __floats2half2_rn(c0, c2), w1 = __floats2half2_rn(c1, c3);   // low half: even stage
+            lut[(code * 2 + p) * kGroups + g] = *reinterpret_cast<const uint32_t*>(&w0);
+            lut[(code * 2 + p) * kGroups + g + 1] = *reinterpret_cast<const uint32_t*>(&w1);
         }
     }
 }
@@ -436,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_tiles_kernel(const __gri
         for (int w = 1; w < kTileCols / 32; ++w) amax = fmaxf(amax, xmax[w]);
         float xscale, xunscale;
         tile_scale(amax, xscale, xunscale);
-        if (cb_half) build_lut_h(lut, reinterpret_cast<const uint4*>(cbs), xs, xscale);
+        if (cb_half) build_lut_mma(lut, reinterpret_cast<const uint4*>(cbs), xs, xscale);
         else build_lut_f16(lut, cbs, xs, xscale);
         __syncthreads();
 
