@@ -396,9 +396,9 @@ int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64
  * shared memory as the A operand of tcgen05.mma (M = 128 weight rows, N = a
  * block of up to 256 tokens, fp32 accumulation in TMEM); only the codes,
  * scales and x are read from HBM.  More than 256 tokens run as blocks of 256,
- * each weight chunk decoded once per block.  A job whose split needs more
- * than the kernel's segment table returns RVQ_ERR_TOO_LARGE.  W: K=4 stages, 256 codes, uint8 codes in the
- * tile-major layout of rvq_tile_codes (weight.indices, 16-byte aligned), no
+ * each weight chunk decoded once per block.  A job of 2^31 or more (row
+ * tile, token block, 64-column chunk) units returns RVQ_ERR_TOO_LARGE.  W:
+ * K=4 stages, 256 codes, uint8 codes in the tile-major layout of rvq_tile_codes (weight.indices, 16-byte aligned), no
  * tail; codebook fp32, fp16 or bf16.  x bf16 [tokens][cols] row-major, 16-byte
  * aligned, cols a multiple of 8; y bf16 [tokens][rows].  Deterministic: split-K
  * pieces are added in a fixed order. */

@@ -19,10 +19,14 @@
 //
 // Work split: the (row tile, token block, chunk) units in that order are cut
 // into one contiguous range per SM, so every CTA decodes the same number of
-// chunks.  A (tile, block) cut into several pieces writes fp32 partial sums
-// to the workspace; the CTA that finishes its last piece (ticket counter)
-// adds the pieces in piece order and writes y, so results do not depend on
-// timing.  Units held by one CTA write y directly.
+// chunks.  Each CTA derives its segments (the (tile, block) pairs its range
+// touches), their piece numbers and workspace slots from the split formula
+// itself, so the launch carries no table.  A (tile, block) cut into several
+// pieces writes fp32 partial sums to the workspace -- slot 2c for the first
+// segment of CTA c, 2c + 1 for its last (a middle segment is never cut); the
+// CTA that finishes its last piece (ticket counter) adds the pieces in piece
+// order and writes y, so results do not depend on timing.  Units held by one
+// CTA write y directly.
 //
 // Only the codes (0.5 B per weight), the scales and x are read from HBM.
 
@@ -31,7 +35,6 @@
 
 #include <mutex>
 #include <string.h>
-#include <vector>
 
 #include "rvq_common.cuh"
 #include "rvq_sm100.cuh"
@@ -51,22 +54,12 @@ constexpr int kChunk = 64;                                   // columns per chun
 constexpr int kChunkVecs = kChunk / 8;
 constexpr int kWStageBytes = kTileRows * kChunk * 2;         // 16 KB
 constexpr int kMaxStages = 4;
-constexpr int kBlockTokens = 256;                          // MMA N per token block (max)
+constexpr int kBlockTokens = 256;                            // MMA N per token block (max)
 constexpr int kMaxTokens = 65536;
-constexpr int kMaxCtas = 160;
-constexpr int kMaxSegs = 1536;
-constexpr int kMaxSegsPerCta = 16;
 constexpr long long kWaitLimit = 1ll << 24;
 constexpr int kBudget = 226 * 1024;                          // dynamic shared memory limit used per CTA
 
 __device__ int g_batch_timeout;
-
-struct Seg {
-    uint32_t unit;            // tile * blocks + token block
-    uint32_t piece_np;        // piece << 8 | npieces
-    uint32_t chunks;          // kc0 << 16 | kc1
-    int32_t slot;             // first workspace slot of the unit's pieces (npieces > 1)
-};
 
 struct BParams {
     CUtensorMap xmap;         // x [T][K] bf16, box {64, npad}, 128-byte swizzle
@@ -74,19 +67,32 @@ struct BParams {
     const void* cb;
     const void* scales;
     __nv_bfloat16* y;         // [T][R]
-    float* part;              // workspace: [slots][npad][128] fp32
-    uint32_t* tickets;        // workspace: [units]
-    int32_t R, G, T, npad, blocks, stages, n_ctas;
+    float* part;              // workspace: [2 n_ctas][npad][128] fp32
+    uint32_t* tickets;        // workspace: [tiles * blocks]
+    int64_t U;                // (tile, token block, chunk) units
+    int32_t R, G, T, npad, blocks, KC, stages, n_ctas;
     int32_t cb_kind, scale_kind, row_scales;
     FastDiv gvdiv, rpsdiv;
-    int32_t seg_first[kMaxCtas + 1];
-    Seg segs[kMaxSegs];
 };
 
-__device__ __forceinline__ int seg_piece(const Seg& s) { return (int)(s.piece_np >> 8); }
-__device__ __forceinline__ int seg_np(const Seg& s) { return (int)(s.piece_np & 255u); }
-__device__ __forceinline__ int seg_kc0(const Seg& s) { return (int)(s.chunks >> 16); }
-__device__ __forceinline__ int seg_kc1(const Seg& s) { return (int)(s.chunks & 0xffffu); }
+// CTA c owns units [range_begin(c), range_begin(c + 1)).
+__device__ __forceinline__ int64_t range_begin(const BParams& p, int c) { return p.U * c / p.n_ctas; }
+// The CTA whose range holds unit u.
+__device__ __forceinline__ int cta_of(const BParams& p, int64_t u) { return (int)(((u + 1) * p.n_ctas - 1) / p.U); }
+
+// The segment that starts at unit u of a range ending at u1: its (tile, block)
+// index and chunk range [kc0, kc1).
+struct Seg {
+    int unit, kc0, kc1;
+};
+__device__ __forceinline__ Seg seg_at(const BParams& p, int64_t u, int64_t u1) {
+    Seg s;
+    s.unit = (int)(u / p.KC);
+    const int64_t base = (int64_t)s.unit * p.KC;
+    s.kc0 = (int)(u - base);
+    s.kc1 = (int)(u1 - base < p.KC ? u1 - base : p.KC);
+    return s;
+}
 
 __device__ __forceinline__ float load_scale_at(const BParams& p, int row, int g) {
     if (p.row_scales) return load_as_f32(p.scales, fastdiv((uint32_t)row, p.rpsdiv), p.scale_kind);
@@ -110,7 +116,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = p.stages;
-    const int s_first = p.seg_first[blockIdx.x], s_last = p.seg_first[blockIdx.x + 1];
+    const int cta = blockIdx.x;
+    const int64_t u_first = range_begin(p, cta), u_last = range_begin(p, cta + 1);
     // two accumulators of npad columns; the epilogue reads 32 columns at a time
     const int tmem_need = p.npad + (p.npad > 32 ? p.npad : 32);
     const uint32_t tmem_cols = tmem_need <= 32 ? 32u : (tmem_need <= 64 ? 64u : (tmem_need <= 128 ? 128u
@@ -141,10 +148,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         vdec::lane_bits(lane, lb);
         const int v = tid & 7;
         int g = 0;
-        for (int si = s_first; si < s_last; ++si) {
-            const Seg sg = p.segs[si];
-            const int tile = (int)sg.unit / p.blocks, kc1 = seg_kc1(sg);
-            for (int kc = seg_kc0(sg); kc < kc1; ++kc, ++g) {
+        for (int64_t u = u_first; u < u_last;) {
+            const Seg sg = seg_at(p, u, u_last);
+            const int tile = sg.unit / p.blocks;
+            u += sg.kc1 - sg.kc0;
+            for (int kc = sg.kc0; kc < sg.kc1; ++kc, ++g) {
                 const int st = g % S;
                 if (g >= S) {                                      // the MMAs of chunk g - S left stage st
                     if (lane == 0) mbar_wait(bar_done + 8 * st, ((g / S) - 1) & 1, kWaitLimit, &g_batch_timeout);
@@ -175,30 +183,25 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         // ---- issuer: x by TMA (S - 1 chunks ahead), MMAs once a chunk's weights are decoded
         if (lane == 0) {
             const uint32_t idesc = instr_desc_bf16(kTileRows, p.npad);
-            // x of the CTA's chunk number g: column chunk and token block, walking the segments
+            // x of the CTA's chunk number g (unit u_first + g): column chunk and token block
             auto load_x = [&](int g) {
-                for (int si = s_first; si < s_last; ++si) {
-                    const Seg& sg = p.segs[si];
-                    const int n = seg_kc1(sg) - seg_kc0(sg);
-                    if (g < n) {
-                        const int st = g % S, kc = seg_kc0(sg) + g, blk = (int)sg.unit % p.blocks;
-                        mbar_expect_tx(bar_x + 8 * st, (uint32_t)xstage_bytes);
-                        tma_load_2d(smem_addr(xs + st * xstage_bytes), &p.xmap, kc * kChunk, blk * p.npad,
-                                    bar_x + 8 * st);
-                        return;
-                    }
-                    g -= n;
-                }
+                const int64_t u = u_first + g;
+                if (u >= u_last) return;
+                const int unit = (int)(u / p.KC), kc = (int)(u - (int64_t)unit * p.KC), blk = unit % p.blocks;
+                const int st = g % S;
+                mbar_expect_tx(bar_x + 8 * st, (uint32_t)xstage_bytes);
+                tma_load_2d(smem_addr(xs + st * xstage_bytes), &p.xmap, kc * kChunk, blk * p.npad, bar_x + 8 * st);
             };
             for (int g = 0; g < S - 1; ++g) load_x(g);
-            int g = 0;
-            for (int si = s_first; si < s_last; ++si) {
-                const Seg sg = p.segs[si];
-                const int acc = (si - s_first) & 1, n_seg = si - s_first;
+            int g = 0, n_seg = 0;
+            for (int64_t u = u_first; u < u_last; ++n_seg) {
+                const Seg sg = seg_at(p, u, u_last);
+                u += sg.kc1 - sg.kc0;
+                const int acc = n_seg & 1;
                 if (n_seg >= 2)                                    // the epilogue has read this accumulator
                     mbar_wait(bar_acce + 8 * acc, ((n_seg >> 1) - 1) & 1, kWaitLimit, &g_batch_timeout);
                 tc_fence_after();
-                const int kc0 = seg_kc0(sg), kc1 = seg_kc1(sg);
+                const int kc0 = sg.kc0, kc1 = sg.kc1;
                 for (int kc = kc0; kc < kc1; ++kc, ++g) {
                     const int st = g % S;
                     mbar_wait(bar_w + 8 * st, (g / S) & 1, kWaitLimit, &g_batch_timeout);
@@ -224,16 +227,21 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         // ---- epilogue warps: warp e reads TMEM lanes 32 e .. 32 e + 31 (tile rows)
         const int e = warp - kDecodeWarps;
         const int r = 32 * e + lane;
-        for (int si = s_first; si < s_last; ++si) {
-            const Seg sg = p.segs[si];
-            const int acc = (si - s_first) & 1, n_seg = si - s_first;
-            const int tile = (int)sg.unit / p.blocks, np = seg_np(sg);
-            const int t0 = ((int)sg.unit % p.blocks) * p.npad, nt = min(p.npad, p.T - t0);
+        int n_seg = 0;
+        for (int64_t u = u_first; u < u_last; ++n_seg) {
+            const Seg sg = seg_at(p, u, u_last);
+            u += sg.kc1 - sg.kc0;
+            const int acc = n_seg & 1;
+            const int tile = sg.unit / p.blocks;
+            const int t0 = (sg.unit % p.blocks) * p.npad, nt = min(p.npad, p.T - t0);
+            // the CTAs whose ranges hold this unit's chunks: pieces cf .. cl, this CTA's is cta - cf
+            const int64_t ubase = (int64_t)sg.unit * p.KC;
+            const int cf = cta_of(p, ubase), np = cta_of(p, ubase + p.KC - 1) - cf + 1;
             const int row = tile * kTileRows + r;
             if (lane == 0) mbar_wait(bar_accf + 8 * acc, (n_seg >> 1) & 1, kWaitLimit, &g_batch_timeout);
             __syncwarp();
             tc_fence_after();
-            float* part = p.part + ((int64_t)(sg.slot + seg_piece(sg)) * p.npad) * kTileRows + r;
+            float* part = p.part + ((int64_t)(2 * cta + (n_seg ? 1 : 0)) * p.npad) * kTileRows + r;
             for (int c0 = 0; c0 < p.npad; c0 += 32) {
                 uint32_t vals[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * e) << 16) + (uint32_t)(acc * p.npad + c0), vals);
@@ -263,11 +271,15 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
                 asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
                 if (last_piece) {
                     __threadfence();
-                    const float* base_p = p.part + ((int64_t)sg.slot * p.npad) * kTileRows + r;
+                    // piece 0 is CTA cf's last segment unless cf's range starts at this unit;
+                    // piece q > 0 is the first segment of CTA cf + q
+                    const int slot0 = 2 * cf + (range_begin(p, cf) == ubase ? 0 : 1);
+                    const float* base_p = p.part + r;
                     if (row < p.R) {
                         for (int t = 0; t < nt; ++t) {
-                            float sum = __ldcg(base_p + (int64_t)t * kTileRows);
-                            for (int q = 1; q < np; ++q) sum += __ldcg(base_p + ((int64_t)q * p.npad + t) * kTileRows);
+                            float sum = __ldcg(base_p + ((int64_t)slot0 * p.npad + t) * kTileRows);
+                            for (int q = 1; q < np; ++q)
+                                sum += __ldcg(base_p + ((int64_t)(2 * (cf + q)) * p.npad + t) * kTileRows);
                             p.y[(int64_t)(t0 + t) * p.R + row] = __float2bfloat16_rn(sum);
                         }
                     }
@@ -329,8 +341,9 @@ int stages_for(int npad) {
     return s > kMaxStages ? kMaxStages : s;
 }
 
-// Segments of the balanced split.  Returns the workspace bytes it needs
-// (partials, then one ticket per (tile, token block) unit) or a negative status.
+// The balanced split's sizes.  Returns the workspace bytes it needs (two
+// partial slots per CTA, then one ticket per (tile, token block) unit) or a
+// negative status.
 int64_t plan(const rvq_gemv_batch_job& j, int sms, BParams* p) {
     const int64_t R = j.rows, G = j.cols / 8, T = j.tokens;
     const int64_t KC = (G + kChunkVecs - 1) / kChunkVecs;
@@ -338,59 +351,16 @@ int64_t plan(const rvq_gemv_batch_job& j, int sms, BParams* p) {
     const int64_t npad = npad_of(T), NB = (T + npad - 1) / npad;
     const int64_t NU = NT * NB;                                   // (tile, token block) units
     const int64_t U = NU * KC;
-    if (NU >= (1ll << 31)) return -RVQ_ERR_TOO_LARGE;
-    int64_t ctas = sms < kMaxCtas ? sms : kMaxCtas;
-    if (ctas > U) ctas = U;
-    // pieces of every unit: the CTA ranges that overlap it
-    int nseg = 0;
-    int64_t slots = 0;
-    std::vector<int> unit_np((size_t)NU, 0);
-    std::vector<int64_t> unit_slot((size_t)NU, 0);
-    for (int pass = 0; pass < 2; ++pass) {
-        nseg = 0;
-        std::vector<int> piece(pass ? (size_t)NU : 0, 0);
-        for (int64_t c = 0; c < ctas; ++c) {
-            const int64_t u0 = U * c / ctas, u1 = U * (c + 1) / ctas;
-            if (p) p->seg_first[c] = nseg;
-            int in_cta = 0;
-            for (int64_t u = u0; u < u1;) {
-                const int64_t unit = u / KC, kc0 = u % KC;
-                const int64_t kc1 = (u1 - unit * KC) < KC ? (u1 - unit * KC) : KC;
-                if (pass == 0) {
-                    unit_np[(size_t)unit] += 1;
-                } else {
-                    if (nseg >= kMaxSegs || ++in_cta > kMaxSegsPerCta) return -RVQ_ERR_TOO_LARGE;
-                    Seg& s = p->segs[nseg];
-                    const int np = unit_np[(size_t)unit];
-                    s.unit = (uint32_t)unit;
-                    s.piece_np = ((uint32_t)piece[(size_t)unit] << 8) | (uint32_t)np;
-                    s.chunks = ((uint32_t)kc0 << 16) | (uint32_t)kc1;
-                    s.slot = np > 1 ? (int32_t)unit_slot[(size_t)unit] : 0;
-                    piece[(size_t)unit] += 1;
-                }
-                ++nseg;
-                u = unit * KC + kc1;
-            }
-        }
-        if (pass == 0) {
-            for (int64_t t = 0; t < NU; ++t) {
-                if (unit_np[(size_t)t] > 255) return -RVQ_ERR_TOO_LARGE;
-                if (unit_np[(size_t)t] > 1) {
-                    unit_slot[(size_t)t] = slots;
-                    slots += unit_np[(size_t)t];
-                }
-            }
-            if (slots >= (1ll << 31)) return -RVQ_ERR_TOO_LARGE;
-            if (!p) break;
-        }
-    }
+    if (U >= (1ll << 31)) return -RVQ_ERR_TOO_LARGE;
+    const int64_t ctas = sms < U ? sms : U;
     if (p) {
-        p->seg_first[ctas] = nseg;
+        p->U = U;
+        p->KC = (int32_t)KC;
         p->n_ctas = (int32_t)ctas;
         p->npad = (int32_t)npad;
         p->blocks = (int32_t)NB;
     }
-    const int64_t part_bytes = (slots * npad * kTileRows * 4 + 255) / 256 * 256;
+    const int64_t part_bytes = (2 * ctas * npad * kTileRows * 4 + 255) / 256 * 256;
     return part_bytes + NU * 4;
 }
 
@@ -433,7 +403,7 @@ int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t worksp
     int sms = 0;
     rc = prepare(&sms);
     if (rc != RVQ_OK) return rc;
-    static thread_local BParams p;
+    BParams p;
     memset(&p, 0, sizeof(p));
     const int64_t need = plan(*job, sms, &p);
     if (need < 0) return (int)-need;

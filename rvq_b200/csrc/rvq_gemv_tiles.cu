@@ -220,8 +220,8 @@ __device__ __forceinline__ void load_batch(uint32_t dst, const uint32_t* lines, 
 // cb[2 pair + 1][c] . x'_g), x'_g = 2^-E x[8g : 8g + 8].
 // ---------------------------------------------------------------------------
 
-// FFMA: warp w builds words p = w + 32 j (p = 2 c + pair, word index 32 p + g);
-// lane = group.  Two words' four codebook rows are loaded (broadcast) before
+// FFMA (codebooks fp16 cannot hold exactly, staged in fp32): warp w builds
+// words p = w + 32 j (p = 2 c + pair, word index 32 p + g); lane = group.  Two words' four codebook rows are loaded (broadcast) before
 // any is stored; each store is one conflict-free 128-byte row of words.
 __device__ __forceinline__ void build_lut_f16(uint32_t* __restrict__ lut, const float* __restrict__ cbs,
                                               const float* __restrict__ xs, float xscale) {
