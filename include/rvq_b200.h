@@ -393,10 +393,10 @@ int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64
  * F.linear: infer_compressed_layerwise_triton.py:263, 290-292):
  *   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < tokens (1..65536)
  * W is rebuilt bit-identically to rvq_decode's bf16 slot values straight into
- * shared memory as the A operand of tcgen05.mma (M = 128 weight rows, N = a
- * block of up to 256 tokens, fp32 accumulation in TMEM); only the codes,
- * scales and x are read from HBM.  More than 256 tokens run as blocks of 256,
- * each weight chunk decoded once per block.  A job of 2^31 or more (row
+ * tensor memory as the A operand of tcgen05.mma (M = 128 weight rows, N = a
+ * block of up to 192 tokens, fp32 accumulation in TMEM); only the codes,
+ * scales and x are read from HBM.  More than 192 tokens run as equal blocks
+ * of at most 192, each weight chunk decoded once per block.  A job of 2^31 or more (row
  * tile, token block, 64-column chunk) units returns RVQ_ERR_TOO_LARGE.  W:
  * K=4 stages, 256 codes, uint8 codes in the tile-major layout of rvq_tile_codes (weight.indices, 16-byte aligned), no
  * tail; codebook fp32, fp16 or bf16.  x bf16 [tokens][cols] row-major, 16-byte

@@ -3,19 +3,22 @@
 //   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < T tokens, W an RVQ entry
 //
 // The reference materialises W into the slot and calls F.linear
-// (infer_compressed_layerwise_triton.py:290-292).  Here W never reaches HBM:
-// it stays the A operand of tcgen05.mma.  A CTA owns 128-row tiles of W and
-// ranges of 64-column chunks ("segments"); for every chunk, 16 decoder warps
-// rebuild the 128 x 64 weights bit-identically to the slot's bf16 values
-// (rvq_vecdecode.cuh) straight into shared memory in the K-major
-// 128-byte-swizzled layout (one RVQ vector = one 16-byte swizzle chunk), the
-// issuer warp loads x[0:T][chunk] by TMA (rows past T read as zero) and issues
-// four tcgen05.mma (kind::f16, M = 128 weight rows, N = a block of up to 256
-// tokens, K = 16), accumulating in TMEM.  Four epilogue warps read each
-// finished segment with tcgen05.ld; two accumulators alternate, so the next
-// segment's MMAs run while the previous one is read out.  A prompt of T > 256
-// tokens runs as token blocks of 256: each weight chunk is decoded once per
-// block and feeds 128 x 256 x 64 MACs.
+// (infer_compressed_layerwise_triton.py:290-292).  Here W never reaches HBM
+// or shared memory: it is the A operand of tcgen05.mma read from tensor
+// memory.  A CTA owns 128-row tiles of W and ranges of 64-column chunks
+// ("segments").  For every chunk, 16 decoder warps rebuild the 128 x 64
+// weights bit-identically to the slot's bf16 values (rvq_vecdecode.cuh; the
+// codebook is the only large shared-memory table) and store them into a TMEM
+// weight stage with tcgen05.st: warp w owns TMEM lanes 32 (w % 4) .. + 31, one
+// weight row per thread, and two of the chunk's 8 vectors.  Their code words
+// and scales are loaded kPrefetch chunks ahead, so HBM latency is not paid per
+// chunk.  The issuer warp loads x[block][chunk] by TMA (rows past T read as
+// zero) and issues four tcgen05.mma (kind::f16, A = the TMEM stage, B = x in
+// shared memory, M = 128 weight rows, N = a block of up to 192 tokens, K = 16),
+// accumulating in TMEM.  Four epilogue warps read each finished segment with
+// tcgen05.ld; two accumulators alternate, so the next segment's MMAs run while
+// the previous one is read out.  A prompt of more than 192 tokens runs as
+// equal token blocks: each weight chunk is decoded once per block.
 //
 // Work split: the (row tile, token block, chunk) units in that order are cut
 // into one contiguous range per SM, so every CTA decodes the same number of
@@ -52,9 +55,9 @@ constexpr int kThreads = (kIssuer + 1) * 32;                 // 672
 constexpr int kTileRows = 128;                               // MMA M: weight rows per tile
 constexpr int kChunk = 64;                                   // columns per chunk (one 128-byte swizzle row)
 constexpr int kChunkVecs = kChunk / 8;
-constexpr int kWStageBytes = kTileRows * kChunk * 2;         // 16 KB
 constexpr int kMaxStages = 4;
-constexpr int kBlockTokens = 256;                            // MMA N per token block (max)
+constexpr int kPrefetch = 4;                                 // chunks of codes and scales in flight per decoder
+constexpr int kBlockTokens = 192;                            // MMA N per token block (max)
 constexpr int kMaxTokens = 65536;
 constexpr long long kWaitLimit = 1ll << 24;
 constexpr int kBudget = 226 * 1024;                          // dynamic shared memory limit used per CTA
@@ -94,6 +97,17 @@ __device__ __forceinline__ Seg seg_at(const BParams& p, int64_t u, int64_t u1) {
     return s;
 }
 
+// TMEM columns: accumulators at 0 and npad, each read 32 columns at a time
+// (up to column npad + round32(npad) - 1), then weight stages of 32 columns
+// from a_base_of(npad).
+__host__ __device__ __forceinline__ int a_base_of(int npad) {
+    return (npad + (npad + 31) / 32 * 32 + 31) / 32 * 32;
+}
+__host__ __device__ __forceinline__ uint32_t tmem_cols_of(int npad, int stages) {
+    const int need = a_base_of(npad) + 32 * stages;
+    return need <= 32 ? 32u : (need <= 64 ? 64u : (need <= 128 ? 128u : (need <= 256 ? 256u : 512u)));
+}
+
 __device__ __forceinline__ float load_scale_at(const BParams& p, int row, int g) {
     if (p.row_scales) return load_as_f32(p.scales, fastdiv((uint32_t)row, p.rpsdiv), p.scale_kind);
     if (g >= p.G) return 0.f;
@@ -104,9 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     char* cbs = reinterpret_cast<char*>(base);                               // 128 KB codebook
-    uint8_t* ws = base + vdec::kCbBytes;                                     // W stages
     const int xstage_bytes = p.npad * 128;
-    uint8_t* xs = ws + p.stages * kWStageBytes;                              // x stages
+    uint8_t* xs = base + vdec::kCbBytes;                                     // x stages
     uint64_t* bars = reinterpret_cast<uint64_t*>(xs + p.stages * xstage_bytes);
     // w_full[S] | x_full[S] | done[S] | acc_full[2] | acc_free[2]
     const uint32_t bar_w = smem_addr(bars), bar_x = bar_w + 8 * kMaxStages, bar_done = bar_x + 8 * kMaxStages;
@@ -118,10 +131,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
     const int S = p.stages;
     const int cta = blockIdx.x;
     const int64_t u_first = range_begin(p, cta), u_last = range_begin(p, cta + 1);
-    // two accumulators of npad columns; the epilogue reads 32 columns at a time
-    const int tmem_need = p.npad + (p.npad > 32 ? p.npad : 32);
-    const uint32_t tmem_cols = tmem_need <= 32 ? 32u : (tmem_need <= 64 ? 64u : (tmem_need <= 128 ? 128u
-                                                       : (tmem_need <= 256 ? 256u : 512u)));
+    // TMEM: two accumulators of npad columns (the epilogue reads 32 columns at a
+    // time), then S weight stages of 32 columns (128 rows x 64 bf16)
+    const uint32_t a_base = (uint32_t)a_base_of(p.npad);
+    const uint32_t tmem_cols = tmem_cols_of(p.npad, S);
 
     if (tid == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
@@ -143,38 +156,55 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
     const uint32_t tmem = *tmem_slot;
 
     if (warp < kDecodeWarps) {
-        // ---- decoders: thread (v = tid & 7, r = tid / 8 + 64 j) rebuilds vector v of rows r of each chunk
+        // ---- decoders: warp w owns TMEM lanes 32 (w % 4) .. + 31 (tile rows) and
+        // vectors 2 (w / 4), 2 (w / 4) + 1 of every chunk; thread = one row.
+        // Code words and scales are fetched kPrefetch chunks ahead.
         uint32_t lb[4];
         vdec::lane_bits(lane, lb);
-        const int v = tid & 7;
-        int g = 0;
-        for (int64_t u = u_first; u < u_last;) {
-            const Seg sg = seg_at(p, u, u_last);
-            const int tile = sg.unit / p.blocks;
-            u += sg.kc1 - sg.kc0;
-            for (int kc = sg.kc0; kc < sg.kc1; ++kc, ++g) {
+        const int quarter = warp & 3, vp = warp >> 2;
+        const int r = 32 * quarter + lane;
+        const int n_chunks = (int)(u_last - u_first);
+        const uint32_t t_lane = tmem + ((uint32_t)(32 * quarter) << 16) + a_base + 8u * (uint32_t)vp;
+        int f_unit = (int)(u_first / p.KC), f_kc = (int)(u_first - (int64_t)f_unit * p.KC);
+        uint2 cw[kPrefetch];
+        float cs0[kPrefetch], cs1[kPrefetch];
+        // fetch the next chunk in CTA order into ring slot i
+        auto fetch = [&](uint2& w, float& s0, float& s1) {
+            const int row = (f_unit / p.blocks) * kTileRows + r;
+            w = make_uint2(0u, 0u);
+            s0 = s1 = 0.f;
+            if (row < p.R) {
+                const uint32_t* line = p.codes + ((int64_t)(f_kc >> 2) * p.R + row) * 32 + (f_kc & 3) * kChunkVecs;
+                w = __ldg(reinterpret_cast<const uint2*>(line) + vp);
+                s0 = load_scale_at(p, row, f_kc * kChunkVecs + 2 * vp);
+                s1 = load_scale_at(p, row, f_kc * kChunkVecs + 2 * vp + 1);
+            }
+            if (++f_kc == p.KC) {
+                f_kc = 0;
+                ++f_unit;
+            }
+        };
+#pragma unroll
+        for (int i = 0; i < kPrefetch; ++i)
+            if (i < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
+        for (int g0 = 0; g0 < n_chunks; g0 += kPrefetch) {
+#pragma unroll
+            for (int i = 0; i < kPrefetch; ++i) {
+                const int g = g0 + i;
+                if (g >= n_chunks) break;
                 const int st = g % S;
+                const uint4 q0 = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i])
+                                         : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i]);
+                const uint4 q1 = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i])
+                                         : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i]);
+                if (g + kPrefetch < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
                 if (g >= S) {                                      // the MMAs of chunk g - S left stage st
                     if (lane == 0) mbar_wait(bar_done + 8 * st, ((g / S) - 1) & 1, kWaitLimit, &g_batch_timeout);
                     __syncwarp();
                 }
-                const uint32_t* lines = p.codes + ((int64_t)(kc >> 2) * p.R) * 32 + (kc & 3) * kChunkVecs + v;
-                uint8_t* wst = ws + st * kWStageBytes;
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int r = (tid >> 3) + 64 * j;
-                    const int row = tile * kTileRows + r;
-                    uint32_t w = 0u;
-                    float s = 0.f;
-                    if (row < p.R) {
-                        w = __ldg(lines + (int64_t)row * 32);
-                        s = load_scale_at(p, row, kc * kChunkVecs + v);
-                    }
-                    const uint4 q = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, w, lb, s)
-                                            : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, w, lb, s);
-                    *reinterpret_cast<uint4*>(wst + r * 128 + ((v ^ (r & 7)) << 4)) = q;
-                }
-                fence_async_shared();
+                tmem_st8(t_lane + 32u * (uint32_t)st, q0, q1);
+                tmem_st_wait();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar_w + 8 * st);
             }
@@ -207,11 +237,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
                     mbar_wait(bar_w + 8 * st, (g / S) & 1, kWaitLimit, &g_batch_timeout);
                     mbar_wait(bar_x + 8 * st, (g / S) & 1, kWaitLimit, &g_batch_timeout);
                     tc_fence_after();
-                    const uint32_t wa = smem_addr(ws + st * kWStageBytes), xa = smem_addr(xs + st * xstage_bytes);
+                    const uint32_t wa = tmem + a_base + 32u * (uint32_t)st, xa = smem_addr(xs + st * xstage_bytes);
 #pragma unroll
                     for (int ks = 0; ks < kChunk / 16; ++ks)
-                        mma_bf16(tmem + (uint32_t)(acc * p.npad), sw128_desc(wa + 32 * ks), sw128_desc(xa + 32 * ks),
-                                 idesc, kc > kc0 || ks > 0);
+                        mma_bf16_ts(tmem + (uint32_t)(acc * p.npad), wa + 8u * (uint32_t)ks, sw128_desc(xa + 32 * ks),
+                                    idesc, kc > kc0 || ks > 0);
                     mma_commit(bar_done + 8 * st);
                     if (kc + 1 == kc1) mma_commit(bar_accf + 8 * acc);
                     // x of chunk g + S - 1 goes to stage (g + S - 1) % S: still unused when
@@ -333,12 +363,19 @@ int prepare(int* sms) {
     return g_ok[dev] ? RVQ_OK : RVQ_ERR_UNAVAILABLE;
 }
 
-int npad_of(int64_t T) { return T >= kBlockTokens ? kBlockTokens : (int)((T + 15) / 16 * 16); }
+// Tokens per block (the MMA N, a multiple of 16): all of them up to
+// kBlockTokens, else the prompt cut into equal blocks of at most kBlockTokens.
+int npad_of(int64_t T) {
+    const int64_t nb = (T + kBlockTokens - 1) / kBlockTokens;
+    const int64_t per = (T + nb - 1) / nb;
+    return (int)((per + 15) / 16 * 16);
+}
 
 int stages_for(int npad) {
-    const int per = kWStageBytes + npad * 128;
-    int s = (kBudget - 1024 - vdec::kCbBytes - 256) / per;
-    return s > kMaxStages ? kMaxStages : s;
+    int s = (kBudget - 1024 - vdec::kCbBytes - 256) / (npad * 128);
+    s = s > kMaxStages ? kMaxStages : s;
+    while (s > 1 && a_base_of(npad) + 32 * s > 512) --s;
+    return s;
 }
 
 // The balanced split's sizes.  Returns the workspace bytes it needs (two
@@ -434,7 +471,7 @@ int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t worksp
     p.gvdiv = make_fastdiv(gv);
     p.row_scales = gv % (uint32_t)p.G == 0;
     p.rpsdiv = make_fastdiv(p.row_scales ? gv / (uint32_t)p.G : 1u);
-    const size_t smem = 1024 + (size_t)vdec::kCbBytes + (size_t)p.stages * (kWStageBytes + p.npad * 128) + 256;
+    const size_t smem = 1024 + (size_t)vdec::kCbBytes + (size_t)p.stages * p.npad * 128 + 256;
     rvq_gemv_batch_kernel<<<p.n_ctas, kThreads, smem, (cudaStream_t)stream>>>(p);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -124,7 +124,7 @@ def take_batch_timeout() -> bool:
 
 
 class BatchGemvPlan:
-    """``y = x @ W^T`` for ``tokens`` bf16 rows of x (any number; blocks of 256)
+    """``y = x @ W^T`` for ``tokens`` bf16 rows of x (any number; blocks of at most 192)
     with W decoded on chip into the tensor cores' operand (``rvq_gemv_batch``); fixed pointers,
     so a launch can be captured in a CUDA graph.  ``entry["codes_tiled"]``
     (from ``gemv.tile_codes``) is required.  The workspace (split-K partials

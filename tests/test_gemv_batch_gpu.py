@@ -44,10 +44,12 @@ def rel(got, want):
     (333, 520, 5, None, torch.float32),        # ragged rows and a partial last chunk
     (8, 8, 1, 8, torch.float32),               # one vector
     (3000, 1000, 17, 40, torch.float32),       # 5 vectors per scale
-    (200, 512, 256, None, torch.float32),      # 256 tokens: two stages, 512 TMEM columns
-    (1000, 1024, 300, None, torch.float32),    # 300 tokens: a full and a partial token block
+    (200, 512, 256, None, torch.float32),      # 256 tokens: two blocks of 128
+    (1000, 1024, 300, None, torch.float32),    # 300 tokens: two blocks of 160 (the last partial)
+    (640, 512, 192, None, torch.float32),      # 192 tokens: one block, 512 TMEM columns
     (9728, 2560, 2048, None, torch.float16),   # a 2048-token prompt on the gate projection
     (2048, 2560, 8, None, "f32_not_f16"),      # codebook fp16 cannot hold: global fp32 reads
+    (2048, 2560, 8, 128, torch.float16),       # group 128 (the compressor default): 2 chunks per scale
 ])
 def test_batch_matches_bf16_reconstruction(rows, cols, tokens, group, cb_dtype, cuda_device):
     g = torch.Generator().manual_seed(rows * 7 + cols + tokens)
