@@ -50,8 +50,14 @@ using namespace sm100;
 
 constexpr int kDecodeWarps = 16;
 constexpr int kEpiWarps = 4;
-constexpr int kIssuer = kDecodeWarps + kEpiWarps;           // warp index of the issuer
-constexpr int kThreads = (kIssuer + 1) * 32;                 // 672
+constexpr int kIssuer = kDecodeWarps + kEpiWarps;           // warp index of the MMA issuer
+constexpr int kProducer = kIssuer + 1;                       // warp index of the x loader
+constexpr int kThreads = (kProducer + 1) * 32;               // 704
+// Named barrier 2 + s hands TMEM/x stage s to the issuer: decoder warps and the
+// x loader arrive, the issuer waits (no shared-memory polling on that path).
+constexpr int kStageBarThreads = (kDecodeWarps + 2) * 32;
+constexpr int kRedTokens = 16;                               // tokens per step of the split-K reduction
+constexpr int kRedPieces = 1;                                // pieces loaded per round of the reduction
 constexpr int kTileRows = 128;                               // MMA M: weight rows per tile
 constexpr int kChunk = 64;                                   // columns per chunk (one 128-byte swizzle row)
 constexpr int kChunkVecs = kChunk / 8;
@@ -121,16 +127,19 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
     const int xstage_bytes = p.npad * 128;
     uint8_t* xs = base + vdec::kCbBytes;                                     // x stages
     uint64_t* bars = reinterpret_cast<uint64_t*>(xs + p.stages * xstage_bytes);
-    // w_full[S] | x_full[S] | done[S] | acc_full[2] | acc_free[2]
-    const uint32_t bar_w = smem_addr(bars), bar_x = bar_w + 8 * kMaxStages, bar_done = bar_x + 8 * kMaxStages;
+    // x_full[S] | done[S] | acc_full[2] | acc_free[2]
+    const uint32_t bar_x = smem_addr(bars), bar_done = bar_x + 8 * kMaxStages;
     const uint32_t bar_accf = bar_done + 8 * kMaxStages, bar_acce = bar_accf + 16;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kMaxStages + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 4);
     __shared__ int last_piece;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = p.stages;
     const int cta = blockIdx.x;
     const int64_t u_first = range_begin(p, cta), u_last = range_begin(p, cta + 1);
+    const int n_chunks = (int)(u_last - u_first);
+    // the CTA's first chunk: (tile, token block) unit and column chunk
+    const int unit0 = (int)(u_first / p.KC), kc_first = (int)(u_first - (int64_t)unit0 * p.KC);
     // TMEM: two accumulators of npad columns (the epilogue reads 32 columns at a
     // time), then S weight stages of 32 columns (128 rows x 64 bf16)
     const uint32_t a_base = (uint32_t)a_base_of(p.npad);
@@ -138,7 +147,6 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
 
     if (tid == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
-            mbar_init(bar_w + 8 * s, kDecodeWarps);
             mbar_init(bar_x + 8 * s, 1);
             mbar_init(bar_done + 8 * s, 1);
         }
@@ -149,110 +157,146 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         mbar_init_fence();
     }
     if (warp == 0) tmem_alloc(smem_addr(tmem_slot), tmem_cols);
-    const bool cb_smem = vdec::stage_cb8(p.cb, p.cb_kind, cbs, tid, kThreads);   // ends with a barrier
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();                                                         // barriers initialised
+
+    // ---- x loader: chunk g's x into stage g % S (for g >= S once the MMAs of
+    // chunk g - S are done); once it has landed, arrive on the stage barrier
+    int x_st = 0, x_ph = 0, x_blk = unit0 % p.blocks, x_kc = kc_first;
+    auto load_x = [&](int st) {
+        mbar_expect_tx(bar_x + 8 * st, (uint32_t)xstage_bytes);
+        tma_load_2d(smem_addr(xs + st * xstage_bytes), &p.xmap, x_kc * kChunk, x_blk * p.npad, bar_x + 8 * st);
+        if (++x_kc == p.KC) {
+            x_kc = 0;
+            if (++x_blk == p.blocks) x_blk = 0;
+        }
+    };
+    if (warp == kProducer && lane == 0)
+        for (int g = 0; g < S && g < n_chunks; ++g) load_x(g);
+
+    // ---- decoders: warp w owns TMEM lanes 32 (w % 4) .. + 31 (tile rows) and
+    // vectors 2 (w / 4), 2 (w / 4) + 1 of every chunk; thread = one row.  Code
+    // words and scales are fetched kPrefetch chunks ahead (the first ones
+    // before the codebook is staged); a per-row scale is read once per tile.
+    const int quarter = warp & 3, vp = (warp >> 2) & 3;
+    const int r = 32 * quarter + lane;
+    int f_tile = unit0 / p.blocks, f_blk = unit0 % p.blocks, f_kc = kc_first;
+    int s_tile = -1;
+    float s_row = 0.f;
+    uint2 cw[kPrefetch];
+    float cs0[kPrefetch], cs1[kPrefetch];
+    auto fetch = [&](uint2& w, float& s0, float& s1) {
+        const int row = f_tile * kTileRows + r;
+        w = make_uint2(0u, 0u);
+        s0 = s1 = 0.f;
+        if (row < p.R) {
+            const uint32_t* line = p.codes + ((int64_t)(f_kc >> 2) * p.R + row) * 32 + (f_kc & 3) * kChunkVecs;
+            w = __ldg(reinterpret_cast<const uint2*>(line) + vp);
+            if (p.row_scales) {
+                if (f_tile != s_tile) {
+                    s_tile = f_tile;
+                    s_row = load_as_f32(p.scales, fastdiv((uint32_t)row, p.rpsdiv), p.scale_kind);
+                }
+                s0 = s1 = s_row;
+            } else {
+                s0 = load_scale_at(p, row, f_kc * kChunkVecs + 2 * vp);
+                s1 = load_scale_at(p, row, f_kc * kChunkVecs + 2 * vp + 1);
+            }
+        }
+        if (++f_kc == p.KC) {
+            f_kc = 0;
+            if (++f_blk == p.blocks) {
+                f_blk = 0;
+                ++f_tile;
+            }
+        }
+    };
+    if (warp < kDecodeWarps) {
+#pragma unroll
+        for (int i = 0; i < kPrefetch; ++i)
+            if (i < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
+    }
+
+    const bool cb_smem = vdec::stage_cb8(p.cb, p.cb_kind, cbs, tid, kThreads);   // ends with a barrier
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
     if (warp < kDecodeWarps) {
-        // ---- decoders: warp w owns TMEM lanes 32 (w % 4) .. + 31 (tile rows) and
-        // vectors 2 (w / 4), 2 (w / 4) + 1 of every chunk; thread = one row.
-        // Code words and scales are fetched kPrefetch chunks ahead.
+        // Each chunk: decode into registers, wait until the MMAs of chunk g - S
+        // have left TMEM stage g % S, store, arrive on the stage barrier.
         uint32_t lb[4];
         vdec::lane_bits(lane, lb);
-        const int quarter = warp & 3, vp = warp >> 2;
-        const int r = 32 * quarter + lane;
-        const int n_chunks = (int)(u_last - u_first);
         const uint32_t t_lane = tmem + ((uint32_t)(32 * quarter) << 16) + a_base + 8u * (uint32_t)vp;
-        int f_unit = (int)(u_first / p.KC), f_kc = (int)(u_first - (int64_t)f_unit * p.KC);
-        uint2 cw[kPrefetch];
-        float cs0[kPrefetch], cs1[kPrefetch];
-        // fetch the next chunk in CTA order into ring slot i
-        auto fetch = [&](uint2& w, float& s0, float& s1) {
-            const int row = (f_unit / p.blocks) * kTileRows + r;
-            w = make_uint2(0u, 0u);
-            s0 = s1 = 0.f;
-            if (row < p.R) {
-                const uint32_t* line = p.codes + ((int64_t)(f_kc >> 2) * p.R + row) * 32 + (f_kc & 3) * kChunkVecs;
-                w = __ldg(reinterpret_cast<const uint2*>(line) + vp);
-                s0 = load_scale_at(p, row, f_kc * kChunkVecs + 2 * vp);
-                s1 = load_scale_at(p, row, f_kc * kChunkVecs + 2 * vp + 1);
-            }
-            if (++f_kc == p.KC) {
-                f_kc = 0;
-                ++f_unit;
-            }
-        };
-#pragma unroll
-        for (int i = 0; i < kPrefetch; ++i)
-            if (i < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
+        int st = 0, ph = 0;
         for (int g0 = 0; g0 < n_chunks; g0 += kPrefetch) {
 #pragma unroll
             for (int i = 0; i < kPrefetch; ++i) {
                 const int g = g0 + i;
                 if (g >= n_chunks) break;
-                const int st = g % S;
                 const uint4 q0 = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i])
                                          : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i]);
                 const uint4 q1 = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i])
                                          : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i]);
                 if (g + kPrefetch < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
                 if (g >= S) {                                      // the MMAs of chunk g - S left stage st
-                    if (lane == 0) mbar_wait(bar_done + 8 * st, ((g / S) - 1) & 1, kWaitLimit, &g_batch_timeout);
+                    if (lane == 0) mbar_wait(bar_done + 8 * st, ph ^ 1, kWaitLimit, &g_batch_timeout);
                     __syncwarp();
                 }
                 tmem_st8(t_lane + 32u * (uint32_t)st, q0, q1);
                 tmem_st_wait();
                 tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar_w + 8 * st);
-            }
-        }
-    } else if (warp == kIssuer) {
-        // ---- issuer: x by TMA (S - 1 chunks ahead), MMAs once a chunk's weights are decoded
-        if (lane == 0) {
-            const uint32_t idesc = instr_desc_bf16(kTileRows, p.npad);
-            // x of the CTA's chunk number g (unit u_first + g): column chunk and token block
-            auto load_x = [&](int g) {
-                const int64_t u = u_first + g;
-                if (u >= u_last) return;
-                const int unit = (int)(u / p.KC), kc = (int)(u - (int64_t)unit * p.KC), blk = unit % p.blocks;
-                const int st = g % S;
-                mbar_expect_tx(bar_x + 8 * st, (uint32_t)xstage_bytes);
-                tma_load_2d(smem_addr(xs + st * xstage_bytes), &p.xmap, kc * kChunk, blk * p.npad, bar_x + 8 * st);
-            };
-            for (int g = 0; g < S - 1; ++g) load_x(g);
-            int g = 0, n_seg = 0;
-            for (int64_t u = u_first; u < u_last; ++n_seg) {
-                const Seg sg = seg_at(p, u, u_last);
-                u += sg.kc1 - sg.kc0;
-                const int acc = n_seg & 1;
-                if (n_seg >= 2)                                    // the epilogue has read this accumulator
-                    mbar_wait(bar_acce + 8 * acc, ((n_seg >> 1) - 1) & 1, kWaitLimit, &g_batch_timeout);
-                tc_fence_after();
-                const int kc0 = sg.kc0, kc1 = sg.kc1;
-                for (int kc = kc0; kc < kc1; ++kc, ++g) {
-                    const int st = g % S;
-                    mbar_wait(bar_w + 8 * st, (g / S) & 1, kWaitLimit, &g_batch_timeout);
-                    mbar_wait(bar_x + 8 * st, (g / S) & 1, kWaitLimit, &g_batch_timeout);
-                    tc_fence_after();
-                    const uint32_t wa = tmem + a_base + 32u * (uint32_t)st, xa = smem_addr(xs + st * xstage_bytes);
-#pragma unroll
-                    for (int ks = 0; ks < kChunk / 16; ++ks)
-                        mma_bf16_ts(tmem + (uint32_t)(acc * p.npad), wa + 8u * (uint32_t)ks, sw128_desc(xa + 32 * ks),
-                                    idesc, kc > kc0 || ks > 0);
-                    mma_commit(bar_done + 8 * st);
-                    if (kc + 1 == kc1) mma_commit(bar_accf + 8 * acc);
-                    // x of chunk g + S - 1 goes to stage (g + S - 1) % S: still unused when
-                    // g = 0, else chunk g - 1's, once its MMAs are done
-                    if (g >= 1)
-                        mbar_wait(bar_done + 8 * ((g - 1) % S), ((g - 1) / S) & 1, kWaitLimit, &g_batch_timeout);
-                    load_x(g + S - 1);
+                named_arrive(2 + st, kStageBarThreads);
+                if (++st == S) {
+                    st = 0;
+                    ph ^= 1;
                 }
             }
         }
-        __syncwarp();
+    } else if (warp == kIssuer) {
+        // ---- MMA issuer: once stage g % S holds chunk g's weights and x, four
+        // MMAs into the segment's accumulator, committed to done[g % S]
+        const uint32_t idesc = instr_desc_bf16(kTileRows, p.npad);
+        int st = 0, n_seg = 0;
+        for (int64_t u = u_first; u < u_last; ++n_seg) {
+            const Seg sg = seg_at(p, u, u_last);
+            u += sg.kc1 - sg.kc0;
+            const int acc = n_seg & 1;
+            if (n_seg >= 2) {                                      // the epilogue has read this accumulator
+                if (lane == 0) mbar_wait(bar_acce + 8 * acc, ((n_seg >> 1) - 1) & 1, kWaitLimit, &g_batch_timeout);
+                __syncwarp();
+            }
+            const uint32_t d = tmem + (uint32_t)(acc * p.npad);
+            for (int kc = sg.kc0; kc < sg.kc1; ++kc) {
+                named_sync(2 + st, kStageBarThreads);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t wa = tmem + a_base + 32u * (uint32_t)st, xa = smem_addr(xs + st * xstage_bytes);
+#pragma unroll
+                    for (int ks = 0; ks < kChunk / 16; ++ks)
+                        mma_bf16_ts(d, wa + 8u * (uint32_t)ks, sw128_desc(xa + 32 * ks), idesc, kc > sg.kc0 || ks > 0);
+                    mma_commit(bar_done + 8 * st);
+                    if (kc + 1 == sg.kc1) mma_commit(bar_accf + 8 * acc);
+                }
+                __syncwarp();
+                if (++st == S) st = 0;
+            }
+        }
+    } else if (warp == kProducer) {
+        for (int g = 0; g < n_chunks; ++g) {
+            if (lane == 0) {
+                if (g >= S) {                                      // stage free: the MMAs of chunk g - S are done
+                    mbar_wait(bar_done + 8 * x_st, x_ph ^ 1, kWaitLimit, &g_batch_timeout);
+                    load_x(x_st);
+                }
+                mbar_wait(bar_x + 8 * x_st, x_ph, kWaitLimit, &g_batch_timeout);
+            }
+            __syncwarp();
+            named_arrive(2 + x_st, kStageBarThreads);
+            if (++x_st == S) {
+                x_st = 0;
+                x_ph ^= 1;
+            }
+        }
     } else {
         // ---- epilogue warps: warp e reads TMEM lanes 32 e .. 32 e + 31 (tile rows)
         const int e = warp - kDecodeWarps;
@@ -268,16 +312,17 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
             const int64_t ubase = (int64_t)sg.unit * p.KC;
             const int cf = cta_of(p, ubase), np = cta_of(p, ubase + p.KC - 1) - cf + 1;
             const int row = tile * kTileRows + r;
-            if (lane == 0) mbar_wait(bar_accf + 8 * acc, (n_seg >> 1) & 1, kWaitLimit, &g_batch_timeout);
+            if (lane == 0) mbar_wait_sleep(bar_accf + 8 * acc, (n_seg >> 1) & 1, kWaitLimit, &g_batch_timeout);
             __syncwarp();
             tc_fence_after();
-            float* part = p.part + ((int64_t)(2 * cta + (n_seg ? 1 : 0)) * p.npad) * kTileRows + r;
+            // partials: [slot][128 rows][npad] fp32, a row's tokens contiguous
+            float* part = p.part + ((int64_t)(2 * cta + (n_seg ? 1 : 0)) * kTileRows + r) * p.npad;
             for (int c0 = 0; c0 < p.npad; c0 += 32) {
                 uint32_t vals[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * e) << 16) + (uint32_t)(acc * p.npad + c0), vals);
                 tmem_ld_wait();
-                const int tn = min(32, nt - c0);
                 if (np == 1) {
+                    const int tn = min(32, nt - c0);
                     if (row < p.R) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
@@ -285,16 +330,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
                                 p.y[(int64_t)(t0 + c0 + i) * p.R + row] = __float2bfloat16_rn(__uint_as_float(vals[i]));
                     }
                 } else {
+                    const int nw = min(32, p.npad - c0);                 // a multiple of 16
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (i < tn) part[(int64_t)(c0 + i) * kTileRows] = __uint_as_float(vals[i]);
+                    for (int i = 0; i < 32; i += 4)
+                        if (i < nw)
+                            __stcg(reinterpret_cast<float4*>(part + c0 + i),
+                                   make_float4(__uint_as_float(vals[i]), __uint_as_float(vals[i + 1]),
+                                               __uint_as_float(vals[i + 2]), __uint_as_float(vals[i + 3])));
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_acce + 8 * acc);
             if (np > 1) {
-                // the CTA that finishes the tile's last piece adds the pieces in piece order
+                // the CTA that finishes the unit's last piece adds the pieces in piece order
                 __threadfence();
                 asm volatile("bar.sync 1, %0;\n" ::"n"(kEpiWarps * 32) : "memory");
                 if (e == 0 && lane == 0) last_piece = atomicAdd(&p.tickets[sg.unit], 1u) == (uint32_t)(np - 1);
@@ -304,13 +353,47 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
                     // piece 0 is CTA cf's last segment unless cf's range starts at this unit;
                     // piece q > 0 is the first segment of CTA cf + q
                     const int slot0 = 2 * cf + (range_begin(p, cf) == ubase ? 0 : 1);
-                    const float* base_p = p.part + r;
                     if (row < p.R) {
-                        for (int t = 0; t < nt; ++t) {
-                            float sum = __ldcg(base_p + ((int64_t)slot0 * p.npad + t) * kTileRows);
-                            for (int q = 1; q < np; ++q)
-                                sum += __ldcg(base_p + ((int64_t)(2 * (cf + q)) * p.npad + t) * kTileRows);
-                            p.y[(int64_t)(t0 + t) * p.R + row] = __float2bfloat16_rn(sum);
+                        for (int tb = 0; tb < nt; tb += kRedTokens) {
+                            // kRedTokens tokens of kRedPieces pieces in flight at once
+                            float4 sum[kRedTokens / 4];
+                            const float4* s0 = reinterpret_cast<const float4*>(
+                                p.part + ((int64_t)slot0 * kTileRows + r) * p.npad + tb);
+#pragma unroll
+                            for (int j = 0; j < kRedTokens / 4; ++j) sum[j] = __ldcg(s0 + j);
+                            for (int q0 = 1; q0 < np; q0 += kRedPieces) {
+                                float4 v[kRedPieces][kRedTokens / 4];
+#pragma unroll
+                                for (int qq = 0; qq < kRedPieces; ++qq) {
+                                    if (q0 + qq < np) {
+                                        const float4* sq = reinterpret_cast<const float4*>(
+                                            p.part + ((int64_t)(2 * (cf + q0 + qq)) * kTileRows + r) * p.npad + tb);
+#pragma unroll
+                                        for (int j = 0; j < kRedTokens / 4; ++j) v[qq][j] = __ldcg(sq + j);
+                                    }
+                                }
+#pragma unroll
+                                for (int qq = 0; qq < kRedPieces; ++qq) {
+                                    if (q0 + qq < np) {
+#pragma unroll
+                                        for (int j = 0; j < kRedTokens / 4; ++j) {
+                                            sum[j].x += v[qq][j].x;
+                                            sum[j].y += v[qq][j].y;
+                                            sum[j].z += v[qq][j].z;
+                                            sum[j].w += v[qq][j].w;
+                                        }
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int j = 0; j < kRedTokens / 4; ++j) {
+                                const float f[4] = {sum[j].x, sum[j].y, sum[j].z, sum[j].w};
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const int t = tb + 4 * j + k;
+                                    if (t < nt) p.y[(int64_t)(t0 + t) * p.R + row] = __float2bfloat16_rn(f[k]);
+                                }
+                            }
                         }
                     }
                     if (e == 0 && lane == 0) p.tickets[sg.unit] = 0u;  // ready for the next launch

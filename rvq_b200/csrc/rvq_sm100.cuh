@@ -38,6 +38,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long lo
     return false;
 }
 
+// The same for a warp that waits long (a whole segment): it sleeps between
+// polls, leaving issue slots to the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, long long limit, int* flag) {
+    for (long long i = 0; i < limit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(200);
+    }
+    atomicExch(flag, 1);
+    return false;
+}
+
+// Hardware named barriers (ids 1..15) between a subset of the CTA's warps: a
+// whole warp arrives without waiting, or arrives and waits for `count` threads.
+__device__ __forceinline__ void named_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
@@ -114,6 +134,16 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint4& a, const u
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(taddr), "r"(a.x),
         "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+        : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (32x32b shape).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint4 (&q)[4]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};\n" ::"r"(taddr),
+        "r"(q[0].x), "r"(q[0].y), "r"(q[0].z), "r"(q[0].w), "r"(q[1].x), "r"(q[1].y), "r"(q[1].z), "r"(q[1].w),
+        "r"(q[2].x), "r"(q[2].y), "r"(q[2].z), "r"(q[2].w), "r"(q[3].x), "r"(q[3].y), "r"(q[3].z), "r"(q[3].w)
         : "memory");
 }
 

@@ -31,37 +31,64 @@ __device__ __forceinline__ void lane_bits(int lane, uint32_t (&lb)[kStages]) {
         lb[k] = ((uint32_t)(k & 1) << 7) | ((uint32_t)(lane & 7) << 4) | ((uint32_t)(k >> 1) << 16);
 }
 
+// Load codebook entry e (8 values): returned as is for an fp16 codebook, else
+// into f as fp32.
+__device__ __forceinline__ uint4 cb_entry_f16(const void* cb, int cb_kind, int e, float (&f)[8]) {
+    if (cb_kind == RVQ_F16) return __ldg(reinterpret_cast<const uint4*>(cb) + e);
+    if (cb_kind == RVQ_F32) {                            // 32-byte entries: two 16-byte loads
+        const float4 a = __ldg(reinterpret_cast<const float4*>(cb) + 2 * e);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(cb) + 2 * e + 1);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) f[t] = load_as_f32(cb, (int64_t)e * 8 + t, cb_kind);
+    }
+    return make_uint4(0u, 0u, 0u, 0u);
+}
+
+// fp16 form of a loaded entry (fp32 values f, or q itself for an fp16 codebook);
+// sets *inexact when a value is not an exact fp16 number.
+__device__ __forceinline__ uint4 cb_entry_pack(int cb_kind, const uint4& q, const float (&f)[8], int* inexact) {
+    if (cb_kind == RVQ_F16) return q;
+    uint32_t w[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const float f0 = f[2 * t], f1 = f[2 * t + 1];
+        const __half2 h = __floats2half2_rn(f0, f1);
+        *inexact |= (__float_as_uint(__low2float(h)) != __float_as_uint(f0)) |
+                    (__float_as_uint(__high2float(h)) != __float_as_uint(f1)) | isnan(f0) | isnan(f1);
+        w[t] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void cb_entry_store(char* cbs, int e, int lane, const uint4& q) {
+    char* base = cbs + ((e >> 9) << 16) + ((e & 255) << 8) + (((e >> 8) & 1) << 7);
+#pragma unroll
+    for (int i = 0; i < kCopies; ++i) {
+        const int cp = (i + lane) & (kCopies - 1);
+        *reinterpret_cast<uint4*>(base + cp * 16) = q;
+    }
+}
+
 // Stage the [4][256][8] codebook (fp32, fp16 or bf16 kind) into `cbs` as fp16
 // with 8 copies; all `nthreads` threads of the CTA call it (thread index
 // `tid`).  Returns true if every value is an exact fp16 number (false: the
-// caller reads the codebook from global memory instead).  Ends with a
-// CTA-wide barrier.
+// caller reads the codebook from global memory instead).  Each thread loads
+// two entries before converting and storing them (one memory round trip when
+// nthreads >= 512).  Ends with a CTA-wide barrier.
 __device__ __forceinline__ bool stage_cb8(const void* cb, int cb_kind, char* cbs, int tid, int nthreads) {
     const int lane = tid & 31;
     int inexact = 0;
-    for (int e = tid; e < kStages * kCodes; e += nthreads) {
-        uint4 q;
-        if (cb_kind == RVQ_F16) {
-            q = __ldg(reinterpret_cast<const uint4*>(cb) + e);
-        } else {
-            uint32_t w[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const float f0 = load_as_f32(cb, (int64_t)e * 8 + 2 * t, cb_kind);
-                const float f1 = load_as_f32(cb, (int64_t)e * 8 + 2 * t + 1, cb_kind);
-                const __half2 h = __floats2half2_rn(f0, f1);
-                inexact |= (__float_as_uint(__low2float(h)) != __float_as_uint(f0)) |
-                           (__float_as_uint(__high2float(h)) != __float_as_uint(f1)) | isnan(f0) | isnan(f1);
-                w[t] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-            q = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        char* base = cbs + ((e >> 9) << 16) + ((e & 255) << 8) + (((e >> 8) & 1) << 7);
-#pragma unroll
-        for (int i = 0; i < kCopies; ++i) {
-            const int cp = (i + lane) & (kCopies - 1);
-            *reinterpret_cast<uint4*>(base + cp * 16) = q;
-        }
+    for (int e0 = tid; e0 < kStages * kCodes; e0 += 2 * nthreads) {
+        const int e1 = e0 + nthreads;
+        const bool has1 = e1 < kStages * kCodes;
+        float f0[8], f1[8];
+        const uint4 q0 = cb_entry_f16(cb, cb_kind, e0, f0);
+        uint4 q1 = make_uint4(0u, 0u, 0u, 0u);
+        if (has1) q1 = cb_entry_f16(cb, cb_kind, e1, f1);
+        cb_entry_store(cbs, e0, lane, cb_entry_pack(cb_kind, q0, f0, &inexact));
+        if (has1) cb_entry_store(cbs, e1, lane, cb_entry_pack(cb_kind, q1, f1, &inexact));
     }
     return !__syncthreads_or(inexact);
 }
