@@ -38,6 +38,7 @@
 
 #include <mutex>
 #include <string.h>
+#include <type_traits>
 
 #include "rvq_common.cuh"
 #include "rvq_sm100.cuh"
@@ -62,7 +63,7 @@ constexpr int kTileRows = 128;                               // MMA M: weight ro
 constexpr int kChunk = 64;                                   // columns per chunk (one 128-byte swizzle row)
 constexpr int kChunkVecs = kChunk / 8;
 constexpr int kMaxStages = 4;
-constexpr int kPrefetch = 4;                                 // chunks of codes and scales in flight per decoder
+constexpr int kPrefetch = 2;                                 // chunks of codes and scales in flight per decoder
 constexpr int kBlockTokens = 192;                            // MMA N per token block (max)
 constexpr int kMaxTokens = 65536;
 constexpr long long kWaitLimit = 1ll << 24;
@@ -223,35 +224,40 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
 
     if (warp < kDecodeWarps) {
         // Each chunk: decode into registers, wait until the MMAs of chunk g - S
-        // have left TMEM stage g % S, store, arrive on the stage barrier.
+        // have left TMEM stage g % S, store, arrive on the stage barrier.  One
+        // loop per codebook source (shared memory, or global for a codebook
+        // fp16 cannot hold), so the hot loop holds a single decode path.
         uint32_t lb[4];
         vdec::lane_bits(lane, lb);
         const uint32_t t_lane = tmem + ((uint32_t)(32 * quarter) << 16) + a_base + 8u * (uint32_t)vp;
-        int st = 0, ph = 0;
-        for (int g0 = 0; g0 < n_chunks; g0 += kPrefetch) {
+        auto decode_loop = [&](auto smem_tag) {
+            constexpr bool kSmem = decltype(smem_tag)::value;
+            int st = 0, ph = 0;
+            for (int g0 = 0; g0 < n_chunks; g0 += kPrefetch) {
 #pragma unroll
-            for (int i = 0; i < kPrefetch; ++i) {
-                const int g = g0 + i;
-                if (g >= n_chunks) break;
-                const uint4 q0 = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i])
-                                         : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i]);
-                const uint4 q1 = cb_smem ? vdec::weights_bf16<true>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i])
-                                         : vdec::weights_bf16<false>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i]);
-                if (g + kPrefetch < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
-                if (g >= S) {                                      // the MMAs of chunk g - S left stage st
-                    if (lane == 0) mbar_wait(bar_done + 8 * st, ph ^ 1, kWaitLimit, &g_batch_timeout);
-                    __syncwarp();
-                }
-                tmem_st8(t_lane + 32u * (uint32_t)st, q0, q1);
-                tmem_st_wait();
-                tc_fence_before();
-                named_arrive(2 + st, kStageBarThreads);
-                if (++st == S) {
-                    st = 0;
-                    ph ^= 1;
+                for (int i = 0; i < kPrefetch; ++i) {
+                    const int g = g0 + i;
+                    if (g >= n_chunks) break;
+                    const uint4 q0 = vdec::weights_bf16<kSmem>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i]);
+                    const uint4 q1 = vdec::weights_bf16<kSmem>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i]);
+                    if (g + kPrefetch < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
+                    if (g >= S) {                                  // the MMAs of chunk g - S left stage st
+                        if (lane == 0) mbar_wait(bar_done + 8 * st, ph ^ 1, kWaitLimit, &g_batch_timeout);
+                        __syncwarp();
+                    }
+                    tmem_st8(t_lane + 32u * (uint32_t)st, q0, q1);
+                    tmem_st_wait();
+                    tc_fence_before();
+                    named_arrive(2 + st, kStageBarThreads);
+                    if (++st == S) {
+                        st = 0;
+                        ph ^= 1;
+                    }
                 }
             }
-        }
+        };
+        if (cb_smem) decode_loop(std::integral_constant<bool, true>{});
+        else decode_loop(std::integral_constant<bool, false>{});
     } else if (warp == kIssuer) {
         // ---- MMA issuer: once stage g % S holds chunk g's weights and x, four
         // MMAs into the segment's accumulator, committed to done[g % S]
