@@ -392,16 +392,20 @@ int rvq_tile_codes(const void* planes, int64_t stage_stride, int64_t rows, int64
  * counterpart in the reference, which reconstructs W into the slot and calls
  * F.linear: infer_compressed_layerwise_triton.py:263, 290-292):
  *   y[t][r] = bf16( sum_c x[t][c] * W[r][c] ),  t < tokens (1..65536)
- * W is rebuilt bit-identically to rvq_decode's bf16 slot values straight into
- * tensor memory as the A operand of tcgen05.mma (M = 128 weight rows, N = a
- * block of up to 192 tokens, fp32 accumulation in TMEM); only the codes,
- * scales and x are read from HBM.  More than 192 tokens run as equal blocks
- * of at most 192, each weight chunk decoded once per block.  A job of 2^31 or more (row
- * tile, token block, 64-column chunk) units returns RVQ_ERR_TOO_LARGE.  W:
- * K=4 stages, 256 codes, uint8 codes in the tile-major layout of rvq_tile_codes (weight.indices, 16-byte aligned), no
- * tail; codebook fp32, fp16 or bf16.  x bf16 [tokens][cols] row-major, 16-byte
- * aligned, cols a multiple of 8; y bf16 [tokens][rows].  Deterministic: split-K
- * pieces are added in a fixed order. */
+ * W is rebuilt on chip straight into tensor memory as the A operand of
+ * tcgen05.mma (M = 128 weight rows, N = a block of up to 192 tokens, fp32
+ * accumulation in TMEM); only the codes, scales and x are read from HBM.
+ * More than 192 tokens run as equal blocks of at most 192, each weight chunk
+ * decoded once per block.
+ * exact != 0: every weight is bit-identical to rvq_decode's bf16 slot value;
+ * exact == 0: the four fp16 codewords are summed in fp16, then widened to
+ * fp32, scaled and rounded to bf16 (a codebook fp16 cannot hold always takes
+ * the exact path).  A job of 2^31 or more (row tile, token block, 64-column
+ * chunk) units returns RVQ_ERR_TOO_LARGE.  W: K=4 stages, 256 codes, uint8
+ * codes in the tile-major layout of rvq_tile_codes (weight.indices, 16-byte
+ * aligned), no tail; codebook fp32, fp16 or bf16.  x bf16 [tokens][cols]
+ * row-major, 16-byte aligned, cols a multiple of 8; y bf16 [tokens][rows].
+ * Deterministic: split-K pieces are added in a fixed order. */
 typedef struct rvq_gemv_batch_job {
     rvq_entry weight;         /* weight.out is ignored */
     const void* x;            /* device, [tokens][cols] */
@@ -411,6 +415,8 @@ typedef struct rvq_gemv_batch_job {
     int64_t tokens;
     int32_t x_kind;           /* RVQ_BF16 */
     int32_t y_kind;           /* RVQ_BF16 */
+    int32_t exact;            /* 1: bit-exact bf16 weights; 0: fp16 stage sums */
+    int32_t reserved;         /* 0 */
 } rvq_gemv_batch_job;
 
 /* Bytes of workspace rvq_gemv_batch needs for this job on the current device

@@ -9,8 +9,9 @@ between uses):
 
 * ``fused``:  rvq_gemv / rvq_gemv_tiles (batch 1, table GEMV) and
   rvq_gemv_tiles_exact (bit-exact bf16 weights), W never materialised;
-* ``fused_tc``: rvq_gemv_batch, W decoded bit-exactly into tensor memory as
-  the tcgen05 MMA's A operand (every batch size, and the 2048-token prefill);
+* ``fused_tc``: rvq_gemv_batch, W decoded into tensor memory as the tcgen05
+  MMA's A operand (every batch size, and the 2048-token prefill); fp16 stage
+  sums, and ``fused_tc_exact`` with bit-exact bf16 weights;
 * ``decode+gemm``: rvq_decode_layer into a bf16 slot, then torch.matmul
   (cuBLAS) -- the reference's dataflow (infer_compressed_layerwise_triton.py:
   263, 290-292);
@@ -138,14 +139,16 @@ def run(reps: int = 200, device="cuda:0", batches=(1, 8, 64, 2048), only=None):
 
         r = reps if b < 2048 else max(20, reps // 10)
         flops = 2.0 * b * ROWS * COLS
-        if want(f"fused_tc_b{b}"):
-            # the tensor-core fused GEMM (W decoded on chip, never to HBM)
-            y_fb = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)
-            bplans = [BatchGemvPlan(c, cbd, x, y_fb) for c in tl]
-            t_fb = _time(lambda i: bplans[i % COPIES].launch(), r, stream)
-            out["results"][f"fused_tc_b{b}"] = {"us": round(t_fb, 2), "TFLOP/s": round(flops / t_fb / 1e6, 2),
-                                                "GB/s": round((code_bytes + b * (COLS + ROWS) * 2) / t_fb / 1e3, 1)}
-            del bplans
+        for exact in (False, True):
+            name = f"fused_tc{'_exact' if exact else ''}_b{b}"
+            if want(name):
+                # the tensor-core fused GEMM (W decoded on chip, never to HBM)
+                y_fb = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)
+                bplans = [BatchGemvPlan(c, cbd, x, y_fb, exact=exact) for c in tl]
+                t_fb = _time(lambda i: bplans[i % COPIES].launch(), r, stream)
+                out["results"][name] = {"us": round(t_fb, 2), "TFLOP/s": round(flops / t_fb / 1e6, 2),
+                                        "GB/s": round((code_bytes + b * (COLS + ROWS) * 2) / t_fb / 1e3, 1)}
+                del bplans
         if b >= 64 and want(f"fused_gemm_b{b}"):
             # prefill-style: weight decoded into shared memory feeding tcgen05 MMAs
             y_fg = torch.empty(b, ROWS, dtype=torch.bfloat16, device=device)

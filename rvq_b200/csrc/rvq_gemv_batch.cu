@@ -32,6 +32,9 @@
 // CTA write y directly.
 //
 // Only the codes (0.5 B per weight), the scales and x are read from HBM.
+//
+// exact = 0 decodes the weights with fp16 stage sums (weights_bf16_fast)
+// instead of the bit-exact fp32 chain.
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -82,6 +85,7 @@ struct BParams {
     int64_t U;                // (tile, token block, chunk) units
     int32_t R, G, T, npad, blocks, KC, stages, n_ctas;
     int32_t cb_kind, scale_kind, row_scales;
+    int32_t exact;            // 1: bit-exact bf16 weights, 0: fp16 stage sums
     FastDiv gvdiv, rpsdiv;
 };
 
@@ -230,16 +234,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
         uint32_t lb[4];
         vdec::lane_bits(lane, lb);
         const uint32_t t_lane = tmem + ((uint32_t)(32 * quarter) << 16) + a_base + 8u * (uint32_t)vp;
-        auto decode_loop = [&](auto smem_tag) {
-            constexpr bool kSmem = decltype(smem_tag)::value;
+        auto decode_loop = [&](auto mode_tag) {
+            constexpr int kMode = decltype(mode_tag)::value;     // 0 fast, 1 exact, 2 exact from global
+            auto decode = [&](uint32_t w, float s) -> uint4 {
+                if (kMode == 0) return vdec::weights_bf16_fast(cbs, w, lb, s);
+                return vdec::weights_bf16<kMode == 1>(cbs, p.cb, p.cb_kind, w, lb, s);
+            };
             int st = 0, ph = 0;
             for (int g0 = 0; g0 < n_chunks; g0 += kPrefetch) {
 #pragma unroll
                 for (int i = 0; i < kPrefetch; ++i) {
                     const int g = g0 + i;
                     if (g >= n_chunks) break;
-                    const uint4 q0 = vdec::weights_bf16<kSmem>(cbs, p.cb, p.cb_kind, cw[i].x, lb, cs0[i]);
-                    const uint4 q1 = vdec::weights_bf16<kSmem>(cbs, p.cb, p.cb_kind, cw[i].y, lb, cs1[i]);
+                    const uint4 q0 = decode(cw[i].x, cs0[i]);
+                    const uint4 q1 = decode(cw[i].y, cs1[i]);
                     if (g + kPrefetch < n_chunks) fetch(cw[i], cs0[i], cs1[i]);
                     if (g >= S) {                                  // the MMAs of chunk g - S left stage st
                         if (lane == 0) mbar_wait(bar_done + 8 * st, ph ^ 1, kWaitLimit, &g_batch_timeout);
@@ -256,8 +264,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemv_batch_kernel(const __gri
                 }
             }
         };
-        if (cb_smem) decode_loop(std::integral_constant<bool, true>{});
-        else decode_loop(std::integral_constant<bool, false>{});
+        if (!cb_smem) decode_loop(std::integral_constant<int, 2>{});
+        else if (p.exact) decode_loop(std::integral_constant<int, 1>{});
+        else decode_loop(std::integral_constant<int, 0>{});
     } else if (warp == kIssuer) {
         // ---- MMA issuer: once stage g % S holds chunk g's weights and x, four
         // MMAs into the segment's accumulator, committed to done[g % S]
@@ -556,6 +565,7 @@ int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t worksp
     p.T = (int32_t)job->tokens;
     p.cb_kind = w.codebook_kind;
     p.scale_kind = w.scale_kind;
+    p.exact = job->exact ? 1 : 0;
     const uint32_t gv = (uint32_t)w.group_vecs;
     p.gvdiv = make_fastdiv(gv);
     p.row_scales = gv % (uint32_t)p.G == 0;

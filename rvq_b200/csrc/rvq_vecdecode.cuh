@@ -128,5 +128,39 @@ __device__ __forceinline__ uint4 weights_bf16(const char* cbs, const void* cb, i
     return r;
 }
 
+// Faster form for consumers that need y within a tolerance, not bit-exact
+// weights: ((c0 + c1) + c2) + c3 summed in fp16 (three packed add.rn.f16x2
+// per pair), widened to fp32, scaled and rounded to bf16 -- 20 instead of 32
+// arithmetic instructions per vector; each weight is within a few fp16 ulps
+// of the exact sum before the bf16 rounding.  Codebook staged by stage_cb8.
+// SCALE false leaves the scale to the caller (a per-row scale applied to y).
+template <bool SCALE = true>
+__device__ __forceinline__ uint4 weights_bf16_fast(const char* cbs, uint32_t w, const uint32_t (&lb)[kStages],
+                                                   float s) {
+    uint4 q[kStages];
+#pragma unroll
+    for (int k = 0; k < kStages; ++k)
+        q[k] = *reinterpret_cast<const uint4*>(cbs + __byte_perm(w, lb[k], 0x7604 | (k << 4)));
+    const uint32_t* a = reinterpret_cast<const uint32_t*>(&q[0]);
+    const uint32_t* b = reinterpret_cast<const uint32_t*>(&q[1]);
+    const uint32_t* c = reinterpret_cast<const uint32_t*>(&q[2]);
+    const uint32_t* d = reinterpret_cast<const uint32_t*>(&q[3]);
+    uint32_t out[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t h;
+        asm("add.rn.f16x2 %0, %1, %2;" : "=r"(h) : "r"(a[i]), "r"(b[i]));
+        asm("add.rn.f16x2 %0, %0, %1;" : "+r"(h) : "r"(c[i]));
+        asm("add.rn.f16x2 %0, %0, %1;" : "+r"(h) : "r"(d[i]));
+        float lo, hi;
+        asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n cvt.f32.f16 %0, l;\n cvt.f32.f16 %1, h;\n}\n"
+            : "=f"(lo), "=f"(hi)
+            : "r"(h));
+        if (SCALE) mul2_f32(lo, hi, s);
+        out[i] = pack2(lo, hi, RVQ_BF16);
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 }  // namespace vdec
 }  // namespace rvq

@@ -94,7 +94,8 @@ def rvq_matmul(x: torch.Tensor, entry: Dict[str, object], codebook: torch.Tensor
 class RvqGemvBatchJob(ctypes.Structure):
     _fields_ = [("weight", _native.RvqEntry), ("x", ctypes.c_void_p), ("y", ctypes.c_void_p),
                 ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("tokens", ctypes.c_int64),
-                ("x_kind", ctypes.c_int32), ("y_kind", ctypes.c_int32)]
+                ("x_kind", ctypes.c_int32), ("y_kind", ctypes.c_int32), ("exact", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 _batch_bound = False
@@ -127,10 +128,13 @@ class BatchGemvPlan:
     """``y = x @ W^T`` for ``tokens`` bf16 rows of x (any number; blocks of at most 192)
     with W decoded on chip into the tensor cores' operand (``rvq_gemv_batch``); fixed pointers,
     so a launch can be captured in a CUDA graph.  ``entry["codes_tiled"]``
-    (from ``gemv.tile_codes``) is required.  The workspace (split-K partials
-    and zeroed tickets) is allocated here once."""
+    (from ``gemv.tile_codes``) is required.  ``exact``: weights bit-identical
+    to the decoded bf16 slot (slower); otherwise the stage codewords are
+    summed in fp16.  The workspace (split-K partials and zeroed tickets) is
+    allocated here once."""
 
-    def __init__(self, entry: Dict[str, object], codebook: torch.Tensor, x: torch.Tensor, y: torch.Tensor):
+    def __init__(self, entry: Dict[str, object], codebook: torch.Tensor, x: torch.Tensor, y: torch.Tensor,
+                 exact: bool = False):
         if not gemv_supported(entry) or entry.get("codes_tiled") is None:
             raise NotImplementedError("rvq_gemv_batch needs a K=4 uint8 entry with codes_tiled")
         rows, cols = (int(s) for s in entry["shape"])
@@ -149,7 +153,7 @@ class BatchGemvPlan:
                                group_size=int(entry["group_size"]), trimmed=int(entry["trimmed_numel"]))
         w.indices = codes.data_ptr()
         self.job = RvqGemvBatchJob(w, x.data_ptr(), y.data_ptr(), rows, cols, int(x.shape[0]),
-                                   _native.RVQ_BF16, _native.RVQ_BF16)
+                                   _native.RVQ_BF16, _native.RVQ_BF16, 1 if exact else 0, 0)
         self.device = y.device
         with torch.cuda.device(self.device):
             nbytes = int(_batch_lib().rvq_gemv_batch_workspace_size(ctypes.byref(self.job)))

@@ -55,6 +55,9 @@ def test_step_struct_layouts():
     assert ctypes.sizeof(step.RvqAttnArgs) == 3 * 24 + 8 * 8 + 4 * 4 + 4 * 4
     from rvq_b200 import gemv
     assert ctypes.sizeof(gemv.RvqGemvTileJob) == ctypes.sizeof(_native.RvqEntry) + 2 * 24 + 3 * 8
+    from rvq_b200 import gemm
+    # entry + x, y + rows, cols, tokens + x_kind, y_kind, exact, reserved
+    assert ctypes.sizeof(gemm.RvqGemvBatchJob) == ctypes.sizeof(_native.RvqEntry) + 2 * 8 + 3 * 8 + 4 * 4
     assert gemv.tiles_count(2560) == 10 and gemv.tiles_count(9728) == 38 and gemv.tiles_count(520) == 3
     lib = gemv._tiles_lib()
     assert lib.rvq_tile_codes_bytes(9728, 2560) == 10 * 9728 * 128

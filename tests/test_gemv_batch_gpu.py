@@ -1,11 +1,14 @@
 """GPU: rvq_gemv_batch (fused GEMM on tcgen05, batches and prompts) against the oracle.
 
-The kernel multiplies x by the bit-exact bf16 slot weights (the oracle's
-reconstruction rounded to nearest even) with fp32 accumulation in TMEM, then
-rounds y to bf16.  So y agrees with the fp64 product of x and the oracle's
-bf16 weights to the bf16 output rounding (2^-9 relative per element; the
-norm-wise bound used here is 4e-3), well inside config 3's 1e-2 tolerance
-against the reference's reconstruct-then-matmul, which is also checked.
+In exact mode the kernel multiplies x by the bit-exact bf16 slot weights
+(the oracle's reconstruction rounded to nearest even) with fp32 accumulation
+in TMEM, then rounds y to bf16.  So y agrees with the fp64 product of x and
+the oracle's bf16 weights to the bf16 output rounding (2^-9 relative per
+element; the norm-wise bound used here is 4e-3).  The fast mode sums the
+stage codewords in fp16 before scaling and rounding to bf16, so a weight may
+differ from the slot's by one bf16 ulp; the same bound holds.  Both are well
+inside config 3's 1e-2 tolerance against the reference's
+reconstruct-then-matmul, which is also checked.
 """
 
 import numpy as np
@@ -46,12 +49,16 @@ def rel(got, want):
     (3000, 1000, 17, 40, torch.float32),       # 5 vectors per scale
     (200, 512, 256, None, torch.float32),      # 256 tokens: two blocks of 128
     (1000, 1024, 300, None, torch.float32),    # 300 tokens: two blocks of 160 (the last partial)
+    (9728, 2560, 128, None, torch.float16),    # 128 tokens: one block
+    (2560, 2560, 150, None, torch.float16),    # 150 tokens: one block of 160
+    (2560, 9728, 64, 128, torch.float16),      # down projection, 64 tokens, group-128 scales
     (640, 512, 192, None, torch.float32),      # 192 tokens: one block, 512 TMEM columns
     (9728, 2560, 2048, None, torch.float16),   # a 2048-token prompt on the gate projection
     (2048, 2560, 8, None, "f32_not_f16"),      # codebook fp16 cannot hold: global fp32 reads
     (2048, 2560, 8, 128, torch.float16),       # group 128 (the compressor default): 2 chunks per scale
 ])
-def test_batch_matches_bf16_reconstruction(rows, cols, tokens, group, cb_dtype, cuda_device):
+@pytest.mark.parametrize("exact", [False, True], ids=["fast", "exact"])
+def test_batch_matches_bf16_reconstruction(rows, cols, tokens, group, cb_dtype, exact, cuda_device):
     g = torch.Generator().manual_seed(rows * 7 + cols + tokens)
     cb = synthetic.make_codebook(4, 256, 8, g)
     if cb_dtype == "f32_not_f16":
@@ -62,7 +69,7 @@ def test_batch_matches_bf16_reconstruction(rows, cols, tokens, group, cb_dtype, 
     dev = {k: (v.to(cuda_device) if torch.is_tensor(v) else v) for k, v in entry.items()}
     dev["codes_tiled"] = tile_codes(dev["indices"], rows, cols)
     y = torch.full((tokens, rows), float("nan"), dtype=torch.bfloat16, device=cuda_device)
-    plan = BatchGemvPlan(dev, cb.to(cuda_device, cb_dtype), x.to(cuda_device), y)
+    plan = BatchGemvPlan(dev, cb.to(cuda_device, cb_dtype), x.to(cuda_device), y, exact=exact)
     plan.launch()
     torch.cuda.synchronize()
     w = oracle_w_bf16(entry, cb)
