@@ -378,45 +378,69 @@ def time_device(plans, steps, warmup, stream, world):
 
 
 def time_e2e(rel, cbs_host, device, steps, warmup, stream):
-    """Reference-facing API end to end: pinned host -> device upload of the
-    layer's compressed tensors (infer_compressed_layerwise_triton.py:424-432),
-    decode_into per key (lines 161-176), decoded slot -> pinned host."""
+    """Reference-facing API end to end: every step uploads the layer's
+    compressed tensors and codebooks from pinned host memory
+    (infer_compressed_layerwise_triton.py:424-432), decodes them with
+    decode_into per key (lines 161-176) and copies the decoded slot back to
+    pinned host memory.  Steps are pipelined over three streams (upload,
+    decode, download) with two buffer sets, so one step's upload and the
+    previous step's download run while a decode runs (PCIe is full duplex);
+    events order every reuse of a buffer set.  Timed from the first upload to
+    the last download."""
     from rvq_b200.engine import decode_into
     host = {k: {ek: (ev.pin_memory() if torch.is_tensor(ev) else ev) for ek, ev in e.items()}
             for k, e in rel.items()}
     host_cbs = {k: v.float().pin_memory() for k, v in cbs_host.items()}
-    dev = {k: {ek: (torch.empty_like(ev, device=device) if torch.is_tensor(ev) else ev)
-               for ek, ev in e.items()} for k, e in rel.items()}
-    dev_cbs = {k: torch.empty_like(v, device=device) for k, v in host_cbs.items()}
-    slot = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16, device=device) for k, e in rel.items()}
-    back = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16).pin_memory()
-            for k, e in rel.items()}
+    sets = []
+    for _ in range(2):
+        dev = {k: {ek: (torch.empty_like(ev, device=device) if torch.is_tensor(ev) else ev)
+                   for ek, ev in e.items()} for k, e in rel.items()}
+        dev_cbs = {k: torch.empty_like(v, device=device) for k, v in host_cbs.items()}
+        slot = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16, device=device) for k, e in rel.items()}
+        back = {k: torch.empty(tuple(e["shape"]), dtype=torch.bfloat16).pin_memory() for k, e in rel.items()}
+        ev = {n: torch.cuda.Event() for n in ("in", "cmp", "out")}
+        sets.append({"dev": dev, "cbs": dev_cbs, "slot": slot, "back": back, "ev": ev, "used": False})
     h2d = sum(v.numel() * v.element_size() for e in host.values() for v in e.values() if torch.is_tensor(v))
     h2d += sum(v.numel() * v.element_size() for v in host_cbs.values())
-    d2h = sum(v.numel() * v.element_size() for v in back.values())
+    d2h = sum(v.numel() * v.element_size() for v in sets[0]["back"].values())
     launches = sum(1 for e in rel.values() if e["method"] != "bf16_raw")
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    s_cmp = stream
 
-    def step():
-        for k, v in host_cbs.items():
-            dev_cbs[k].copy_(v, non_blocking=True)
-        for k, e in host.items():
-            for ek, ev in e.items():
-                if torch.is_tensor(ev):
-                    dev[k][ek].copy_(ev, non_blocking=True)
-        for k, e in dev.items():
-            decode_into(e, dev_cbs, slot[k])
-        for k in slot:
-            back[k].copy_(slot[k], non_blocking=True)
+    def step(i):
+        b = sets[i % 2]
+        ev = b["ev"]
+        if b["used"]:
+            s_in.wait_event(ev["cmp"])              # the decode of step i - 2 has read these inputs
+            s_cmp.wait_event(ev["out"])             # the download of step i - 2 has read this slot
+        b["used"] = True
+        with torch.cuda.stream(s_in):
+            for k, v in host_cbs.items():
+                b["cbs"][k].copy_(v, non_blocking=True)
+            for k, e in host.items():
+                for ek, hv in e.items():
+                    if torch.is_tensor(hv):
+                        b["dev"][k][ek].copy_(hv, non_blocking=True)
+            ev["in"].record(s_in)
+        s_cmp.wait_event(ev["in"])
+        with torch.cuda.stream(s_cmp):
+            for k, e in b["dev"].items():
+                decode_into(e, b["cbs"], b["slot"][k])
+            ev["cmp"].record(s_cmp)
+        s_out.wait_event(ev["cmp"])
+        with torch.cuda.stream(s_out):
+            for k in b["slot"]:
+                b["back"][k].copy_(b["slot"][k], non_blocking=True)
+            ev["out"].record(s_out)
 
-    with torch.cuda.stream(stream):
-        for _ in range(warmup):
-            step()
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(steps):
-            step()
-        end.record(stream)
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for i in range(steps):
+        step(warmup + i)
+    end.record(s_out)
     torch.cuda.synchronize()
     return start.elapsed_time(end), h2d, d2h, launches * steps
 
@@ -519,6 +543,7 @@ def run_ours(args, world, rank, local):
         e2e = {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                "api": "rvq_b200.engine.decode_into per entry (reference-facing)",
+               "pipelining": "upload, decode and download on three streams, two buffer sets",
                "gpu_launches": e2e_launches}
 
     cpu = None
