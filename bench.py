@@ -470,7 +470,8 @@ def overlap_leg(device):
 def batch1_leg(world, device, peak):
     """Batch-1 greedy generation, ms/token (the metric's second half).  N=1:
     the 36-layer 2560/9728 model in every weight mode (dense bf16, slot
-    decode + cuBLAS, fused table GEMV, fused exact-weight GEMV), each mode's
+    decode + cuBLAS, fused table GEMV, fused exact-weight GEMV, fused table
+    GEMV with the whole step as one persistent cooperative launch), each mode's
     ids checked against the drop-in engine (HF decoder layers on decoded
     slots, bit-identical to the oracle engine pinned to the reference
     engine's output), and the 64-layer 5120/25600 model; N>1: the 64-layer
@@ -486,7 +487,7 @@ def batch1_leg(world, device, peak):
             out["config2_36_layers"] = bench_generate.run(36, 128, 128, 151936, reps=2, device=device,
                                                           hbm_gbs=peak)
         c4 = {}
-        for mode in ("fused", "fused_exact"):
+        for mode in ("fused", "fused_exact") + (("fused_persistent",) if world == 1 else ()):
             c4[mode] = bench_tp.measure(bench_tp.SHAPE, 64, 151936, mode, device, group)
             c4[mode]["per_gpu_weight_GB/s"] = round(bench_tp.bytes_per_token(bench_tp.SHAPE, 64, 151936, world)
                                                     / (c4[mode]["ms_per_token"] * 1e6), 1)

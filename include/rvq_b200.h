@@ -432,6 +432,90 @@ int rvq_gemv_batch(const rvq_gemv_batch_job* job, void* workspace, size_t worksp
  * the current device.  Returns 1 if set, 0 if not, or -RVQ_ERR_CUDA. */
 int rvq_take_batch_timeout(void);
 
+/* Persistent batch-1 decode step: ONE cooperative launch (one CTA per SM)
+ * runs every layer of a Qwen3 decoder for one token, i.e. per layer the
+ * residual add + RMSNorm, the q/k/v, o, gate/up and down table GEMVs
+ * (rvq_gemv_tiles, silu(gate) * up fused into down) and the decode attention,
+ * then the final norm.  It replaces the per-layer kernel sequence
+ * rvq_step_norm, rvq_gemv_tiles, rvq_step_attention, ... (the reference's
+ * per-layer module calls of _layerwise_logits, infer_compressed_layerwise_
+ * triton.py:271-292, with the weight never materialised).  Phases hand over
+ * through counters in `sync` (bounded waits: a wait that gives up sets the
+ * flag rvq_persist_take_error reads).  Every phase repeats the arithmetic
+ * of the kernel it replaces in the same order, so h, x_final and the KV cache
+ * are bit-identical to that kernel sequence.  Limits: tensor-parallel size 1,
+ * head_dim 128, n_heads / n_kv <= 8, (n_heads / n_kv) * max_len <= 15360,
+ * hidden <= 16384, every projection K=4 / 256 codes / d=8 / uint8 codes in
+ * the tile-major layout of rvq_tile_codes. */
+typedef struct rvq_persist_layer {
+    rvq_entry proj[7];        /* q, k, v, o, gate, up, down; weight.out ignored */
+    const void* input_norm;   /* device bf16 [hidden] */
+    const void* post_norm;    /* device bf16 [hidden] */
+    const void* q_norm;       /* device bf16 [head_dim] */
+    const void* k_norm;       /* device bf16 [head_dim] */
+    void* k_cache;            /* device bf16 [n_kv][max_len][head_dim], this layer */
+    void* v_cache;
+} rvq_persist_layer;
+
+typedef struct rvq_persist_model {
+    int32_t n_layers;
+    int32_t hidden;
+    int32_t intermediate;
+    int32_t n_heads;
+    int32_t n_kv;
+    int32_t head_dim;
+    int32_t max_len;
+    int32_t vocab;
+    float eps;
+    float scaling;
+    float valid_bias;         /* as rvq_attn_args */
+    int32_t reserved;         /* 0 */
+    const void* embed;        /* device bf16 [vocab][hidden] */
+    const void* final_norm;   /* device bf16 [hidden] */
+    const void* cos;          /* device bf16 [max_len][head_dim] */
+    const void* sin;
+    const int64_t* token;     /* device, the step's token */
+    const int64_t* pos;       /* device, its position */
+    void* h;                  /* device bf16 [hidden], the residual stream */
+    void* x_final;            /* device bf16 [hidden], output: final-normed h */
+    void* attn_out;           /* device bf16 [n_heads * head_dim] */
+    float* q_part;            /* device fp32 partials [rvq_gemv_tiles_count(cols)][rows] of q, ... */
+    float* k_part;
+    float* v_part;
+    float* o_part;
+    float* gate_part;
+    float* up_part;
+    float* down_part;
+    uint32_t* sync;           /* device, RVQ_PERSIST_SYNC_WORDS words, 16-byte aligned, zero before the
+                                 first step; every step leaves its counters at zero */
+} rvq_persist_model;
+
+#define RVQ_PERSIST_SYNC_WORDS 32
+
+/* Bytes of the step plan for this model on the current device (0: not
+ * supported; rvq_persist_plan tells why). */
+int64_t rvq_persist_plan_bytes(const rvq_persist_model* m, const rvq_persist_layer* layers);
+
+/* Writes the plan (host memory, `bytes` from rvq_persist_plan_bytes): the
+ * model, every layer's GEMV jobs and the unit split of each GEMV phase over
+ * the CTAs.  The caller copies it to device memory (16-byte aligned). */
+int rvq_persist_plan(const rvq_persist_model* m, const rvq_persist_layer* layers, void* plan, int64_t bytes);
+
+/* Host-only: the plan for `n_ctas` CTAs (16..160) without a device, for
+ * inspection.  plan NULL: returns the size; else writes it and returns the
+ * size; a negative value is -status. */
+int64_t rvq_persist_plan_for(const rvq_persist_model* m, const rvq_persist_layer* layers, int32_t n_ctas,
+                             void* plan, int64_t bytes);
+
+/* One decode step with the plan at `plan_dev` (device).  No allocation, no
+ * sync; may be captured in a CUDA graph. */
+int rvq_persist_step(const void* plan_dev, void* stream);
+
+/* Reads and clears the sticky flag of rvq_persist_step (a phase wait or a
+ * code-word copy gave up; that step's outputs are invalid).  Synchronises the
+ * current device.  Returns 1 if set, 0 if not, or -RVQ_ERR_CUDA. */
+int rvq_persist_take_error(void);
+
 /* Prefill GEMM with the weight decoded into shared memory, never into HBM:
  *   y[m][n] = bf16( sum_k x[m][k] * W[n][k] )
  * with W the RVQ entry reconstructed exactly as rvq_decode would (bit-identical

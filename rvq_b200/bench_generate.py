@@ -77,7 +77,7 @@ def margin(logits):
 
 
 def run(layers=36, prompt_len=128, new=128, vocab=151936, reps=3,
-        modes=("dense", "slot", "fused", "fused_exact"), reference=True, device="cuda:0", hbm_gbs=None):
+        modes=("dense", "slot", "fused", "fused_exact", "fused_persistent"), reference=True, device="cuda:0", hbm_gbs=None):
     """TTFT, ms/token and greedy ids per weight mode, then the same prompt
     through the drop-in engine (``_layerwise_logits`` over HF decoder layers
     on slot weights, bit-identical to the oracle engine that is pinned to the
@@ -100,10 +100,14 @@ def run(layers=36, prompt_len=128, new=128, vocab=151936, reps=3,
     per_layer = shape.weights_per_block()
     head = vocab * shape.hidden * 2
     fused_bytes = layers * (per_layer // 8 * 4 + sum(o for _, o, _ in shape.projections()) * 2) + head
-    bytes_tok = {"dense": layers * per_layer * 2 + head, "fused": fused_bytes, "fused_exact": fused_bytes}
+    bytes_tok = {"dense": layers * per_layer * 2 + head, "fused": fused_bytes, "fused_exact": fused_bytes,
+                 "fused_persistent": fused_bytes}
     ids = {}
     for mode in modes:
-        dec = Qwen3Decoder(cfg, art, device, mode=mode, max_len=prompt_len + new + 8, artifact_is_shard=True)
+        # "fused_persistent": fused weights, the whole step as one cooperative launch
+        wmode, impl = ("fused", "persistent") if mode == "fused_persistent" else (mode, "native")
+        dec = Qwen3Decoder(cfg, art, device, mode=wmode, max_len=prompt_len + new + 8, artifact_is_shard=True,
+                           step_impl=impl)
         res, ids[mode] = time_mode(dec, prompt, new, reps)
         dec.check_waits()
         if mode in bytes_tok:
@@ -147,7 +151,7 @@ def main(argv=None):
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--new", type=int, default=128)
     ap.add_argument("--vocab", type=int, default=151936)
-    ap.add_argument("--modes", default="dense,slot,fused,fused_exact")
+    ap.add_argument("--modes", default="dense,slot,fused,fused_exact,fused_persistent")
     ap.add_argument("--no-reference", action="store_true")
     a = ap.parse_args(argv)
     print(json.dumps(run(a.layers, a.prompt, a.new, a.vocab, modes=tuple(a.modes.split(",")),

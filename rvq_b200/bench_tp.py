@@ -59,8 +59,9 @@ def measure(shape, layers, vocab, mode, device, group=None, prompt_len=128, new=
     cfg = synthetic.qwen3_config(shape, layers, vocab)
     art = synthetic.make_tp_shard_artifact(shape, layers, vocab, rank, world, seed=seed, device=device)
     prompt = torch.randint(0, vocab, (prompt_len,), generator=torch.Generator().manual_seed(1234)).to(device)
-    dec = Qwen3Decoder(cfg, art, device, mode=mode, max_len=prompt_len + new + 8, tp_group=group,
-                       artifact_is_shard=True, tp_reduce=tp_reduce)
+    wmode, impl = ("fused", "persistent") if mode == "fused_persistent" else (mode, "native")
+    dec = Qwen3Decoder(cfg, art, device, mode=wmode, max_len=prompt_len + new + 8, tp_group=group,
+                       artifact_is_shard=True, tp_reduce=tp_reduce, step_impl=impl)
     del art
     dec.capture()
     dec.generate(prompt, 4)

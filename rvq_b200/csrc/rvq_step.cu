@@ -13,86 +13,15 @@
 #include <type_traits>
 
 #include "rvq_common.cuh"
+#include "rvq_stepops.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace rvq {
 namespace {
 
-__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+using namespace stepops;
 
-__device__ __forceinline__ float bf16_at(const void* p, int64_t i) {
-    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
-}
-
-__device__ __forceinline__ void put_bf16(void* p, int64_t i, float v) {
-    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
-}
-
-// Value i of a vector operand (see rvq_vec).  Partials are added in tile
-// order; their loads are issued 8 at a time ahead of the adds, so a 38-tile
-// sum costs 5 memory round trips instead of 38.
-__device__ __forceinline__ float vec_value(const rvq_vec& v, int64_t i) {
-    if (v.kind == RVQ_F32) {
-        const float* p = reinterpret_cast<const float*>(v.ptr) + i;
-        const int64_t n = v.n;
-        const int nt = v.ntiles;
-        float s = __ldg(p);
-        int t = 1;
-        for (; t + 8 <= nt; t += 8) {
-            float c[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) c[k] = __ldg(p + (int64_t)(t + k) * n);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) s += c[k];
-        }
-        float c[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) c[k] = (t + k < nt) ? __ldg(p + (int64_t)(t + k) * n) : 0.f;
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-            if (t + k < nt) s += c[k];
-        return bf16r(s);
-    }
-    return load_as_f32(v.ptr, i, v.kind);
-}
-
-// vec_value with up to 32 partial loads in flight per thread (the tile sum is
-// still taken in tile order): for consumers with few threads per element.
-__device__ __forceinline__ float vec_value_deep(const rvq_vec& v, int64_t i) {
-    if (v.kind != RVQ_F32 || v.ntiles <= 8) return vec_value(v, i);
-    const float* p = reinterpret_cast<const float*>(v.ptr) + i;
-    const int64_t n = v.n;
-    const int nt = v.ntiles;
-    if (nt <= 32) {                                  // one round: 32 loads (clamped to the last tile)
-        float c[32];
-#pragma unroll
-        for (int k = 0; k < 32; ++k) c[k] = __ldg(p + (int64_t)min(k, nt - 1) * n);
-        float s = c[0];
-#pragma unroll
-        for (int k = 1; k < 32; ++k)
-            if (k < nt) s += c[k];
-        return bf16r(s);
-    }
-    float s = __ldg(p);
-    int t = 1;
-    for (; t + 32 <= nt; t += 32) {                  // whole chunks: 32 loads, then the adds in order
-        float c[32];
-#pragma unroll
-        for (int k = 0; k < 32; ++k) c[k] = __ldg(p + (int64_t)(t + k) * n);
-#pragma unroll
-        for (int k = 0; k < 32; ++k) s += c[k];
-    }
-    for (; t + 8 <= nt; t += 8) {
-        float c[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) c[k] = __ldg(p + (int64_t)(t + k) * n);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) s += c[k];
-    }
-    for (; t < nt; ++t) s += __ldg(p + (int64_t)t * n);
-    return bf16r(s);
-}
 
 __device__ int g_tp_timeout;                 // sticky: a landing-buffer wait gave up
 
@@ -129,12 +58,6 @@ __device__ __forceinline__ bool wait_arrivals(const uint32_t* arrivals, uint32_t
     }
     atomicExch(&g_tp_timeout, 1);
     return false;
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
 }
 
 // ---------------------------------------------------------------------------
@@ -223,49 +146,6 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxRep = 16;
 constexpr int kKeyChunk = 4;          // keys whose rows a warp loads before using them
-
-// RMSNorm (weight w) + rotary embedding of one head held by one warp:
-// lane holds elements d = lane + 32 j, j < hd / 32.  Returns through `o`.
-template <int HD>
-__device__ __forceinline__ void norm_rope_head(const float* x, const float* w, float eps, const float* cv,
-                                               const float* sv, float* o) {
-    constexpr int J = HD / 32;
-    const int lane = threadIdx.x & 31;
-    float v[J];
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-        v[j] = x[lane + 32 * j];
-        ss = fmaf(v[j], v[j], ss);
-    }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / (float)HD + eps);
-#pragma unroll
-    for (int j = 0; j < J; ++j) v[j] = bf16r(w[lane + 32 * j] * bf16r(v[j] * inv));
-    // rotate_half: d < HD/2 -> -v[d + HD/2], else v[d - HD/2]; held by the same lane
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-        const int d = lane + 32 * j;
-        const float rot = j < J / 2 ? -v[j + J / 2] : v[j - J / 2];
-        o[j] = bf16r(bf16r(v[j] * cv[d]) + bf16r(rot * sv[d]));
-    }
-}
-
-// E consecutive bf16 of a cache row as floats.
-template <int E>
-__device__ __forceinline__ void load_row_slice(const __nv_bfloat16* src, float (&out)[E]) {
-    if constexpr (E == 2) {
-        const __nv_bfloat162 w = *reinterpret_cast<const __nv_bfloat162*>(src);
-        out[0] = __low2float(w);
-        out[1] = __high2float(w);
-    } else {
-        using V = typename std::conditional<E == 4, uint2, uint4>::type;
-        const V w = *reinterpret_cast<const V*>(src);
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&w);
-#pragma unroll
-        for (int t = 0; t < E; ++t) out[t] = __bfloat162float(e[t]);
-    }
-}
 
 // Shared-memory floats of one CTA (host sizes the dynamic allocation with it).
 __host__ __device__ constexpr int attn_smem_floats(int hd, int rep, int keys_per_cta) {

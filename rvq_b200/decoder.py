@@ -99,7 +99,12 @@ class Qwen3Decoder:
     ``artifact_is_shard`` (rvq_b200/shard.py layout).  ``tp_reduce``: how the
     native step sums the row-parallel outputs over the ranks: "push" (peer
     stores over NVLink into landing buffers, rvq_b200/tp.py) or "nccl"
-    (``dist.all_reduce`` captured in the graph); prefill always uses NCCL."""
+    (``dist.all_reduce`` captured in the graph); prefill always uses NCCL.
+    ``step_impl``: how a decode step runs -- "native" (one launch per
+    operation: rvq_step norms and attention, rvq_gemv_tiles GEMVs, replayed
+    from a CUDA graph), "persistent" (fused mode on one GPU: the whole step as
+    one cooperative launch, rvq_b200/persist.py, bit-identical to "native") or
+    "torch" (the PyTorch ops of the prompt path)."""
 
     def __init__(self, config, artifact, device, mode: str = "fused", max_len: int = 512,
                  runtime_dtype: torch.dtype = torch.bfloat16, causal: bool = False,
@@ -107,13 +112,17 @@ class Qwen3Decoder:
                  tp_reduce: str = "push"):
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
-        if step_impl not in ("native", "torch"):
-            raise ValueError("step_impl is 'native' (rvq_step kernels) or 'torch'")
-        if runtime_dtype != torch.bfloat16 and step_impl == "native":
+        if step_impl not in ("native", "torch", "persistent"):
+            raise ValueError("step_impl is 'native' (rvq_step kernels), 'persistent' or 'torch'")
+        native = step_impl in ("native", "persistent")
+        if runtime_dtype != torch.bfloat16 and native:
             raise NotImplementedError("the native decode step computes in bf16")
         if mode == "fused_exact" and step_impl != "native":
             raise NotImplementedError("fused_exact runs on the native decode step")
+        if step_impl == "persistent" and (mode != "fused" or tp_group is not None):
+            raise NotImplementedError("the persistent decode step runs fused mode on one GPU")
         self.step_impl = step_impl
+        self.native = native
         self.mode = mode
         self.fused = mode in ("fused", "fused_exact")
         self.device = dev = torch.device(device)
@@ -125,7 +134,7 @@ class Qwen3Decoder:
         self.tp = dist.get_world_size(tp_group) if tp_group is not None else 1
         if tp_reduce not in ("push", "nccl"):
             raise ValueError("tp_reduce is 'push' or 'nccl'")
-        self.push = self.tp > 1 and tp_reduce == "push" and step_impl == "native"
+        self.push = self.tp > 1 and tp_reduce == "push" and native
         self.exchange = None
         if self.tp > 1:
             from .shard import shard_artifact, sharded_dims
@@ -166,8 +175,12 @@ class Qwen3Decoder:
         self._tok = torch.zeros(1, dtype=torch.long, device=dev)
         self._pos = torch.zeros(1, dtype=torch.long, device=dev)
         self._setup_weights()
-        if step_impl == "native":
+        self.persist = None
+        if native:
             self._build_step_ops()
+        if step_impl == "persistent":
+            from .persist import PersistentStep
+            self.persist = PersistentStep(self)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
 
     # -- weights -----------------------------------------------------------------
@@ -197,7 +210,7 @@ class Qwen3Decoder:
                 if not gemv_supported(E[n]):
                     raise NotImplementedError(f"fused mode needs rvq_gemv-compatible entries ({n})")
             cb = lambda n: self.codebooks[E[n]["codebook_id"]]
-            if self.step_impl == "native":      # rvq_gemv_tiles plans: _build_step_ops
+            if self.native:                     # rvq_gemv_tiles plans: _build_step_ops
                 for n in PROJ:
                     rows, cols = (int(v) for v in E[n]["shape"])
                     E[n]["codes_tiled"] = tile_codes(E[n]["indices"], rows, cols)
@@ -475,6 +488,12 @@ class Qwen3Decoder:
             self._mv(self.lm_head, self.x_final, self.logits_buf)
         return self.logits_buf
 
+    def _step_persistent(self) -> torch.Tensor:
+        """The native step as one cooperative launch (rvq_b200/persist.py), then the head."""
+        self.persist.launch()
+        self._mv(self.lm_head, self.x_final, self.logits_buf)
+        return self.logits_buf
+
     # -- prefill (eager) and graph-replayed decode steps -------------------------------
     def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
         """Prompt ids [T] (device) -> last-position logits; cache rows 0..T-1 written."""
@@ -486,7 +505,8 @@ class Qwen3Decoder:
     def capture(self) -> "Qwen3Decoder":
         """Record one decode step (token ``self._tok`` at ``self._pos``) as a CUDA graph."""
         kv = (self.k_cache.clone(), self.v_cache.clone())
-        run = self._step_native if self.step_impl == "native" else (lambda: self._forward(self._tok, self._pos))
+        run = {"native": self._step_native, "persistent": self._step_persistent}.get(
+            self.step_impl, lambda: self._forward(self._tok, self._pos))
         with torch.inference_mode():
             s = torch.cuda.Stream(self.device)
             s.wait_stream(torch.cuda.current_stream(self.device))
@@ -530,6 +550,8 @@ class Qwen3Decoder:
                 from .gemv import take_wait_timeout
                 if take_wait_timeout():
                     failed.append("a fused GEMV code-copy wait")
+            if self.persist is not None and self.persist.take_error():
+                failed.append("a persistent-step phase or code-copy wait")
         if failed:
             raise RuntimeError(" and ".join(failed) + " timed out; the generated tokens are invalid")
 

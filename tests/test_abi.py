@@ -202,3 +202,25 @@ def test_int8_entry_checks(lib):
     e.tail_numel, e.trimmed = 0, 1 << 31
     assert lib.rvq_check_int8_entry(ctypes.byref(e)) == _native.RVQ_ERR_TOO_LARGE
     assert lib.rvq_decode_layer_mixed(None, 0, None, 40, None, 0, None) == _native.RVQ_ERR_INVALID
+
+
+def test_persist_structs_and_host_checks(lib):
+    """The persistent decode step's structs and its argument checks (no device
+    memory touched; without a GPU the planner reports nothing plannable)."""
+    import torch
+    from rvq_b200 import persist
+    assert ctypes.sizeof(persist.RvqPersistLayer) == 7 * ctypes.sizeof(_native.RvqEntry) + 6 * 8
+    # 12 four-byte fields, 17 pointers
+    assert ctypes.sizeof(persist.RvqPersistModel) == 12 * 4 + 17 * 8
+    assert persist.SYNC_WORDS == 32
+    plib = persist._lib()
+    assert plib.rvq_persist_step(None, None) == _native.RVQ_ERR_INVALID
+    assert plib.rvq_persist_step(ctypes.c_void_p(0x1008), None) == _native.RVQ_ERR_INVALID   # not 16-byte aligned
+    assert plib.rvq_persist_plan(None, None, None, 0) == _native.RVQ_ERR_INVALID
+    if not torch.cuda.is_available():
+        m = persist.RvqPersistModel()
+        layers = (persist.RvqPersistLayer * 1)()
+        assert plib.rvq_persist_plan_bytes(ctypes.byref(m), layers) == 0
+        buf = (ctypes.c_char * 16)()
+        assert plib.rvq_persist_plan(ctypes.byref(m), layers, buf, 16) == _native.RVQ_ERR_UNAVAILABLE
+        assert plib.rvq_persist_step(ctypes.c_void_p(0x1000), None) == _native.RVQ_ERR_UNAVAILABLE
