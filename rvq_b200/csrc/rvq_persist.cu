@@ -29,12 +29,15 @@
 // arrivals, GEMV-phase arrivals, attention arrivals, exit).  A producer CTA
 // synchronises, fences and adds 1; a consumer's thread 0 spins (acquire
 // loads, about one second at most, then a sticky error flag and no further
-// waits) until the count for this layer is reached.  A consumer waits only
-// where it needs the data: a CTA starts the code-word copies of its next GEMV
-// unit and stages the codebook before it waits for the operand.  The last CTA
-// to leave resets the counters, so every step starts from zero.  All CTAs are
-// co-resident (cooperative launch), and every wait is on an earlier phase, so
-// no wait can depend on a CTA that waits for it.
+// waits) until the count for this layer is reached.  Every CTA passes the
+// phase's wait before it arrives, even one without work in the phase, so no
+// CTA arrives at phase k + 1 before all have arrived at phase k, and a count
+// of k x (arrivals per phase) therefore means phases 1..k are complete.  A CTA
+// starts the code-word copies of its next GEMV unit and stages the codebook
+// before it waits for the operand.  The last CTA to leave resets the
+// counters, so every step starts from zero.  All CTAs are co-resident
+// (cooperative launch), and every wait is on an earlier phase, so no wait can
+// depend on a CTA that waits for it.
 //
 // Data written inside the launch and read by other CTAs (h, the partials,
 // attn_out, the norm sums) is read through L2 (ld.global.cg), never through
@@ -479,7 +482,10 @@ __device__ __forceinline__ void gemv_phase(const PHead* P, const PPhase& ph, TJo
                                            UnitState& st, bool prefetched, Wait&& wait, Stage&& stage) {
     const int32_t* cf = at<int32_t>(P, P->cta_first_off) + ph.cta_first;
     const int u0 = cf[blockIdx.x], u1 = cf[blockIdx.x + 1];
-    if (u0 >= u1) return;
+    if (u0 >= u1) {                                  // no units: still wait, so that this CTA's
+        wait();                                      // arrival cannot run ahead of the phase before
+        return;
+    }
     {   // the phase's jobs into shared memory (read on every row batch)
         constexpr int kWords = (int)(sizeof(TJob) / 4);
         static_assert(sizeof(TJob) % 4 == 0, "TJob words");
