@@ -490,7 +490,7 @@ typedef struct rvq_persist_model {
                                  first step; every step leaves its counters at zero */
 } rvq_persist_model;
 
-#define RVQ_PERSIST_SYNC_WORDS 32
+#define RVQ_PERSIST_SYNC_WORDS 1024
 
 /* Bytes of the step plan for this model on the current device (0: not
  * supported; rvq_persist_plan tells why). */

@@ -25,8 +25,9 @@
 // attention's per-range maxima, sums and P V partial sums combined in range
 // order), so h, x_final and the KV cache are bit-identical to the plain step.
 //
-// Hand-over between phases: four monotonic counters in global memory (norm
-// arrivals, GEMV-phase arrivals, attention arrivals, exit).  A producer CTA
+// Hand-over between phases: monotonic counters in global memory (norm
+// arrivals, GEMV-phase arrivals spread over 16 counters, attention arrivals,
+// exit).  A producer CTA
 // synchronises, fences and adds 1; a consumer's thread 0 spins (acquire
 // loads, about one second at most, then a sticky error flag and no further
 // waits) until the count for this layer is reached.  Every CTA passes the
@@ -72,15 +73,24 @@ constexpr int kHD = 128;
 constexpr int kE = kHD / 32;
 constexpr int kMaxRep = 8;
 constexpr int kNormMaxSlice = 2048;                // two elements per thread
-// attention scratch in the table + codebook space (floats)
-constexpr int kScratch = tiles::kLutWords + tiles::kCbFloats;
+// attention scratch: the table, codebook and ring space (floats); the P V
+// partial of every (range, warp) for 4 heads sits in its last 128 KB
+constexpr int kScratch = tiles::kLutWords + tiles::kCbFloats + tiles::kRing * tiles::kBatchRows * tiles::kGroups;
 constexpr int kAttnFixed = 8592;
 constexpr int kMaxScores = 15360;                  // rep * max_len
-static_assert(kAttnFixed + kMaxScores <= kScratch, "attention scratch");
+constexpr int kPvOffset = tiles::kLutWords + tiles::kCbFloats;
+constexpr int kPvFloats = kRanks * 8 * 4 * 128;    // [range][warp][head of 4][HD]
+static_assert(kAttnFixed + kMaxScores <= kPvOffset && kPvOffset + kPvFloats <= kScratch, "attention scratch");
 constexpr int kPhases = 4;                         // GEMV phases per layer
 
-enum { kCtrNorm = 0, kCtrGemv = 1, kCtrAttn = 2, kCtrExit = 3, kCtrWords = 4, kSsWord = 8 };
-static_assert(kSsWord + kRanks <= RVQ_PERSIST_SYNC_WORDS, "sync words");
+// sync words: each counter and the norm sums on a 128-byte line of its own
+// (the counters are polled by every CTA; the sums are read by one thread per
+// CTA).  GEMV-phase arrivals are spread over kSub counters (CTA c adds to
+// counter c % kSub), so that 148 CTAs finishing together do not queue on one
+// address.
+constexpr int kSub = 16;
+enum { kCtrNorm = 0, kCtrAttn = 32, kCtrExit = 64, kSsWord = 96, kCtrGemv = 128 };
+static_assert(kCtrGemv + 32 * kSub <= RVQ_PERSIST_SYNC_WORDS, "sync words");
 
 static __device__ int g_persist_error;             // sticky: a phase wait gave up, or a bad grid
 
@@ -124,27 +134,31 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
     uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
-// Every thread: returns once *ctr >= target (thread 0 polls), or after about a
-// second without it (then the sticky flag is set and this CTA waits no more).
+// Every thread: returns once *ctr >= target (thread 0 polls with relaxed
+// loads, spaced out so that a hundred waiting CTAs do not crowd the counter's
+// L2 line, then one acquire fence), or after about a second without it (then
+// the sticky flag is set and this CTA waits no more).
 __device__ __forceinline__ void wait_count(const uint32_t* ctr, uint32_t target, volatile int* failed) {
     if (threadIdx.x == 0 && !*failed) {
         const uint64_t t0 = globaltimer_ns();
         bool ok = false;
-        for (uint32_t i = 0; i < (1u << 26); ++i) {
-            if ((int32_t)(ld_acquire(ctr) - target) >= 0) {
+        for (uint32_t i = 0; i < (1u << 24); ++i) {
+            if ((int32_t)(ld_relaxed(ctr) - target) >= 0) {
                 ok = true;
                 break;
             }
-            if (i > 256) __nanosleep(64);
-            if ((i & 255) == 0 && globaltimer_ns() - t0 > 1000000000ull) break;
+            __nanosleep(100);
+            if ((i & 63) == 0 && globaltimer_ns() - t0 > 1000000000ull) break;
         }
-        if (!ok) {
+        if (ok) {
+            asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+        } else {
             atomicExch(&g_persist_error, 1);
             *failed = 1;
         }
@@ -152,13 +166,38 @@ __device__ __forceinline__ void wait_count(const uint32_t* ctr, uint32_t target,
     __syncthreads();
 }
 
-// Every thread: this CTA's writes so far are published, then the counter advances.
+// Every thread: returns once every CTA has arrived at `phases` GEMV phases
+// (lane k < kSub of warp 0 polls counter k against its share of the CTAs).
+__device__ __forceinline__ void wait_gemv(const uint32_t* ctr, int G, uint32_t phases, volatile int* failed) {
+    const int k = threadIdx.x;
+    if (k < kSub && !*failed) {
+        const uint32_t target = (uint32_t)(G / kSub + (k < G % kSub ? 1 : 0)) * phases;
+        const uint32_t* p = ctr + kCtrGemv + 32 * k;
+        const uint64_t t0 = globaltimer_ns();
+        bool ok = false;
+        for (uint32_t i = 0; i < (1u << 24); ++i) {
+            if ((int32_t)(ld_relaxed(p) - target) >= 0) {
+                ok = true;
+                break;
+            }
+            __nanosleep(100);
+            if ((i & 63) == 0 && globaltimer_ns() - t0 > 1000000000ull) break;
+        }
+        if (ok) {
+            asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+        } else {
+            atomicExch(&g_persist_error, 1);
+            *failed = 1;
+        }
+    }
+    __syncthreads();
+}
+
+// Every thread: this CTA's writes so far are published (the barrier, then a
+// release add by thread 0), and the counter advances.
 __device__ __forceinline__ void arrive(uint32_t* ctr) {
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ctr, 1u);
-    }
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(ctr) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -167,8 +206,8 @@ __device__ __forceinline__ void arrive(uint32_t* ctr) {
 
 // h[slice] <- embed row (first) or h + add, kept in keep0 / keep1 (elements
 // lo + tid and lo + tid + 1024); the slice's sum of squares to ss[rank].
-__device__ __forceinline__ void norm_slice(const PHead* P, int rank, const rvq_vec* add, bool first, float& keep0,
-                                           float& keep1, float* warp_ss) {
+__device__ __noinline__ void norm_slice(const PHead* P, int rank, const rvq_vec* add, bool first, float& keep0,
+                                        float& keep1, float* warp_ss) {
     const rvq_persist_model& m = P->m;
     const int H = m.hidden;
     const int slice = (H + kRanks - 1) / kRanks;
@@ -189,7 +228,7 @@ __device__ __forceinline__ void norm_slice(const PHead* P, int rank, const rvq_v
                 hv = bf16_at(m.embed, row + i);
             } else {
                 hv = ldcg_f32(m.h, i, RVQ_BF16);
-                hv = bf16r(hv + vec_value<true>(*add, i));
+                hv = bf16r(hv + vec_value_deep<true>(*add, i));
             }
             put_bf16(m.h, i, hv);
             if (k == 0) keep0 = hv;
@@ -207,12 +246,21 @@ __device__ __forceinline__ void norm_slice(const PHead* P, int rank, const rvq_v
     }
 }
 
-// rsqrt(mean(h^2) + eps) from the 8 slices' sums, added in rank order.
-__device__ __forceinline__ float norm_inv(const PHead* P) {
-    const float* ss = reinterpret_cast<const float*>(P->m.sync + kSsWord);
-    float total = 0.f;
-    for (int r = 0; r < kRanks; ++r) total += __ldcg(ss + r);
-    return rsqrtf(total / (float)P->m.hidden + P->m.eps);
+// rsqrt(mean(h^2) + eps) from the 8 slices' sums, added in rank order; thread
+// 0 reads them, the others get the result through shared memory.
+__device__ __forceinline__ float norm_inv(const PHead* P, float* inv_sh) {
+    if (threadIdx.x == 0) {
+        const float* ss = reinterpret_cast<const float*>(P->m.sync + kSsWord);
+        float v[kRanks];
+#pragma unroll
+        for (int r = 0; r < kRanks; ++r) v[r] = __ldcg(ss + r);
+        float total = 0.f;
+#pragma unroll
+        for (int r = 0; r < kRanks; ++r) total += v[r];
+        *inv_sh = rsqrtf(total / (float)P->m.hidden + P->m.eps);
+    }
+    __syncthreads();
+    return *inv_sh;
 }
 
 // The GEMV operand of a normed phase: x = bf16(w * bf16(h * inv)) over the tile.
@@ -253,7 +301,7 @@ __device__ __noinline__ void attend(const PHead* P, const PLayer& Ly, int kv, fl
     float* knew = sm + 2304;
     float* vnew = knew + kHD;
     float* wsm = sm + 2560;                        // q_norm, k_norm, cos[pos], sin[pos]
-    float* run = sm + 3072;                        // [4 ranges][1024]: one range's warp sum
+    float* pw = sm + kPvOffset;                    // [range][warp][4 heads][HD] P V partials
     float* oacc = sm + 7168;                       // [rep * HD]: the ranges' sum
     float* mloc = sm + 8192;                       // [range][head] maxima
     float* sloc = sm + 8256;                       // [range][head] sums
@@ -393,66 +441,60 @@ __device__ __noinline__ void attend(const PHead* P, const PLayer& Ly, int kv, fl
     __syncthreads();
 
     // 5. P V: warp w of range r takes keys j0 + w + 8 i (in increasing order),
-    //    4 heads per pass; a range's 8 warps are added in warp order, the
-    //    ranges in range order
-    for (int p = 0; p < 4; ++p) {
-        const int q = warp >> 3, w = warp & 7, r = 4 * (p & 1) + q, hg = 4 * (p >> 1);
-        if (hg >= rep) break;                      // uniform
-        const int j0 = r * kpc, j1 = min(L, j0 + kpc);
-        float acc[4][kE];
+    //    4 heads at a time, and stores its partial; then each output element
+    //    adds a range's 8 warps in warp order and the ranges in range order
+    for (int hg = 0; hg < rep; hg += 4) {
+        for (int p = 0; p < 2; ++p) {
+            const int w = warp & 7, r = 4 * p + (warp >> 3);
+            const int j0 = r * kpc, j1 = min(L, j0 + kpc);
+            float acc[4][kE];
 #pragma unroll
-        for (int h = 0; h < 4; ++h)
+            for (int h = 0; h < 4; ++h)
 #pragma unroll
-            for (int e = 0; e < kE; ++e) acc[h][e] = 0.f;
-        for (int jb = j0 + w; jb < j1; jb += 8 * 4) {
-            float vd[4][kE];
+                for (int e = 0; e < kE; ++e) acc[h][e] = 0.f;
+            for (int jb = j0 + w; jb < j1; jb += 8 * 4) {
+                float vd[4][kE];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int j = jb + c * 8;
-                if (j == pos || j >= j1) {
+                for (int c = 0; c < 4; ++c) {
+                    const int j = jb + c * 8;
+                    if (j == pos || j >= j1) {
 #pragma unroll
-                    for (int e = 0; e < kE; ++e) vd[c][e] = vnew[d0 + e];
-                } else {
-                    load_row_slice<kE>(vc + (int64_t)j * kHD + d0, vd[c]);
-                }
-            }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int j = jb + c * 8;
-                if (j >= j1) break;
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    if (hg + h < rep) {
-                        const float pv = sc[(hg + h) * max_len + j];
-#pragma unroll
-                        for (int e = 0; e < kE; ++e) acc[h][e] = fmaf(pv, vd[c][e], acc[h][e]);
+                        for (int e = 0; e < kE; ++e) vd[c][e] = vnew[d0 + e];
+                    } else {
+                        load_row_slice<kE>(vc + (int64_t)j * kHD + d0, vd[c]);
                     }
                 }
-            }
-        }
-        for (int s = 0; s < 8; ++s) {
-            if (w == s) {
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    if (hg + h < rep) {
+                for (int c = 0; c < 4; ++c) {
+                    const int j = jb + c * 8;
+                    if (j >= j1) break;
 #pragma unroll
-                        for (int e = 0; e < kE; ++e) {
-                            float* dst = run + q * 1024 + h * kHD + d0 + e;
-                            *dst = s == 0 ? acc[h][e] : *dst + acc[h][e];
+                    for (int h = 0; h < 4; ++h) {
+                        if (hg + h < rep) {
+                            const float pv = sc[(hg + h) * max_len + j];
+#pragma unroll
+                            for (int e = 0; e < kE; ++e) acc[h][e] = fmaf(pv, vd[c][e], acc[h][e]);
                         }
                     }
                 }
             }
-            __syncthreads();
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+#pragma unroll
+                for (int e = 0; e < kE; ++e) pw[((r * 8 + w) * 4 + h) * kHD + d0 + e] = acc[h][e];
         }
-        // the pass's 4 ranges (heads hg .. hg + 3) into the output sum, in range order
+        __syncthreads();
         const int nh = min(4, rep - hg);
         for (int i = tid; i < nh * kHD; i += kThreads) {
-            const int o = hg * kHD + i;
-            float t = (p & 1) == 0 ? 0.f : oacc[o];
+            float t = 0.f;
+            for (int r = 0; r < kRanks; ++r) {
+                const float* q = pw + (r * 8 * 4) * kHD + i;     // warp 0 of range r, head i / HD
+                float u = q[0];
 #pragma unroll
-            for (int qq = 0; qq < 4; ++qq) t += run[qq * 1024 + i];
-            oacc[o] = t;
+                for (int w = 1; w < 8; ++w) u += q[w * 4 * kHD];
+                t += u;
+            }
+            oacc[hg * kHD + i] = t;
         }
         __syncthreads();
     }
@@ -516,6 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_persist_kernel(const PHead* _
     __shared__ volatile int aborted;
     __shared__ volatile int failed;
     __shared__ float warp_ss[kWarps];
+    __shared__ float inv_sh;
     __shared__ TJob sjobs[3];
     const TileSmem S = tiles::tile_smem(smem, slot_done, xmax, &aborted);
     if (threadIdx.x == 0) failed = 0;
@@ -528,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_persist_kernel(const PHead* _
     const int G = (int)gridDim.x, c = (int)blockIdx.x, L = m.n_layers;
     const PLayer* layers = at<PLayer>(P, P->layers_off);
     uint32_t* ctr = m.sync;
+    uint32_t* gemv_ctr = ctr + kCtrGemv + 32 * (c % kSub);
     const bool norm_cta = c < kRanks;
     const int kv = c - (G - m.n_kv);                 // >= 0: this CTA attends for kv head kv
     const rvq_vec down_v = {m.down_part, m.hidden, P->inter_tiles, RVQ_F32};
@@ -543,57 +587,56 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_persist_kernel(const PHead* _
         bool pre = false;
         if (norm_cta) {                              // norm 1
             pre = prefetch_phase(P, Ly.ph[0], S);
-            if (l > 0) wait_count(ctr + kCtrGemv, G32 * 4 * l32, &failed);
+            if (l > 0) wait_gemv(ctr, G, 4 * l32, &failed);
             norm_slice(P, c, &down_v, l == 0, keep0, keep1, warp_ss);
             arrive(ctr + kCtrNorm);
         }
         gemv_phase(P, Ly.ph[0], sjobs, S, st, pre,
                    [&] {
                        wait_count(ctr + kCtrNorm, kRanks * (2 * l32 + 1), &failed);
-                       inv = norm_inv(P);
+                       inv = norm_inv(P, &inv_sh);
                    },
                    [&](const TJob& J, int tile) { stage_normed(P, J, tile, Ly.ln1, inv, S); });
-        arrive(ctr + kCtrGemv);
+        arrive(gemv_ctr);
 
         pre = false;
-        if (kv >= 0) {                               // attention
-            pre = prefetch_phase(P, Ly.ph[1], S);
-            wait_count(ctr + kCtrGemv, G32 * (4 * l32 + 1), &failed);
+        if (kv >= 0) {                               // attention (its scratch takes the ring too)
+            wait_gemv(ctr, G, 4 * l32 + 1, &failed);
             attend(P, Ly, kv, reinterpret_cast<float*>(S.lut));
             st.cb = nullptr;                         // the codebook space was scratch
             arrive(ctr + kCtrAttn);
         }
         gemv_phase(P, Ly.ph[1], sjobs, S, st, pre,
                    [&] { wait_count(ctr + kCtrAttn, (uint32_t)m.n_kv * (l32 + 1), &failed); }, stage_op);
-        arrive(ctr + kCtrGemv);
+        arrive(gemv_ctr);
 
         pre = false;
         if (norm_cta) {                              // norm 2
             pre = prefetch_phase(P, Ly.ph[2], S);
-            wait_count(ctr + kCtrGemv, G32 * (4 * l32 + 2), &failed);
+            wait_gemv(ctr, G, 4 * l32 + 2, &failed);
             norm_slice(P, c, &o_v, false, keep0, keep1, warp_ss);
             arrive(ctr + kCtrNorm);
         }
         gemv_phase(P, Ly.ph[2], sjobs, S, st, pre,
                    [&] {
                        wait_count(ctr + kCtrNorm, kRanks * (2 * l32 + 2), &failed);
-                       inv = norm_inv(P);
+                       inv = norm_inv(P, &inv_sh);
                    },
                    [&](const TJob& J, int tile) { stage_normed(P, J, tile, Ly.ln2, inv, S); });
-        arrive(ctr + kCtrGemv);
+        arrive(gemv_ctr);
 
         gemv_phase(P, Ly.ph[3], sjobs, S, st, false,
-                   [&] { wait_count(ctr + kCtrGemv, G32 * (4 * l32 + 3), &failed); }, stage_op);
-        arrive(ctr + kCtrGemv);
+                   [&] { wait_gemv(ctr, G, 4 * l32 + 3, &failed); }, stage_op);
+        arrive(gemv_ctr);
     }
 
     if (norm_cta) {                                  // final norm
         const uint32_t L32 = (uint32_t)L;
-        wait_count(ctr + kCtrGemv, G32 * 4 * L32, &failed);
+        wait_gemv(ctr, G, 4 * L32, &failed);
         norm_slice(P, c, &down_v, false, keep0, keep1, warp_ss);
         arrive(ctr + kCtrNorm);
         wait_count(ctr + kCtrNorm, kRanks * (2 * L32 + 1), &failed);
-        inv = norm_inv(P);
+        inv = norm_inv(P, &inv_sh);
         const int H = m.hidden;
         const int slice = (H + kRanks - 1) / kRanks;
         const int lo = c * slice, hi = min(H, lo + slice);
@@ -607,7 +650,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_persist_kernel(const PHead* _
         __threadfence();
         const uint32_t old = atomicAdd(ctr + kCtrExit, 1u);
         if (old == G32 - 1) {
-            for (int k = 0; k < kCtrWords; ++k) atomicExch(ctr + k, 0u);
+            atomicExch(ctr + kCtrNorm, 0u);
+            atomicExch(ctr + kCtrAttn, 0u);
+            for (int k = 0; k < kSub; ++k) atomicExch(ctr + kCtrGemv + 32 * k, 0u);
+            atomicExch(ctr + kCtrExit, 0u);
             __threadfence();
         }
     }

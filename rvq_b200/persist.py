@@ -18,7 +18,7 @@ import torch
 
 from . import _native
 
-SYNC_WORDS = 32          # RVQ_PERSIST_SYNC_WORDS
+SYNC_WORDS = 1024        # RVQ_PERSIST_SYNC_WORDS
 
 
 class RvqPersistLayer(ctypes.Structure):

@@ -212,7 +212,7 @@ def test_persist_structs_and_host_checks(lib):
     assert ctypes.sizeof(persist.RvqPersistLayer) == 7 * ctypes.sizeof(_native.RvqEntry) + 6 * 8
     # 12 four-byte fields, 17 pointers
     assert ctypes.sizeof(persist.RvqPersistModel) == 12 * 4 + 17 * 8
-    assert persist.SYNC_WORDS == 32
+    assert persist.SYNC_WORDS == 1024
     plib = persist._lib()
     assert plib.rvq_persist_step(None, None) == _native.RVQ_ERR_INVALID
     assert plib.rvq_persist_step(ctypes.c_void_p(0x1008), None) == _native.RVQ_ERR_INVALID   # not 16-byte aligned
