@@ -536,8 +536,9 @@ class Qwen3Decoder:
     def check_waits(self) -> None:
         """Raise if a bounded device wait of this decoder's kernels gave up
         since the last check: a tensor-parallel landing-buffer wait (the norm
-        then summed whatever the buffer held) or a fused GEMV's wait for its
-        code copies.  Either makes the logits of that step invalid.
+        then summed whatever the buffer held), a fused GEMV's wait for its
+        code copies, or a phase wait of the persistent step.  Any of them
+        makes the logits of that step invalid.
         Synchronises the device."""
         torch.cuda.synchronize(self.device)
         failed = []
