@@ -15,7 +15,10 @@ step (the launches an ncu capture selects from).  ``generate``: greedy
 generation replaying the captured step.  The config-1 block is 2560 / 9728 /
 32q / 8kv / 128, the config-4 block 5120 / 25600 / 64q / 8kv / 128.  With
 ``--tp N`` the kernels are timed on one rank's share of a TP=N model (heads,
-kv heads and intermediate divided by N; no reduction).
+kv heads and intermediate divided by N; no reduction).  ``--persistent``:
+the decoder also holds the persistent step (rvq_b200/persist.py); ``kernels``
+then times its one cooperative launch for all layers as well, and
+``one-step`` runs it instead of the native step.
 """
 
 from __future__ import annotations
@@ -42,15 +45,17 @@ def rank_shape(block: str, tp: int) -> synthetic.BlockShape:
                                 n_kv_heads=b.n_kv_heads // tp, head_dim=b.head_dim)
 
 
-def build(block: str, layers: int, vocab: int, max_len: int, device, tp: int = 1) -> Qwen3Decoder:
+def build(block: str, layers: int, vocab: int, max_len: int, device, tp: int = 1,
+          persistent: bool = False) -> Qwen3Decoder:
     shape = rank_shape(block, tp)
     cfg = synthetic.qwen3_config(shape, layers, vocab)
     art = synthetic.make_tp_shard_artifact(shape, layers, vocab, 0, 1, seed=0, device=device)
-    return Qwen3Decoder(cfg, art, device, mode="fused", max_len=max_len)
+    return Qwen3Decoder(cfg, art, device, mode="fused", max_len=max_len,
+                        step_impl="persistent" if persistent else "native")
 
 
-def time_kernels(block: str, layers: int, device, tp: int = 1) -> dict:
-    dec = build(block, layers, 151936, 256, device, tp)
+def time_kernels(block: str, layers: int, device, tp: int = 1, persistent: bool = False) -> dict:
+    dec = build(block, layers, 151936, 256, device, tp, persistent)
     prompt = torch.randint(0, 151936, (128,), generator=torch.Generator().manual_seed(1)).to(device)
     dec.generate(prompt, 4)
     dec._pos.fill_(130)
@@ -87,20 +92,27 @@ def time_kernels(block: str, layers: int, device, tp: int = 1) -> dict:
     res["final_norm+head_per_token"] = round(graph_us(
         lambda: (dec.final_op.launch(), dec._mv(dec.lm_head, dec.x_final, dec.logits_buf))), 2)
     res["step_per_layer_incl_head"] = round(graph_us(dec._step_native) / layers, 2)
+    if persistent:
+        res["persistent_launch_per_layer"] = round(graph_us(dec.persist.launch) / layers, 2)
+        res["persistent_step_per_layer_incl_head"] = round(graph_us(dec._step_persistent) / layers, 2)
+        if dec.persist.take_error():
+            raise RuntimeError("a persistent-step wait gave up during the timing")
     dec.close()
     return {"block": block, "tp_rank_share": tp, "layers": layers, "us_per_layer": res,
             "timing": "each kernel replayed alone from a CUDA graph over all layers, CUDA events"}
 
 
-def one_step(block: str, layers: int, device) -> None:
-    dec = build(block, layers, 4096, 64, device)
+def one_step(block: str, layers: int, device, persistent: bool = False) -> None:
+    dec = build(block, layers, 4096, 64, device, persistent=persistent)
     prompt = torch.randint(0, 4096, (16,), generator=torch.Generator().manual_seed(1)).to(device)
     with torch.inference_mode():
         dec.prefill(prompt)
         dec._tok.fill_(3)
         dec._pos.fill_(16)
-        dec._step_native()
+        (dec._step_persistent if persistent else dec._step_native)()
     torch.cuda.synchronize()
+    if persistent and dec.persist.take_error():
+        raise RuntimeError("a persistent-step wait gave up")
 
 
 def generate(block: str, layers: int, new: int, device) -> list:
@@ -118,13 +130,14 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--new", type=int, default=24)
     ap.add_argument("--tp", type=int, default=1, help="time one rank's share of a TP=tp model (kernels only)")
+    ap.add_argument("--persistent", action="store_true", help="also time / run the persistent step")
     a = ap.parse_args(argv)
     device = torch.device("cuda:0")
     torch.cuda.set_device(device)
     if a.what == "kernels":
-        print(json.dumps(time_kernels(a.block, a.layers, device, a.tp)))
+        print(json.dumps(time_kernels(a.block, a.layers, device, a.tp, a.persistent)))
     elif a.what == "one-step":
-        one_step(a.block, a.layers, device)
+        one_step(a.block, a.layers, device, a.persistent)
         print("ok")
     else:
         print(json.dumps({"ids": generate(a.block, a.layers, a.new, device)}))
