@@ -104,12 +104,14 @@ class Qwen3Decoder:
     operation: rvq_step norms and attention, rvq_gemv_tiles GEMVs, replayed
     from a CUDA graph), "persistent" (fused mode on one GPU: the whole step as
     one cooperative launch, rvq_b200/persist.py, bit-identical to "native") or
-    "torch" (the PyTorch ops of the prompt path)."""
+    "torch" (the PyTorch ops of the prompt path).  ``slot_decode_ctas``: CTA
+    budget of the slot mode's side-stream layer decode (None: half the SMs,
+    the budget at which it overlaps the main stream best; 0: every SM)."""
 
     def __init__(self, config, artifact, device, mode: str = "fused", max_len: int = 512,
                  runtime_dtype: torch.dtype = torch.bfloat16, causal: bool = False,
                  step_impl: str = "native", tp_group=None, artifact_is_shard: bool = False,
-                 tp_reduce: str = "push"):
+                 tp_reduce: str = "push", slot_decode_ctas: Optional[int] = None):
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
         if step_impl not in ("native", "torch", "persistent"):
@@ -123,6 +125,7 @@ class Qwen3Decoder:
             raise NotImplementedError("the persistent decode step runs fused mode on one GPU")
         self.step_impl = step_impl
         self.native = native
+        self.slot_decode_ctas = slot_decode_ctas
         self.mode = mode
         self.fused = mode in ("fused", "fused_exact")
         self.device = dev = torch.device(device)
@@ -194,8 +197,14 @@ class Qwen3Decoder:
                      for L in self.layers]
             self.arena = SlotArena(specs, dev)
             self.side = torch.cuda.Stream(dev)
+            # the side-stream decode of the next layer leaves half the SMs to the
+            # layer being computed (otherwise its kernels queue behind the decode)
+            ctas = self.slot_decode_ctas
+            if ctas is None:
+                ctas = torch.cuda.get_device_properties(dev).multi_processor_count // 2
             self.decode_plans = [LayerDecodePlan([(n, L["entries"][n]) for n in PROJ], self.codebooks,
-                                                 self.arena.views(l)) for l, L in enumerate(self.layers)]
+                                                 self.arena.views(l), max_ctas=int(ctas))
+                                 for l, L in enumerate(self.layers)]
         # batch-1 activations at fixed addresses (bound by the GEMV plans, reused by graph replays)
         z = lambda n: torch.zeros(n, dtype=dt, device=dev)
         self.x_attn, self.x_mlp = z(d.hidden), z(d.hidden)
