@@ -27,10 +27,11 @@
 //
 // Hand-over between phases: monotonic counters in global memory (norm
 // arrivals, GEMV-phase arrivals spread over 16 counters, attention arrivals,
-// exit).  A producer CTA
-// synchronises, fences and adds 1; a consumer's thread 0 spins (acquire
-// loads, about one second at most, then a sticky error flag and no further
-// waits) until the count for this layer is reached.  Every CTA passes the
+// exit), each on a 128-byte line of its own.  A producer CTA synchronises,
+// then its thread 0 adds 1 with a release reduction; a consumer polls with
+// relaxed loads spaced by 100 ns and issues one acquire fence once the count
+// for this layer is reached (about one second at most, then a sticky error
+// flag and no further waits).  Every CTA passes the
 // phase's wait before it arrives, even one without work in the phase, so no
 // CTA arrives at phase k + 1 before all have arrived at phase k, and a count
 // of k x (arrivals per phase) therefore means phases 1..k are complete.  A CTA
