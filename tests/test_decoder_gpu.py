@@ -202,3 +202,20 @@ def test_greedy_ids_identical_to_engine_strict(cuda_device):
         first = next((i for i in range(new) if int(ids[i]) != int(ref_ids[i])), None)
         assert first is None or first in flips, (mode, first, flips)
         dec.close()
+
+
+def test_slot_decode_budget_does_not_change_logits(cuda_device):
+    """The slot mode's side-stream decode on every SM, on a few SMs, or on the
+    default half: the decoded slots, hence ids and logits, are the same."""
+    art = synthetic.make_model_artifact(MID, 3, 2048, seed=21)
+    cfg = synthetic.qwen3_config(MID, 3, 2048)
+    prompt = torch.randint(0, 2048, (12,), generator=torch.Generator().manual_seed(22)).to(cuda_device)
+    runs = []
+    for ctas in (0, 16, None):
+        dec = Qwen3Decoder(cfg, art, cuda_device, mode="slot", max_len=40, slot_decode_ctas=ctas)
+        runs.append(dec.generate(prompt, 10, return_logits=True))
+        dec.close()
+    for ids, logits in runs[1:]:
+        assert torch.equal(ids, runs[0][0])
+        for a, b in zip(logits, runs[0][1]):
+            assert torch.equal(a, b)
